@@ -1,0 +1,349 @@
+// Projection GEMMs of the packed decoder forward on the 5th-generation tensor cores (tcgen05 + TMEM), fed by TMA.
+//
+//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )
+//
+// A is the activation (rows = pack tokens, K contiguous), B an nn.Linear weight (out_features x in_features, K
+// contiguous), so both operands are K-major. Replaces the cuBLAS / torch._scaled_mm calls behind every projection of
+// the reference's layers (families/qwen/packed.py:108-125,144-156; families/gemma/packed.py:183-193,254-265;
+// serve/fp8.py:86-101; serve/qwen_fp8.py:38-42).
+//
+// Design (one CTA per SM, persistent over 128 x 256 output tiles):
+//   warp 0      TMA producer: A and B tiles (128-byte rows, 128-byte swizzle) into a 4-stage shared-memory ring;
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=256) into one of two TMEM accumulators
+//               (2 x 256 fp32 columns) and commits each stage back to the producer;
+//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per thread), the fused
+//               epilogue, 16-byte stores; the second accumulator lets tile i's epilogue overlap tile i+1's mainloop.
+// The k-loop is BK = 64 bf16 (or 128 e4m3) elements: one 128-byte swizzle row per operand row.
+#include "common.cuh"
+#include "kd_internal.h"
+
+namespace kd {
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int ROW_BYTES = 128;  // one swizzle row per operand row per stage
+constexpr int STAGES = 4;
+constexpr int A_STAGE_BYTES = BM * ROW_BYTES;  // 16 KB
+constexpr int B_STAGE_BYTES = BN * ROW_BYTES;  // 32 KB
+constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
+constexpr int TMEM_COLS = 512;  // two 128 x 256 fp32 accumulators
+constexpr int THREADS = 192;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+
+struct Args {
+  int M, N, K;
+  __nv_bfloat16* C;
+  int64_t ldc;
+  const __nv_bfloat16* R;  // residual (EPI_RESIDUAL); may alias C
+  int64_t ldr;
+  const float* scale_a;  // FP8: one scale per A row
+  const float* scale_b;  // FP8: one scale per B row (output column)
+  int* status;
+};
+
+template <int EPI>
+KD_DEVICE void store_chunk(const Args& a, int row, int col0, const float (&v)[32]) {
+  // 32 consecutive output columns of one row, rounded to bf16 once (the reference's bf16 Linear output).
+  if (row >= a.M) return;
+  __nv_bfloat16* out = a.C + (int64_t)row * a.ldc + col0;
+  uint32_t packed[16];
+  if constexpr (EPI == KD_EPI_RESIDUAL) {
+    const __nv_bfloat16* res = a.R + (int64_t)row * a.ldr + col0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * j);
+      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        float2 r2 = unpack_bf16x2(rw[t]);
+        // h + bf16(x): the residual add of two bf16 tensors, rounded once.
+        packed[4 * j + t] = pack_bf16x2(r2.x + bf16_round(v[8 * j + 2 * t]), r2.y + bf16_round(v[8 * j + 2 * t + 1]));
+      }
+    }
+  } else {
+#pragma unroll
+    for (int t = 0; t < 16; ++t) packed[t] = pack_bf16x2(v[2 * t], v[2 * t + 1]);
+  }
+  const int n_out = (EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU) ? a.N / 2 : a.N;
+  if (col0 + 32 <= n_out) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      *reinterpret_cast<uint4*>(out + 8 * j) =
+          make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+  } else {
+    for (int t = 0; t < 16; ++t) {
+      if (col0 + 2 * t < n_out) reinterpret_cast<uint32_t*>(out)[t] = packed[t];
+    }
+  }
+}
+
+template <int EPI, bool FP8>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Args args) {
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+
+  const int warp = threadIdx.x / 32;
+  const int m_tiles = (args.M + BM - 1) / BM;
+  const int n_tiles = (args.N + BN - 1) / BN;
+  const int num_tiles = m_tiles * n_tiles;
+  const int elems_per_row = FP8 ? ROW_BYTES : ROW_BYTES / 2;  // BK in elements
+  const int k_blocks = (args.K + elems_per_row - 1) / elems_per_row;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4 * 32);
+    }
+    fence_barrier_init();
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const int m0 = (tile / n_tiles) * BM;
+        const int n0 = (tile % n_tiles) * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status)) goto done;
+          uint8_t* sa = smem + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+          tma_load_2d(&map_a, &full_bar[stage], sa, kb * elems_per_row, m0);
+          tma_load_2d(&map_b, &full_bar[stage], sb, kb * elems_per_row, n0);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    constexpr uint32_t idesc = mma_idesc(FP8 ? 0u : 1u, BM, BN);
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.status)) goto done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, args.status)) goto done;
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_STAGE_BYTES;
+#pragma unroll
+          for (int k = 0; k < ROW_BYTES / 32; ++k) {  // 32 bytes of K per instruction (16 bf16 or 32 e4m3)
+            const uint64_t da = sw128_kmajor_desc(sa + 32 * k);
+            const uint64_t db = sw128_kmajor_desc(sb + 32 * k);
+            if constexpr (FP8)
+              mma_f8_ss(d_tmem, da, db, idesc, (kb | k) != 0);
+            else
+              mma_f16_ss(d_tmem, da, db, idesc, (kb | k) != 0);
+          }
+          mma_commit(&empty_bar[stage]);  // the stage is free once these MMAs have read it
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        mma_commit(&acc_full[acc]);  // the accumulator is complete once every MMA above has finished
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (warps 2..5)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int lane = threadIdx.x & 31;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      const int m0 = (tile / n_tiles) * BM;
+      const int n0 = (tile % n_tiles) * BN;
+      if (!mbar_wait(&acc_full[acc], acc_phase, args.status)) goto done;
+      tc_fence_after();
+      const int row = m0 + quarter * 32 + lane;
+      const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      float sa = 1.0f;
+      if constexpr (FP8) sa = (row < args.M) ? args.scale_a[row] : 0.0f;
+      if constexpr (EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU) {
+        // Columns [0,128) of the tile are gate rows, [128,256) the matching up rows (weights interleaved at load):
+        // out[:, n0/2 + c] = act(gate) * up, each operand rounded to bf16 first as the reference's Linear outputs are.
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t g[32], u[32];
+          tmem_ld32(t_row + c, g);
+          tmem_ld_wait_regs(g);
+          tmem_ld32(t_row + BN / 2 + c, u);
+          tmem_ld_wait_regs(u);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float gf = __uint_as_float(g[j]);
+            float uf = __uint_as_float(u[j]);
+            if constexpr (FP8) {
+              gf *= sa * args.scale_b[n0 + c + j];
+              uf *= sa * args.scale_b[n0 + BN / 2 + c + j];
+            }
+            gf = bf16_round(gf);
+            uf = bf16_round(uf);
+            v[j] = (EPI == KD_EPI_SWIGLU ? silu(gf) : gelu_tanh(gf)) * uf;
+          }
+          store_chunk<EPI>(args, row, n0 / 2 + c, v);
+        }
+      } else {
+        for (int c = 0; c < BN; c += 32) {
+          if (n0 + c >= args.N) break;
+          uint32_t r[32];
+          tmem_ld32(t_row + c, r);
+          tmem_ld_wait_regs(r);
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(r[j]);
+            if constexpr (FP8) {
+              const int col = n0 + c + j;
+              x = x * sa * (col < args.N ? args.scale_b[col] : 0.0f);
+            }
+            v[j] = x;
+          }
+          store_chunk<EPI>(args, row, n0 + c, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      if (++acc == 2) {
+        acc = 0;
+        acc_phase ^= 1;
+      }
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+template <int EPI, bool FP8>
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& args, cudaStream_t stream) {
+  auto kernel = gemm_kernel<EPI, FP8>;
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return KD_ERR_ARGUMENT;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return record_cuda_error(e, "gemm: cudaFuncSetAttribute");
+    configured[dev] = true;
+  }
+  const int m_tiles = (args.M + BM - 1) / BM;
+  const int n_tiles = (args.N + BN - 1) / BN;
+  const int tiles = m_tiles * n_tiles;
+  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, args);
+  return record_cuda_error(cudaGetLastError(), "gemm: launch");
+}
+
+}  // namespace gemm
+}  // namespace kd
+
+using namespace kd;
+
+static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
+                       int64_t ldr, const float* scale_a, const float* scale_b, int M, int N, int K, int epilogue,
+                       int fp8, int* status, cudaStream_t stream) {
+  if (M < 0 || N <= 0 || K <= 0) return set_error(KD_ERR_ARGUMENT, "gemm: M >= 0, N > 0 and K > 0 required");
+  if (M == 0) return KD_OK;
+  if (!A || !B || !C || !status) return set_error(KD_ERR_ARGUMENT, "gemm: null pointer");
+  const int esize = fp8 ? 1 : 2;
+  if ((lda * esize) % 16 || (ldb * esize) % 16 || (reinterpret_cast<uintptr_t>(A) % 16) ||
+      (reinterpret_cast<uintptr_t>(B) % 16))
+    return set_error(KD_ERR_ARGUMENT, "gemm: A and B need 16-byte aligned bases and row strides");
+  if (lda < K || ldb < K) return set_error(KD_ERR_ARGUMENT, "gemm: lda and ldb must be >= K");
+  if (N % 32) return set_error(KD_ERR_ARGUMENT, "gemm: N must be a multiple of 32");
+  const bool gated = epilogue == KD_EPI_SWIGLU || epilogue == KD_EPI_GEGLU;
+  if (gated && N % gemm::BN) return set_error(KD_ERR_ARGUMENT, "gemm: gated epilogues need N % 256 == 0");
+  const int n_out = gated ? N / 2 : N;
+  if (ldc < n_out || (ldc % 8) || (reinterpret_cast<uintptr_t>(C) % 16))
+    return set_error(KD_ERR_ARGUMENT, "gemm: C needs a 16-byte aligned base and ldc % 8 == 0, ldc >= output width");
+  if (epilogue == KD_EPI_RESIDUAL && (!R || ldr < N || (ldr % 8) || (reinterpret_cast<uintptr_t>(R) % 16)))
+    return set_error(KD_ERR_ARGUMENT, "gemm: residual epilogue needs R with ldr >= N, ldr % 8 == 0, 16-byte base");
+  if (fp8 && (!scale_a || !scale_b)) return set_error(KD_ERR_ARGUMENT, "gemm: fp8 needs scale_a and scale_b");
+
+  CUtensorMap ma, mb;
+  const CUtensorMapDataType dt = fp8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const uint32_t box_k = gemm::ROW_BYTES / esize;
+  int rc = make_tma_2d(&ma, A, dt, esize, K, M, lda, box_k, gemm::BM, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tma_2d(&mb, B, dt, esize, K, N, ldb, box_k, gemm::BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+
+  gemm::Args args;
+  args.M = M;
+  args.N = N;
+  args.K = K;
+  args.C = static_cast<__nv_bfloat16*>(C);
+  args.ldc = ldc;
+  args.R = static_cast<const __nv_bfloat16*>(R);
+  args.ldr = ldr;
+  args.scale_a = scale_a;
+  args.scale_b = scale_b;
+  args.status = status;
+
+#define KD_GEMM_CASE(E)                                                         \
+  case E:                                                                       \
+    return fp8 ? gemm::launch<E, true>(ma, mb, args, stream)                    \
+               : gemm::launch<E, false>(ma, mb, args, stream);
+  switch (epilogue) {
+    KD_GEMM_CASE(KD_EPI_STORE)
+    KD_GEMM_CASE(KD_EPI_RESIDUAL)
+    KD_GEMM_CASE(KD_EPI_SWIGLU)
+    KD_GEMM_CASE(KD_EPI_GEGLU)
+    default:
+      return set_error(KD_ERR_ARGUMENT, "gemm: unknown epilogue");
+  }
+#undef KD_GEMM_CASE
+}
+
+extern "C" int kd_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
+                            const void* R, int64_t ldr, int M, int N, int K, int epilogue, int* status,
+                            cudaStream_t stream) {
+  return gemm_common(A, lda, B, ldb, C, ldc, R, ldr, nullptr, nullptr, M, N, K, epilogue, 0, status, stream);
+}
+
+extern "C" int kd_gemm_fp8(const void* A, int64_t lda, const float* scale_a, const void* B, int64_t ldb,
+                           const float* scale_b, void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K,
+                           int epilogue, int* status, cudaStream_t stream) {
+  return gemm_common(A, lda, B, ldb, C, ldc, R, ldr, scale_a, scale_b, M, N, K, epilogue, 1, status, stream);
+}

@@ -1,0 +1,206 @@
+"""Seeded model shapes, random-init weights and packs for tests, the smoke check and the benchmark.
+
+The model shapes are the benchmark configurations of this build: a dense GQA decoder shaped like the reference's
+Qwen3.5 full-attention layers (gated queries, q/k norms, ``(1 + w)`` norms, SwiGLU; families/qwen/packed.py) or like
+its Gemma 4 text layers (sandwich norms, q/k/v norms, attention scale 1, layer scalar, scaled embedding, GeGLU,
+5 sliding-window : 1 global layers; families/gemma/packed.py). Weights are bf16-representable float32 arrays from a
+numpy generator (small shapes) or bf16 tensors drawn on the device (full-size benchmark shapes); packs follow the
+reference's ``pack`` (model/packed.py:73-105) with sequence lengths drawn uniform or log-uniform.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import asdict, dataclass, replace
+
+import numpy as np
+import torch
+
+__all__ = ["CONFIGS", "Spec", "device_weights", "numpy_weights", "synthetic_lengths", "synthetic_pack_arrays"]
+
+
+@dataclass(frozen=True)
+class Spec:
+    """A decoder's shape. ``family`` "qwen" (Qwen3.5 full-attention layers) or "gemma" (Gemma 4 text layers)."""
+
+    family: str
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    intermediate: int
+    vocab: int
+    eps: float = 1e-6
+    rope_theta: float = 1e6  # Qwen, Gemma global layers
+    rope_theta_local: float = 1e4  # Gemma sliding layers
+    partial_rotary: float = 1.0  # Qwen: rotary dims = head_dim * partial_rotary
+    window: int = 1024  # Gemma sliding window (a token and window - 1 before it)
+    global_every: int = 6  # Gemma: layer i is global when (i + 1) % global_every == 0
+    attention: str = "causal"
+    logit_cap: float | None = None
+    codes: int = 3  # readout rows
+
+    def as_dict(self) -> dict:
+        return asdict(self)
+
+    @property
+    def q_width(self) -> int:
+        """Columns of the query projection (Qwen's gated q_proj emits [q | gate] per head)."""
+        return self.heads * self.head_dim * (2 if self.family == "qwen" else 1)
+
+    @property
+    def qkv_width(self) -> int:
+        return self.q_width + 2 * self.kv_heads * self.head_dim
+
+    def layer_types(self) -> list[str]:
+        if self.family == "qwen":
+            return ["full_attention"] * self.layers
+        # Every global_every-th layer is global, and so is the last (Gemma4TextConfig forces a global last layer).
+        return ["full_attention" if (i + 1) % self.global_every == 0 or i == self.layers - 1 else "sliding_attention"
+                for i in range(self.layers)]
+
+    def gemm_flops_per_token(self) -> float:
+        """2 * sum(K * N) over one token's projections, all layers."""
+        h, hd = self.hidden, self.head_dim
+        per_layer = h * self.qkv_width + self.heads * hd * h + h * 2 * self.intermediate + self.intermediate * h
+        return 2.0 * per_layer * self.layers
+
+
+#: The benchmark configurations.
+CONFIGS: dict[str, Spec] = {
+    "tiny": Spec("qwen", 2, 256, 4, 2, 64, 1024, 4096),
+    "qwen-0.8b": Spec("qwen", 28, 1024, 16, 8, 128, 3072, 151936),
+    "qwen-4b": Spec("qwen", 36, 2560, 32, 8, 128, 9728, 151936),
+    "gemma-12b": Spec("gemma", 48, 3840, 16, 8, 256, 15360, 262144, logit_cap=30.0),
+    "gemma-31b": Spec("gemma", 62, 5376, 32, 16, 128, 21504, 262144, logit_cap=30.0),
+}
+
+
+def _bf16_exact(x: np.ndarray) -> np.ndarray:
+    """Rounds float32 values to bf16-representable ones (round to nearest even)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32).reshape(x.shape)
+
+
+def numpy_weights(spec: Spec, seed: int = 0, std: float = 0.02) -> dict[str, np.ndarray]:
+    """Random-init weights (bf16-representable float32), named as the Transformers modules the reference wraps.
+    Projections ~ N(0, std) (Transformers' initializer_range); norm weights away from their identity value so a wrong
+    norm rule shows: Qwen's ``(1 + w)`` weights ~ N(0, 0.1), Gemma's ``w`` ~ 1 + N(0, 0.1); Gemma layer scalars in
+    [0.8, 1.0]; readout rows ~ N(0, std)."""
+    rng = np.random.default_rng(seed)
+    h, hd, hq, hkv, inter = spec.hidden, spec.head_dim, spec.heads, spec.kv_heads, spec.intermediate
+
+    def normal(*shape, scale=std):
+        return _bf16_exact(rng.standard_normal(shape, dtype=np.float32) * np.float32(scale))
+
+    def norm_weight(n):
+        w = rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)
+        return _bf16_exact(w if spec.family == "qwen" else 1.0 + w)
+
+    w: dict[str, np.ndarray] = {"embed_tokens": normal(spec.vocab, h)}
+    for i in range(spec.layers):
+        p = f"layers.{i}."
+        w[p + "input_layernorm"] = norm_weight(h)
+        w[p + "q_proj"] = normal(spec.q_width, h)
+        w[p + "k_proj"] = normal(hkv * hd, h)
+        w[p + "v_proj"] = normal(hkv * hd, h)
+        w[p + "q_norm"] = norm_weight(hd)
+        w[p + "k_norm"] = norm_weight(hd)
+        w[p + "o_proj"] = normal(h, hq * hd)
+        w[p + "post_attention_layernorm"] = norm_weight(h)
+        w[p + "gate_proj"] = normal(inter, h)
+        w[p + "up_proj"] = normal(inter, h)
+        w[p + "down_proj"] = normal(h, inter)
+        if spec.family == "gemma":
+            w[p + "pre_feedforward_layernorm"] = norm_weight(h)
+            w[p + "post_feedforward_layernorm"] = norm_weight(h)
+            w[p + "layer_scalar"] = _bf16_exact(rng.uniform(0.8, 1.0, size=(1,)).astype(np.float32))
+    w["norm"] = norm_weight(h)
+    w["readout"] = normal(spec.codes, h)
+    return w
+
+
+def device_weights(spec: Spec, seed: int, device: torch.device, std: float = 0.02) -> dict[str, torch.Tensor]:
+    """The same layout as ``numpy_weights`` drawn directly on ``device`` in bf16 (full-size benchmark models, where a
+    host-side draw would take minutes): a torch generator seeded with ``seed`` on that device."""
+    gen = torch.Generator(device=device).manual_seed(seed)
+    h, hd, hq, hkv, inter = spec.hidden, spec.head_dim, spec.heads, spec.kv_heads, spec.intermediate
+
+    def normal(*shape, scale=std):
+        return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * scale).bfloat16()
+
+    def norm_weight(n):
+        w = torch.randn(n, generator=gen, device=device, dtype=torch.float32) * 0.1
+        return (w if spec.family == "qwen" else 1.0 + w).bfloat16()
+
+    w: dict[str, torch.Tensor] = {"embed_tokens": normal(spec.vocab, h)}
+    for i in range(spec.layers):
+        p = f"layers.{i}."
+        w[p + "input_layernorm"] = norm_weight(h)
+        w[p + "q_proj"] = normal(spec.q_width, h)
+        w[p + "k_proj"] = normal(hkv * hd, h)
+        w[p + "v_proj"] = normal(hkv * hd, h)
+        w[p + "q_norm"] = norm_weight(hd)
+        w[p + "k_norm"] = norm_weight(hd)
+        w[p + "o_proj"] = normal(h, hq * hd)
+        w[p + "post_attention_layernorm"] = norm_weight(h)
+        w[p + "gate_proj"] = normal(inter, h)
+        w[p + "up_proj"] = normal(inter, h)
+        w[p + "down_proj"] = normal(h, inter)
+        if spec.family == "gemma":
+            w[p + "pre_feedforward_layernorm"] = norm_weight(h)
+            w[p + "post_feedforward_layernorm"] = norm_weight(h)
+            w[p + "layer_scalar"] = (0.8 + 0.2 * torch.rand(1, generator=gen, device=device)).bfloat16()
+    w["norm"] = norm_weight(h)
+    w["readout"] = normal(spec.codes, h)
+    return w
+
+
+def synthetic_lengths(total: int, low: int, high: int, seed: int, log_uniform: bool = True) -> list[int]:
+    """Sequence lengths drawn (log-)uniform in [low, high] until they fill ``total`` tokens exactly (the last one
+    truncated to fit, at least 1)."""
+    rng = np.random.default_rng(seed)
+    out, used = [], 0
+    while used < total:
+        if log_uniform:
+            n = int(round(math.exp(rng.uniform(math.log(low), math.log(high)))))
+        else:
+            n = int(rng.integers(low, high + 1))
+        n = min(n, total - used)
+        out.append(n)
+        used += n
+    return out
+
+
+def synthetic_pack_arrays(lengths: list[int], vocab: int, seed: int, markers_per_seq: tuple[int, int] = (1, 1)
+                          ) -> dict[str, np.ndarray]:
+    """A pack's host arrays (model/packed.py:73-105 for text-only joint sequences): ids uniform in [0, vocab),
+    ``seqpos`` restarting at 0 per sequence, ``cu`` boundaries, and per sequence k markers (k uniform in
+    ``markers_per_seq``): its last token plus k - 1 distinct earlier positions, sorted, as global rows."""
+    rng = np.random.default_rng(seed)
+    ids, seqpos, markers, marker_counts = [], [], [], []
+    cu = [0]
+    for n in lengths:
+        ids.append(rng.integers(0, vocab, size=n, dtype=np.int64))
+        seqpos.append(np.arange(n, dtype=np.int64))
+        k = int(rng.integers(markers_per_seq[0], markers_per_seq[1] + 1))
+        k = max(1, min(k, n))
+        extra = rng.choice(n - 1, size=k - 1, replace=False) if k > 1 else np.zeros(0, dtype=np.int64)
+        local = np.sort(np.concatenate([extra.astype(np.int64), np.array([n - 1], dtype=np.int64)]))
+        markers.append(local + cu[-1])
+        marker_counts.append(k)
+        cu.append(cu[-1] + n)
+    return {
+        "input_ids": np.concatenate(ids),
+        "seqpos": np.concatenate(seqpos),
+        "cu": np.array(cu, dtype=np.int64),
+        "markers": np.concatenate(markers),
+        "marker_cu": np.concatenate([[0], np.cumsum(marker_counts)]).astype(np.int64),
+    }
+
+
+def small(spec: Spec, **changes) -> Spec:
+    """``spec`` with some fields changed (test-sized variants)."""
+    return replace(spec, **changes)

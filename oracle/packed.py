@@ -1,0 +1,311 @@
+"""numpy restatement of the reference's packed forward (Qwen-shaped and Gemma-shaped decoders) and readout.
+
+Test infrastructure only (the checker and the timed CPU baseline); the product path never imports it.
+
+Two modes:
+- ``"fp32"``: float32 everywhere, no intermediate rounding (the reference run in float32 on CPU, which the golden
+  fixtures hold);
+- ``"bf16"``: float32 arithmetic with a bf16 rounding wherever the reference's bf16 path stores a bf16 tensor: after
+  every projection, norm, rotation, activation product, residual sum and attention output, and for the rotary tables.
+  Pointwise groups that the reference fuses into one compiled kernel (families/qwen/fused.py:51-71,
+  families/gemma/fused.py:64-78) round once, at their output.
+
+Weights are dicts of float32 arrays laid out like the Transformers modules the reference wraps (nn.Linear weights
+(out, in)); ``pack`` is a dict with ``input_ids`` (T,), ``seqpos`` (T,), ``cu`` (n + 1,), ``markers`` (M,).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+
+E4M3_MAX = 448.0
+
+
+# ------------------------------------------------------------------------------------------------ rounding
+
+
+def bf16(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bfloat16, returned as float32."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000
+    return u.astype(np.uint32).view(np.float32).reshape(x.shape)
+
+
+def _round(x: np.ndarray, mode: str) -> np.ndarray:
+    return bf16(x) if mode == "bf16" else x.astype(np.float32, copy=False)
+
+
+def _e4m3_table() -> np.ndarray:
+    """Every non-negative finite e4m3fn value (bias 7, no infinities, 0x7F is NaN), ascending."""
+    vals = []
+    for code in range(0x7F):
+        e, m = code >> 3, code & 7
+        vals.append(m / 8.0 * 2.0 ** -6 if e == 0 else (1 + m / 8.0) * 2.0 ** (e - 7))
+    return np.array(vals, dtype=np.float64)
+
+
+_E4M3 = _e4m3_table()
+
+
+def e4m3(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float -> e4m3fn (saturating inputs are clamped to +-448 by the callers), as float32."""
+    x = np.asarray(x, dtype=np.float64)
+    a = np.minimum(np.abs(x), E4M3_MAX)
+    idx = np.searchsorted(_E4M3, a)  # first table value >= a
+    hi = _E4M3[np.minimum(idx, len(_E4M3) - 1)]
+    lo = _E4M3[np.maximum(idx - 1, 0)]
+    pick_lo = (a - lo) < (hi - a)
+    tie = (a - lo) == (hi - a)
+    lo_code = np.maximum(idx - 1, 0)
+    even_lo = (lo_code & 1) == 0
+    out = np.where(pick_lo | (tie & even_lo), lo, hi)
+    out = np.where(a == hi, hi, out)
+    return (np.sign(x) * out).astype(np.float32)
+
+
+def e4m3_rows(x: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Each row scaled into the e4m3 range, rounded to e4m3, and its float32 scale (serve/fp8.py:21-24,
+    serve/qwen_fp8.py:20-23): scale = max(amax, 1e-12) / 448, q = e4m3(clamp(x / scale, +-448))."""
+    x = np.asarray(x, dtype=np.float32)
+    scale = (np.maximum(np.abs(x).max(axis=-1, keepdims=True), np.float32(1e-12)) / np.float32(E4M3_MAX))
+    scale = scale.astype(np.float32)
+    q = e4m3(np.clip(x / scale, -E4M3_MAX, E4M3_MAX))
+    return q, scale
+
+
+# ------------------------------------------------------------------------------------------------ pointwise
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray | None, eps: float, one_plus: bool) -> np.ndarray:
+    """RMSNorm over the last axis in float32: Qwen's ``x * rsqrt(mean(x^2) + eps) * (1 + w)``
+    (families/qwen/fused.py:17-19) or Gemma's ``x * (mean(x^2) + eps)^-0.5 * w`` / without weight
+    (families/gemma/fused.py:21-26). Unrounded; the caller rounds."""
+    h = x.astype(np.float32)
+    ms = (h * h).mean(axis=-1, keepdims=True, dtype=np.float32) + np.float32(eps)
+    # Qwen multiplies by rsqrt, Gemma by pow(., -0.5): the same value, kept in the reference's form.
+    out = h * (np.float32(1.0) / np.sqrt(ms)) if one_plus else h * np.power(ms, np.float32(-0.5))
+    if weight is not None:
+        w = weight.astype(np.float32)
+        out = out * ((np.float32(1.0) + w) if one_plus else w)
+    return out.astype(np.float32)
+
+
+def silu(x: np.ndarray) -> np.ndarray:
+    return x / (np.float32(1.0) + np.exp(-x))
+
+
+def gelu_tanh(x: np.ndarray) -> np.ndarray:
+    """``F.gelu(x, approximate="tanh")`` (families/gemma/fused.py:37-38)."""
+    return np.float32(0.5) * x * (np.float32(1.0) + np.tanh(np.float32(math.sqrt(2.0 / math.pi)) *
+                                                            (x + np.float32(0.044715) * x ** 3)))
+
+
+def rope_tables(positions: np.ndarray, head_dim: int, theta: float, partial: float, mode: str
+                ) -> tuple[np.ndarray, np.ndarray]:
+    """cos/sin (T, rot) at ``positions``: inv_freq = 1 / theta^(arange(0, rot, 2) / rot), emb = cat(f, f)
+    (Transformers' default rotary embedding, as Qwen3_5TextRotaryEmbedding / Gemma4TextRotaryEmbedding compute it, and
+    cast to the activations' dtype)."""
+    rot = int(head_dim * partial)
+    inv_freq = (1.0 / (np.float32(theta) ** (np.arange(0, rot, 2, dtype=np.float32) / np.float32(rot))))
+    inv_freq = inv_freq.astype(np.float32)
+    freqs = positions.astype(np.float32)[:, None] * inv_freq[None, :]
+    emb = np.concatenate([freqs, freqs], axis=-1)
+    return _round(np.cos(emb), mode), _round(np.sin(emb), mode)
+
+
+def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
+    """Rotate-half RoPE on the first ``rot`` dims of (T, H, hd) (Transformers apply_rotary_pos_emb, partial rotary
+    as in Qwen3.5; families/gemma/fused.py:41-45)."""
+    rot = cos.shape[-1]
+    xr, xp = x[..., :rot], x[..., rot:]
+    half = rot // 2
+    rotated = np.concatenate([-xr[..., half:], xr[..., :half]], axis=-1)
+    out = xr * cos[:, None, :] + rotated * sin[:, None, :]
+    return np.concatenate([out, xp], axis=-1).astype(np.float32)
+
+
+# ------------------------------------------------------------------------------------------------ attention
+
+
+def attention_varlen(q: np.ndarray, k: np.ndarray, v: np.ndarray, cu_q: np.ndarray, cu_k: np.ndarray, scale: float,
+                     window: tuple[int, int]) -> np.ndarray:
+    """The varlen attention contract (tests/test_gemma_blocks.py:28-43 in the reference): per sequence, query i sees
+    key j when i + (Lk - Lq) - left <= j <= i + (Lk - Lq) + right (-1: unbounded), GQA by head groups; float32
+    softmax. q (Tq, Hq, d), k/v (Tk, Hkv, d) -> (Tq, Hq, d)."""
+    left, right = window
+    hq, hkv = q.shape[1], k.shape[1]
+    group = hq // hkv
+    out = np.zeros(q.shape, dtype=np.float32)
+    for s in range(len(cu_q) - 1):
+        qa, qb, ka, kb = int(cu_q[s]), int(cu_q[s + 1]), int(cu_k[s]), int(cu_k[s + 1])
+        if qb == qa:
+            continue
+        lq, lk = qb - qa, kb - ka
+        i = np.arange(lq)[:, None] + (lk - lq)
+        j = np.arange(lk)[None, :]
+        mask = np.ones((lq, lk), dtype=bool)
+        if right >= 0:
+            mask &= j <= i + right
+        if left >= 0:
+            mask &= j >= i - left
+        for h in range(hq):
+            qs = q[qa:qb, h, :].astype(np.float32)
+            ks = k[ka:kb, h // group, :].astype(np.float32)
+            vs = v[ka:kb, h // group, :].astype(np.float32)
+            scores = (qs @ ks.T) * np.float32(scale)
+            scores = np.where(mask, scores, -np.inf)
+            peak = scores.max(axis=-1, keepdims=True)
+            peak = np.where(np.isfinite(peak), peak, 0.0)
+            p = np.exp(scores - peak)
+            denom = p.sum(axis=-1, keepdims=True)
+            out[qa:qb, h, :] = (p @ vs) / np.where(denom > 0, denom, 1.0)
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ projections
+
+
+def linear(x: np.ndarray, w: np.ndarray, mode: str, fp8: bool = False, prequantized=None) -> np.ndarray:
+    """``x @ w.T`` (nn.Linear) rounded to the activations' dtype; with ``fp8`` the rowwise-scaled e4m3 product of
+    serve/fp8.py:86-101 / serve/qwen_fp8.py:38-42: (q_x @ q_w.T) * s_x * s_w (float32 accumulation, bf16 out).
+    ``w`` is then the pair (q_w, s_w) and ``prequantized`` optionally the pair (q_x, s_x)."""
+    if not fp8 or not isinstance(w, tuple):  # a projection left in bf16 (Qwen: fewer than 256 outputs)
+        return _round(x.astype(np.float32) @ w.astype(np.float32).T, mode)
+    qw, sw = w
+    qx, sx = prequantized if prequantized is not None else e4m3_rows(x)
+    return _round((qx @ qw.T) * sx * sw.reshape(1, -1), mode)
+
+
+#: Qwen's FP8 path keeps projections with fewer outputs in bf16 (serve/qwen_fp8.py:17, :45-56).
+QWEN_FP8_MIN_FEATURES = 256
+
+
+def quantize_weights(weights: dict, min_features: int = 0) -> dict:
+    """Every projection weight with at least ``min_features`` outputs to (e4m3 rows, (1, out) scales) as Fp8Linear
+    does at load (serve/fp8.py:86-90, serve/qwen_fp8.py:27-33)."""
+    out = dict(weights)
+    for key, w in weights.items():
+        if key.endswith(("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")) and \
+                w.shape[0] >= min_features:
+            q, s = e4m3_rows(w)
+            out[key] = (q, s.reshape(1, -1))
+    return out
+
+
+# ------------------------------------------------------------------------------------------------ Qwen-shaped
+
+
+def qwen_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8: bool = False) -> np.ndarray:
+    """(M, hidden) final-normed hidden states at the markers: families/qwen/packed.py:178-187 over full-attention
+    layers (``layer`` :149-156, ``full_attention`` :119-125, ``_qkv`` :108-117, ``head`` :173-176), causal window
+    (-1, 0) (:31-32). With ``fp8``, every projection is the rowwise FP8 product of serve/qwen_fp8.py:38-42 (the
+    activation quantized from its bf16 value at each call)."""
+    eps, hq, hkv, hd = spec["eps"], spec["heads"], spec["kv_heads"], spec["head_dim"]
+    if fp8:
+        weights = quantize_weights(weights, QWEN_FP8_MIN_FEATURES)
+    ids, seqpos, cu = pack["input_ids"], pack["seqpos"], pack["cu"]
+    t = len(ids)
+    h = _round(weights["embed_tokens"][ids], mode)  # :158-159
+    cos, sin = rope_tables(seqpos, hd, spec["rope_theta"], spec.get("partial_rotary", 1.0), mode)  # :186
+    window = (-1, 0) if spec.get("attention", "causal") == "causal" else (-1, -1)
+    for i in range(spec["layers"]):
+        p = f"layers.{i}."
+        x = _round(rms_norm(h, weights[p + "input_layernorm"], eps, True), mode)  # :150
+        qg = linear(x, weights[p + "q_proj"], mode, fp8).reshape(t, hq, 2 * hd)  # :113
+        q, gate = qg[..., :hd], qg[..., hd:].reshape(t, hq * hd)
+        q = _round(rms_norm(q, weights[p + "q_norm"], eps, True), mode)  # :114
+        k = linear(x, weights[p + "k_proj"], mode, fp8).reshape(t, hkv, hd)
+        k = _round(rms_norm(k, weights[p + "k_norm"], eps, True), mode)  # :115
+        v = linear(x, weights[p + "v_proj"], mode, fp8).reshape(t, hkv, hd)  # :116
+        q, k = _round(apply_rope(q, cos, sin), mode), _round(apply_rope(k, cos, sin), mode)  # :121
+        o = _round(attention_varlen(q, k, v, cu, cu, hd ** -0.5, window), mode).reshape(t, hq * hd)  # :123-124
+        o = _round(o * (np.float32(1.0) / (np.float32(1.0) + np.exp(-gate))), mode)  # :125 sigmoid_mul
+        a = linear(o, weights[p + "o_proj"], mode, fp8)  # :125
+        h = _round(h + a, mode)  # :155 add_rms_norm
+        y = _round(rms_norm(h, weights[p + "post_attention_layernorm"], eps, True), mode)
+        g = linear(y, weights[p + "gate_proj"], mode, fp8)  # fused.mlp :95-97
+        u = linear(y, weights[p + "up_proj"], mode, fp8)
+        m = _round(silu(g) * u, mode)
+        h = _round(h + linear(m, weights[p + "down_proj"], mode, fp8), mode)  # :156
+    return _round(rms_norm(h[pack["markers"]], weights["norm"], eps, True), mode)  # head :173-176
+
+
+# ------------------------------------------------------------------------------------------------ Gemma-shaped
+
+
+def gemma_layer_types(spec: dict) -> list[str]:
+    """Every ``global_every``-th layer global, and the last one (Transformers' Gemma4TextConfig forces a global last
+    layer, the one the reference's bidirectional pruning needs: families/gemma/packed.py:172-173)."""
+    every, n = spec.get("global_every", 6), spec["layers"]
+    return ["full_attention" if (i + 1) % every == 0 or i == n - 1 else "sliding_attention" for i in range(n)]
+
+
+def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8: bool = False) -> np.ndarray:
+    """(M, hidden) at the markers: families/gemma/packed.py:305-323 over single-block sequences (each virtual sequence
+    is a whole sequence: ``block_plan`` :103-151 without branches). Layer :262-265: attention :228-254 (q/k norm +
+    RoPE, v norm without weight, scale 1.0; sliding layers window (W-1, 0) :171, global layers causal), residual
+    ``h + norm(attn)`` (fused.py:29-30), MLP ``norm(down(gelu_tanh(gate z) * up z))`` with z = norm(h) (:258-260),
+    ``(h + mlp) * layer_scalar`` (fused.py:33-34). Embeddings scaled by bf16(sqrt(hidden)) (:283-285). With ``fp8``,
+    the projections are serve/fp8.py's: one activation quantization per fused producer (norm, gelu-mul), o_proj's
+    input quantized at its call (serve/fp8.py:57-84, :104-117)."""
+    eps, hq, hkv, hd, w_len = spec["eps"], spec["heads"], spec["kv_heads"], spec["head_dim"], spec["window"]
+    if fp8:
+        weights = quantize_weights(weights)
+    ids, seqpos, cu = pack["input_ids"], pack["seqpos"], pack["cu"]
+    t = len(ids)
+    scale = np.float32(math.sqrt(spec["hidden"]))
+    if mode == "bf16":
+        scale = bf16(np.array([scale]))[0]
+    h = _round(weights["embed_tokens"][ids] * scale, mode)
+    types = gemma_layer_types(spec)
+    tables = {
+        "sliding_attention": rope_tables(seqpos, hd, spec["rope_theta_local"], 1.0, mode),
+        "full_attention": rope_tables(seqpos, hd, spec["rope_theta"], 1.0, mode),
+    }
+    causal_global = spec.get("attention", "causal") == "causal"
+
+    def normed(x, w):  # the norm (and, for fp8, the quantization fused into it: serve/fp8.py:57-69, :92-99)
+        y = _round(rms_norm(x, w, eps, False), mode)
+        return y, (e4m3_rows(y) if fp8 else None)
+
+    for i in range(spec["layers"]):
+        p = f"layers.{i}."
+        cos, sin = tables[types[i]]
+        x, xq = normed(h, weights[p + "input_layernorm"])
+        q = linear(x, weights[p + "q_proj"], mode, fp8, xq).reshape(t, hq, hd)
+        q = _round(apply_rope(rms_norm(q, weights[p + "q_norm"], eps, False), cos, sin), mode)
+        k = linear(x, weights[p + "k_proj"], mode, fp8, xq).reshape(t, hkv, hd)
+        k = _round(apply_rope(rms_norm(k, weights[p + "k_norm"], eps, False), cos, sin), mode)
+        v = linear(x, weights[p + "v_proj"], mode, fp8, xq).reshape(t, hkv, hd)
+        v = _round(rms_norm(v, None, eps, False), mode)
+        if types[i] == "sliding_attention":
+            window = (w_len - 1, 0)
+        else:
+            window = (-1, 0) if causal_global else (-1, -1)
+        o = _round(attention_varlen(q, k, v, cu, cu, 1.0, window), mode).reshape(t, hq * hd)
+        a = linear(o, weights[p + "o_proj"], mode, fp8)
+        h = _round(h + rms_norm(a, weights[p + "post_attention_layernorm"], eps, False), mode)
+        z, zq = normed(h, weights[p + "pre_feedforward_layernorm"])
+        g = linear(z, weights[p + "gate_proj"], mode, fp8, zq)
+        u = linear(z, weights[p + "up_proj"], mode, fp8, zq)
+        m = _round(gelu_tanh(g) * u, mode)
+        m = linear(m, weights[p + "down_proj"], mode, fp8)
+        m = rms_norm(m, weights[p + "post_feedforward_layernorm"], eps, False)
+        if mode == "bf16":
+            m = bf16(m)
+        h = _round((h + m) * np.float32(weights[p + "layer_scalar"]), mode)
+    return _round(rms_norm(h[pack["markers"]], weights["norm"], eps, False), mode)
+
+
+# ------------------------------------------------------------------------------------------------ readout
+
+
+def readout(hidden: np.ndarray, weight: np.ndarray, cap: float | None = None) -> np.ndarray:
+    """``Readout.forward`` (model/readout.py:30-33): float32 ``hidden @ W.T``, then ``cap * tanh(logits / cap)``."""
+    logits = hidden.astype(np.float32) @ weight.astype(np.float32).T
+    if cap:
+        logits = np.float32(cap) * np.tanh(logits / np.float32(cap))
+    return logits.astype(np.float32)

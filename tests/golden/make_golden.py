@@ -1,0 +1,319 @@
+"""Generates the golden fixtures of this directory by running the reference implementation itself.
+
+Run in a container where the karpo-decision source tree is available (``--reference`` points at its root; the
+fixtures are committed, so the GPU box never needs it):
+
+    python tests/golden/make_golden.py --reference <karpo-decision checkout>
+
+For each case it builds a random-init Transformers backbone (Qwen3_5Model with full-attention layers, or
+Gemma4TextModel with 5 sliding : 1 global layers) with the seeded weights of ``karpo_decision_b200.synthetic``,
+packs seeded sequences with the reference's own ``pack`` and runs the reference's own ``families.*.Packed`` and
+``Readout`` on CPU in float32. FP8 cases run the reference's own ``serve.qwen_fp8.quantize`` / ``serve.fp8.quantize``.
+
+Harness-only substitutions (the CPU has none of the reference's GPU kernels), each a restatement of the contract the
+reference's own tests use:
+- varlen attention: ``varlen_contract`` below, the end-aligned window contract of the reference's
+  tests/test_gemma_blocks.py:28-43, replaces torch's ``varlen_attn`` / FA4;
+- ``torch._scaled_mm`` (rowwise scales are not implemented on CPU): ``(a.float() @ b.float()) * scale_a * scale_b``
+  rounded to the output dtype, the documented semantics of rowwise scaling;
+- Transformers 5.5 names a layer's kind ``layer_type``; the reference reads ``block_type``: aliased per layer;
+- ``transformers.models.gemma4_unified`` (newer Transformers) is absent: stubbed, it is only imported for a type.
+"""
+
+from __future__ import annotations
+
+import argparse
+import contextlib
+import hashlib
+import sys
+import types
+from pathlib import Path
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+HERE = Path(__file__).resolve().parent
+sys.path.insert(0, str(HERE.parents[1]))
+
+from karpo_decision_b200.synthetic import CONFIGS, Spec, numpy_weights, small, synthetic_pack_arrays  # noqa: E402
+
+
+def varlen_contract(q, k, v, cu_q, cu_k, max_q, max_k, scale=None, window_size=(-1, -1), enable_gqa=False):
+    """Per sequence, query i sees key j when i + (Lk - Lq) - left <= j <= i + (Lk - Lq) + right (-1 unbounded)."""
+    left, right = window_size
+    outs = []
+    for qa, qb, ka, kb in zip(cu_q[:-1].tolist(), cu_q[1:].tolist(), cu_k[:-1].tolist(), cu_k[1:].tolist(),
+                              strict=True):
+        if qb == qa:
+            continue
+        i = torch.arange(qb - qa)[:, None] + (kb - ka) - (qb - qa)
+        j = torch.arange(kb - ka)[None, :]
+        mask = torch.ones(qb - qa, kb - ka, dtype=torch.bool)
+        if right >= 0:
+            mask &= j <= i + right
+        if left >= 0:
+            mask &= j >= i - left
+        outs.append(F.scaled_dot_product_attention(q[qa:qb].transpose(0, 1)[None], k[ka:kb].transpose(0, 1)[None],
+                                                   v[ka:kb].transpose(0, 1)[None], attn_mask=mask, scale=scale,
+                                                   enable_gqa=k.shape[1] != q.shape[1])[0].transpose(0, 1))
+    return torch.cat(outs)
+
+
+def scaled_mm_contract(a, b, scale_a, scale_b, out_dtype=torch.bfloat16, **_):
+    return ((a.float() @ b.float()) * scale_a * scale_b).to(out_dtype)
+
+
+def import_reference(root: Path) -> None:
+    sys.path.insert(0, str(root / "src"))
+    if "transformers.models.gemma4_unified" not in sys.modules:
+        pkg = types.ModuleType("transformers.models.gemma4_unified")
+        mod = types.ModuleType("transformers.models.gemma4_unified.modeling_gemma4_unified")
+        mod.Gemma4UnifiedModel = type("Gemma4UnifiedModel", (), {})
+        pkg.modeling_gemma4_unified = mod
+        sys.modules[pkg.__name__] = pkg
+        sys.modules[mod.__name__] = mod
+    with contextlib.suppress(ImportError):
+        import pybase64  # noqa: F401
+    if "pybase64" not in sys.modules:
+        import base64
+        stub = types.ModuleType("pybase64")
+        stub.b64decode = lambda s, validate=False: base64.b64decode(s, validate=validate)
+        sys.modules["pybase64"] = stub
+
+
+def to_torch(weights: dict[str, np.ndarray], key: str) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(weights[key]))
+
+
+def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5Config
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Model
+
+    rot = int(spec.head_dim * spec.partial_rotary)
+    half = rot // 2
+    section = [half - 2 * (half // 3), half // 3, half // 3]
+    text = dict(vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
+                num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
+                head_dim=spec.head_dim, rms_norm_eps=spec.eps, layer_types=["full_attention"] * spec.layers,
+                rope_parameters={"rope_type": "default", "rope_theta": spec.rope_theta,
+                                 "partial_rotary_factor": spec.partial_rotary, "mrope_section": section},
+                attention_bias=False, hidden_act="silu")
+    config = Qwen3_5Config(text_config=text, vision_config={"depth": 1, "hidden_size": 32, "intermediate_size": 64,
+                                                           "num_heads": 2, "out_hidden_size": spec.hidden})
+    config._attn_implementation = "sdpa"
+    model = Qwen3_5Model(config).float().eval()
+    lm = model.language_model
+    with torch.no_grad():
+        lm.embed_tokens.weight.copy_(to_torch(weights, "embed_tokens"))
+        lm.norm.weight.copy_(to_torch(weights, "norm"))
+        for i, layer in enumerate(lm.layers):
+            p = f"layers.{i}."
+            layer.block_type = layer.layer_type  # harness alias (Transformers 5.5 naming)
+            a = layer.self_attn
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                getattr(a, name).weight.copy_(to_torch(weights, p + name))
+            a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
+            a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                getattr(layer.mlp, name).weight.copy_(to_torch(weights, p + name))
+            layer.input_layernorm.weight.copy_(to_torch(weights, p + "input_layernorm"))
+            layer.post_attention_layernorm.weight.copy_(to_torch(weights, p + "post_attention_layernorm"))
+    return model
+
+
+def gemma_lm(spec: Spec, weights: dict[str, np.ndarray]):
+    from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
+    from transformers.models.gemma4.modeling_gemma4 import Gemma4TextModel
+
+    config = Gemma4TextConfig(
+        vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
+        num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
+        head_dim=spec.head_dim, global_head_dim=spec.head_dim, num_global_key_value_heads=spec.kv_heads,
+        attention_k_eq_v=False, sliding_window=spec.window, layer_types=spec.layer_types(),
+        hidden_size_per_layer_input=0, final_logit_softcapping=spec.logit_cap, rms_norm_eps=spec.eps,
+        hidden_activation="gelu_pytorch_tanh",
+        rope_parameters={"sliding_attention": {"rope_type": "default", "rope_theta": spec.rope_theta_local},
+                         "full_attention": {"rope_type": "default", "rope_theta": spec.rope_theta}})
+    config._attn_implementation = "sdpa"
+    lm = Gemma4TextModel(config).float().eval()
+    with torch.no_grad():
+        lm.embed_tokens.weight.copy_(to_torch(weights, "embed_tokens"))
+        lm.norm.weight.copy_(to_torch(weights, "norm"))
+        for i, layer in enumerate(lm.layers):
+            p = f"layers.{i}."
+            a = layer.self_attn
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                getattr(a, name).weight.copy_(to_torch(weights, p + name))
+            a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
+            a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                getattr(layer.mlp, name).weight.copy_(to_torch(weights, p + name))
+            for name in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                         "post_feedforward_layernorm"):
+                getattr(layer, name).weight.copy_(to_torch(weights, p + name))
+            layer.layer_scalar.copy_(to_torch(weights, p + "layer_scalar"))
+    return lm
+
+
+def encoded(arrays: dict[str, np.ndarray], blocks: bool):
+    from karpo_decision.encoding import Encoded
+
+    out = []
+    cu, markers, mcu = arrays["cu"], arrays["markers"], arrays["marker_cu"]
+    for s in range(len(cu) - 1):
+        a, b = int(cu[s]), int(cu[s + 1])
+        local = torch.from_numpy(markers[mcu[s]:mcu[s + 1]] - a)
+        n = b - a
+        kw = {}
+        if blocks:
+            kw = dict(positions=torch.arange(n), segment_ids=torch.zeros(n, dtype=torch.int16))
+        out.append(Encoded(keys=tuple(f"q{i}" for i in range(len(local))), counts=(3,) * len(local),
+                           input_ids=torch.from_numpy(arrays["input_ids"][a:b].copy()), markers=local, **kw))
+    return out
+
+
+def weights_digest(weights: dict[str, np.ndarray]) -> str:
+    h = hashlib.sha256()
+    for key in sorted(weights):
+        h.update(key.encode())
+        h.update(np.ascontiguousarray(weights[key], dtype=np.float32).tobytes())
+    return h.hexdigest()
+
+
+CASES = {
+    # 2 layers, hidden 256, 4/2 heads of 64, SwiGLU 1024, vocab 4096; 8 sequences U[32, 512].
+    "qwen_tiny": dict(spec=CONFIGS["tiny"], lengths=("uniform", 8, 32, 512), markers=(1, 1), fp8=False),
+    # Partial rotary (Qwen3.5's real layers rotate a quarter of each head), 1-4 markers per sequence.
+    "qwen_partial": dict(spec=small(CONFIGS["tiny"], partial_rotary=0.5, layers=2), lengths=("uniform", 6, 8, 200),
+                         markers=(1, 4), fp8=False),
+    # Gemma-shaped: 6 layers (5 sliding : 1 global), window 16, head 64.
+    "gemma_tiny": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
+                       lengths=("uniform", 6, 8, 96), markers=(1, 1), fp8=False),
+    # FP8 projections (serve/qwen_fp8.py and serve/fp8.py).
+    "qwen_tiny_fp8": dict(spec=CONFIGS["tiny"], lengths=("uniform", 4, 32, 160), markers=(1, 2), fp8=True),
+    "gemma_tiny_fp8": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
+                           lengths=("uniform", 4, 8, 96), markers=(1, 1), fp8=True),
+}
+
+
+#: FP8 cases also record, for layer 0, each quantized projection's input (e4m3 values and row scales) and output: the
+#: per-projection pin of the FP8 arithmetic (a random deep model amplifies single e4m3 rounding flips, so the end-to-end
+#: FP8 forward is compared only loosely, as the reference's own tests do: tests/gpu/test_fp8.py:4-5).
+PINNED = ("q_proj", "o_proj", "gate_proj", "down_proj")
+PIN_ROWS = 48
+
+
+def _record_fp8(stack: contextlib.ExitStack, module, captured: dict) -> None:
+    """Wraps ``module.Fp8Linear.forward`` to keep the first call's input and output of each layer-0 projection."""
+    original = module.Fp8Linear.forward
+
+    def forward(self, x):
+        out = original(self, x)
+        name = getattr(self, "_pin_name", None)
+        if name is not None and name not in captured:
+            if type(x).__name__ == "Quantized":
+                values, scale = x.values, x.scale
+            else:
+                values, scale = module.to_e4m3(x.reshape(-1, x.shape[-1]))
+            rows = PIN_ROWS  # the first rows suffice for the pin and keep the fixture small
+            captured[name] = (values.float().reshape(-1, values.shape[-1])[:rows].numpy(),
+                              scale.float().reshape(-1)[:rows].numpy(),
+                              out.float().reshape(-1, out.shape[-1])[:rows].numpy())
+        return out
+
+    stack.enter_context(_patched(module.Fp8Linear, "forward", forward))
+
+
+def _name_pins(packed, module) -> None:
+    for name, child in packed.layers[0].named_modules():
+        if isinstance(child, module.Fp8Linear) and name.rsplit(".", 1)[-1] in PINNED:
+            child._pin_name = name.rsplit(".", 1)[-1]
+
+
+def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
+    from karpo_decision.model.packed import pack
+    from karpo_decision.model.readout import Readout
+
+    spec: Spec = case["spec"]
+    weights = numpy_weights(spec, seed)
+    kind, n, low, high = case["lengths"]
+    rng = np.random.default_rng(seed)
+    lengths = [int(x) for x in rng.integers(low, high + 1, size=n)]
+    arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, case["markers"])
+    seqs = encoded(arrays, blocks=spec.family == "gemma")
+    head = Readout.from_rows(to_torch(weights, "readout"), cap=spec.logit_cap)
+    captured: dict = {}
+    with torch.inference_mode(), contextlib.ExitStack() as stack:
+        if case["fp8"]:
+            stack.enter_context(_patched(torch, "_scaled_mm", scaled_mm_contract))
+        if spec.family == "qwen":
+            from karpo_decision.families.qwen import packed as qp
+
+            model = qwen_backbone(spec, weights)
+            stack.enter_context(_patched(qp, "_kernels", lambda: (None, varlen_contract, None)))
+            packed = qp.Packed(model, "causal")
+            if case["fp8"]:
+                from karpo_decision.serve import qwen_fp8
+                qwen_fp8.quantize(packed)
+                _name_pins(packed, qwen_fp8)
+                _record_fp8(stack, qwen_fp8, captured)
+            p = pack(seqs, model, torch.device("cpu"))
+        else:
+            from karpo_decision.families.gemma import packed as gp
+            from karpo_decision.families.gemma import sliding_attention
+
+            lm = gemma_lm(spec, weights)
+            stack.enter_context(_patched(sliding_attention, "varlen_attn", varlen_contract))
+            stack.enter_context(_patched(gp, "sdpa_kernel", lambda *_: contextlib.nullcontext()))
+            packed = gp.Packed(types.SimpleNamespace(language_model=lm), "causal")
+            if case["fp8"]:
+                from karpo_decision.serve import fp8
+                stack.enter_context(_patched(fp8, "to_e4m3", fp8._rows_e4m3))
+                stack.enter_context(_patched(fp8, "norm_e4m3", fp8._norm_e4m3))
+                stack.enter_context(_patched(fp8, "gelu_mul_e4m3", fp8._gelu_mul_e4m3))
+                fp8.quantize(packed)
+                _name_pins(packed, fp8)
+                _record_fp8(stack, fp8, captured)
+            p = pack(seqs, None, torch.device("cpu"))
+        hidden = packed(p)
+        logits = head(hidden)
+    pins = {}
+    for proj, (values, scale, out) in captured.items():
+        pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
+    return {
+        **pins,
+        "input_ids": arrays["input_ids"], "seqpos": arrays["seqpos"], "cu": arrays["cu"],
+        "markers": arrays["markers"], "marker_cu": arrays["marker_cu"],
+        "hidden": hidden.float().numpy(), "logits": logits.float().numpy(),
+        "seed": np.array(seed), "weights_sha256": np.array(weights_digest(weights)),
+        "spec": np.array(repr(spec.as_dict())),
+    }
+
+
+@contextlib.contextmanager
+def _patched(obj, name, value):
+    old = getattr(obj, name)
+    setattr(obj, name, value)
+    try:
+        yield
+    finally:
+        setattr(obj, name, old)
+
+
+def main() -> None:
+    parser = argparse.ArgumentParser()
+    parser.add_argument("--reference", type=Path, required=True, help="root of a karpo-decision checkout")
+    parser.add_argument("--cases", nargs="*", default=list(CASES))
+    args = parser.parse_args()
+    import_reference(args.reference)
+    torch.manual_seed(0)
+    for name in args.cases:
+        out = run_case(name, CASES[name])
+        np.savez_compressed(HERE / f"{name}.npz", **out)
+        print(name, "tokens", len(out["input_ids"]), "markers", len(out["markers"]), "hidden", out["hidden"].shape,
+              "logit range", float(np.abs(out["logits"]).max()))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,31 @@
+"""Loading the golden fixtures (tests/golden/*.npz, made by tests/golden/make_golden.py from the reference itself)."""
+
+from __future__ import annotations
+
+import ast
+import hashlib
+from pathlib import Path
+
+import numpy as np
+
+from karpo_decision_b200.synthetic import Spec, numpy_weights
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "qwen_tiny_fp8", "gemma_tiny_fp8"]
+
+
+def load(name: str) -> tuple[Spec, dict, dict, dict]:
+    """(spec, weights, pack arrays, expected outputs) of golden case ``name``; the regenerated weights are checked
+    against the digest recorded with the fixture."""
+    z = np.load(GOLDEN / f"{name}.npz")
+    spec = Spec(**ast.literal_eval(str(z["spec"])))
+    weights = numpy_weights(spec, int(z["seed"]))
+    h = hashlib.sha256()
+    for key in sorted(weights):
+        h.update(key.encode())
+        h.update(np.ascontiguousarray(weights[key], dtype=np.float32).tobytes())
+    if h.hexdigest() != str(z["weights_sha256"]):
+        raise AssertionError(f"{name}: regenerated weights differ from the ones the fixture was made with")
+    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu")}
+    expected = {"hidden": z["hidden"], "logits": z["logits"]}
+    return spec, weights, pack, expected

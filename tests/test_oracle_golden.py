@@ -1,0 +1,72 @@
+"""The CPU oracle (oracle/, a numpy restatement) against golden fixtures made by running the reference's own packed
+forward and readout (tests/golden/make_golden.py): the pin that makes the oracle a trustworthy checker."""
+
+import numpy as np
+import pytest
+
+import oracle
+from golden_cases import CASES, GOLDEN, load
+
+PLAIN = [c for c in CASES if not c.endswith("_fp8")]
+FP8 = [c for c in CASES if c.endswith("_fp8")]
+
+
+def forward(spec):
+    return oracle.qwen_forward if spec.family == "qwen" else oracle.gemma_forward
+
+
+@pytest.mark.parametrize("name", PLAIN)
+def test_oracle_matches_reference_fixture(name):
+    spec, weights, pack, expected = load(name)
+    hidden = forward(spec)(weights, spec.as_dict(), pack, mode="fp32")
+    logits = oracle.readout(hidden, weights["readout"], spec.logit_cap)
+    scale = np.abs(expected["hidden"]).max()
+    # float32 restatement vs float32 reference: only the summation order differs.
+    assert np.abs(hidden - expected["hidden"]).max() <= 2e-4 * scale, name
+    assert np.abs(logits - expected["logits"]).max() <= 2e-4, name
+    assert (logits.argmax(-1) == expected["logits"].argmax(-1)).all()
+
+
+@pytest.mark.parametrize("name", FP8)
+def test_oracle_fp8_projection_matches_reference(name):
+    """Layer 0's quantized projections, given the reference's own e4m3 inputs and scales: the oracle's weight
+    quantization and rowwise-scaled product reproduce the reference's outputs (float32 summation order only)."""
+    spec, weights, _, _ = load(name)
+    z = np.load(GOLDEN / f"{name}.npz")
+    pinned = [k[len("pin_"):-len("_out")] for k in z.files if k.startswith("pin_") and k.endswith("_out")]
+    assert pinned, "fixture has no pinned projections"
+    for proj in pinned:
+        w = weights[f"layers.0.{proj}"]
+        qw, sw = oracle.e4m3_rows(w)
+        got = (z[f"pin_{proj}_in"] @ qw.T) * z[f"pin_{proj}_scale"][:, None] * sw.reshape(1, -1)
+        want = z[f"pin_{proj}_out"]
+        assert np.abs(got - want).max() <= 1e-5 * max(np.abs(want).max(), 1e-6), proj
+
+
+@pytest.mark.parametrize("name", FP8)
+def test_oracle_fp8_forward_tracks_reference(name):
+    """The whole FP8 forward: a deep random model turns single e4m3 rounding flips (from float32 summation-order
+    differences in the norms) into visible output changes, so this is a loose check, like the reference's own
+    comparison of its FP8 path (cosine, tests/gpu/test_cuda_qwen_fast.py:60-72)."""
+    spec, weights, pack, expected = load(name)
+    hidden = forward(spec)(weights, spec.as_dict(), pack, mode="fp32", fp8=True)
+    a, b = hidden.ravel(), expected["hidden"].ravel()
+    cosine = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+    assert cosine > 0.9, cosine
+
+
+def test_bf16_rounding_is_nearest_even():
+    import torch
+
+    x = np.array([1.0, 1.00390625, 1.01171875, -2.5, 3.140625, 1e-30], dtype=np.float32)
+    assert np.array_equal(oracle.bf16(x), torch.from_numpy(x).bfloat16().float().numpy())
+
+
+def test_e4m3_matches_torch_cast():
+    import torch
+
+    rng = np.random.default_rng(0)
+    x = np.concatenate([rng.standard_normal(4096).astype(np.float32) * 100,
+                        np.array([0.0, 448.0, -448.0, 1e-4, 0.0009765625, 240.0, 232.0], dtype=np.float32)])
+    ref = torch.from_numpy(x).to(torch.float8_e4m3fn).float().numpy()
+    assert np.array_equal(oracle.packed.e4m3(x), ref)
