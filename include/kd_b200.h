@@ -109,7 +109,7 @@ int kd_rope_table(const float* inv_freq, int rot, int64_t positions, float* cos_
  * ungated (Gemma 4) [Hq x q_hd][Hkv x k_hd][Hkv x v_hd].
  * q/k norm modes KD_NORM_*; v_norm_mode < 0 leaves v unnormalised (Qwen), KD_NORM_NONE is Gemma's v_norm.
  * Replaces families/qwen/packed.py:108-121 (_qkv + fused.rope) and families/gemma/packed.py:183-193 (_q, _kv). */
-int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int32_t* seqpos, int num_heads_q,
+int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* seqpos, int num_heads_q,
                      int num_heads_kv, int head_dim, int gated, const void* q_norm_w, const void* k_norm_w,
                      int qk_norm_mode, int v_norm_mode, float eps, const float* cos_tab, const float* sin_tab, int rot,
                      void* q, void* k, void* v, void* gate, cudaStream_t stream);

@@ -68,8 +68,24 @@ def last_error() -> str:
     return buf.value.decode(errors="replace")
 
 
+_profiler = None
+
+
+def set_profiler(profiler) -> None:
+    """Installs (or removes, with None) the per-launch event recorder of ``profile.kernels``."""
+    global _profiler
+    _profiler = profiler
+
+
 def call(name: str, *args) -> None:
     """Calls entry point ``name``; raises KernelError with the library's message on a non-zero status."""
-    rc = getattr(load(), name)(*args)
+    fn = getattr(load(), name)
+    prof = _profiler
+    if prof is None:
+        rc = fn(*args)
+    else:
+        token = prof.before(name, args)
+        rc = fn(*args)
+        prof.after(name, args, token)
     if rc != KD_OK:
         raise KernelError(f"{name} failed ({rc}): {last_error()}")

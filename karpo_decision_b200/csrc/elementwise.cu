@@ -1,0 +1,529 @@
+// Memory-bound kernels of the packed forward: embedding gather, RMSNorm variants (with residual sums, layer scalar and
+// e4m3 quantization fused), q/k/v norm + RoPE on the fused QKV projection output, rotary tables, the marker head and
+// the readout. All use 16-byte vector accesses along contiguous rows; one warp per row (or per token-head).
+//
+// Numerics follow the reference's fused pointwise ops (families/qwen/fused.py, families/gemma/fused.py,
+// serve/fp8.py): float32 math on bf16 inputs with one bf16 rounding per compiled op output.
+#include "common.cuh"
+#include "kd_internal.h"
+
+namespace kd {
+namespace ew {
+
+constexpr int WARPS = 8;  // rows per 256-thread block
+
+KD_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+KD_DEVICE float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+KD_DEVICE void load8(const __nv_bfloat16* p, float (&f)[8]) {
+  uint4 v = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float2 t = unpack_bf16x2(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+KD_DEVICE void store8(__nv_bfloat16* p, const float (&f)[8]) {
+  *reinterpret_cast<uint4*>(p) =
+      make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+}
+
+// Multiplier of the normalized value: none, w, or 1 + w (norm_mode KD_NORM_*).
+KD_DEVICE void norm_weights(const __nv_bfloat16* w, int mode, int col, float (&m)[8]) {
+  if (mode == KD_NORM_NONE || w == nullptr) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = 1.0f;
+    return;
+  }
+  load8(w + col, m);
+  if (mode == KD_NORM_ONE_PLUS) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m[i] = 1.0f + m[i];
+  }
+}
+
+// 1 / sqrt(mean(x^2) + eps) with IEEE-rounded sqrt and division.
+KD_DEVICE float inv_rms(float sumsq, int cols, float eps) { return 1.0f / sqrtf(sumsq / (float)cols + eps); }
+
+// ------------------------------------------------------------------------------------------------ embedding
+
+__global__ void embed_kernel(const int64_t* __restrict__ ids, int64_t T, const __nv_bfloat16* __restrict__ table,
+                             int64_t vocab, int hidden, float scale, __nv_bfloat16* __restrict__ out) {
+  const int64_t row = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (row >= T) return;
+  int64_t id = ids[row];
+  id = id < 0 ? 0 : (id >= vocab ? vocab - 1 : id);  // ids outside the vocabulary clamp (validated on the host)
+  const __nv_bfloat16* src = table + id * hidden;
+  __nv_bfloat16* dst = out + row * hidden;
+  const int lane = threadIdx.x & 31;
+  for (int c = lane * 8; c < hidden; c += 256) {
+    if (scale == 0.0f) {
+      *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+    } else {
+      float f[8];
+      load8(src + c, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] *= scale;  // bf16 x bf16(scale), rounded once
+      store8(dst + c, f);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ RMSNorm family
+
+// out = norm(x) (optionally gathered rows: src row = rows_idx[row]).
+__global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, const int64_t* __restrict__ rows_idx,
+                               const __nv_bfloat16* __restrict__ w, int mode, float eps, __nv_bfloat16* __restrict__ out,
+                               int64_t ldo, int64_t rows, int cols) {
+  const int64_t row = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t src_row = rows_idx ? rows_idx[row] : row;
+  const __nv_bfloat16* xr = x + src_row * ldx;
+  float ss = 0.f;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float f[8];
+    load8(xr + c, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  }
+  const float inv = inv_rms(warp_sum(ss), cols, eps);
+  __nv_bfloat16* orow = out + row * ldo;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float f[8], m[8];
+    load8(xr + c, f);
+    norm_weights(w, mode, c, m);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = (f[i] * inv) * m[i];
+    store8(orow + c, f);
+  }
+}
+
+// Qwen residual: h = bf16(h + x); y = norm(h).
+__global__ void add_rmsnorm_kernel(__nv_bfloat16* __restrict__ h, const __nv_bfloat16* __restrict__ x,
+                                   const __nv_bfloat16* __restrict__ w, int mode, float eps,
+                                   __nv_bfloat16* __restrict__ y, int64_t rows, int cols) {
+  const int64_t row = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  __nv_bfloat16* hr = h + row * cols;
+  const __nv_bfloat16* xr = x + row * cols;
+  float ss = 0.f;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float a[8], b[8];
+    load8(hr + c, a);
+    load8(xr + c, b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      a[i] = bf16_round(a[i] + b[i]);
+      ss += a[i] * a[i];
+    }
+    store8(hr + c, a);
+  }
+  const float inv = inv_rms(warp_sum(ss), cols, eps);
+  __syncwarp();
+  __nv_bfloat16* yr = y + row * cols;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float a[8], m[8];
+    load8(hr + c, a);
+    norm_weights(w, mode, c, m);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a[i] = (a[i] * inv) * m[i];
+    store8(yr + c, a);
+  }
+}
+
+// Gemma residual: out = bf16(h + norm(x)); with a layer scalar: out = bf16((h + bf16(norm(x))) * scalar);
+// mode < 0 skips the norm (x is already normed).
+__global__ void norm_add_kernel(const __nv_bfloat16* h, const __nv_bfloat16* __restrict__ x,
+                                const __nv_bfloat16* __restrict__ w, int mode, float eps,
+                                const __nv_bfloat16* __restrict__ scalar, __nv_bfloat16* out, int64_t rows, int cols) {
+  const int64_t row = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat16* hr = h + row * cols;
+  const __nv_bfloat16* xr = x + row * cols;
+  float inv = 1.0f;
+  if (mode >= 0) {
+    float ss = 0.f;
+    for (int c = lane * 8; c < cols; c += 256) {
+      float f[8];
+      load8(xr + c, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+    inv = inv_rms(warp_sum(ss), cols, eps);
+  }
+  const float s = scalar ? __bfloat162float(*scalar) : 1.0f;
+  __nv_bfloat16* orow = out + row * cols;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float a[8], b[8], m[8];
+    load8(hr + c, a);
+    load8(xr + c, b);
+    if (mode >= 0) {
+      norm_weights(w, mode, c, m);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) b[i] = (b[i] * inv) * m[i];
+    }
+    if (scalar) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = (a[i] + bf16_round(b[i])) * s;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a[i] = a[i] + b[i];
+    }
+    store8(orow + c, a);
+  }
+}
+
+// y = bf16(norm(x)) (or x itself when mode < 0), then per-row e4m3: s = max(amax(y), 1e-12) * (1 / 448),
+// q = e4m3(clamp(y / s, +-448)) (serve/fp8.py:21-24, :57-69).
+__global__ void rmsnorm_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                    const __nv_bfloat16* __restrict__ w, int mode, float eps,
+                                    __nv_fp8_e4m3* __restrict__ q, float* __restrict__ scale, int64_t rows, int cols) {
+  const int64_t row = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (row >= rows) return;
+  const int lane = threadIdx.x & 31;
+  const __nv_bfloat16* xr = x + row * ldx;
+  float inv = 1.0f;
+  if (mode >= 0) {
+    float ss = 0.f;
+    for (int c = lane * 8; c < cols; c += 256) {
+      float f[8];
+      load8(xr + c, f);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+    inv = inv_rms(warp_sum(ss), cols, eps);
+  }
+  float amax = 0.f;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float f[8], m[8];
+    load8(xr + c, f);
+    if (mode >= 0) norm_weights(w, mode, c, m);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float yv = mode >= 0 ? bf16_round((f[i] * inv) * m[i]) : f[i];
+      amax = fmaxf(amax, fabsf(yv));
+    }
+  }
+  amax = warp_max(amax);
+  // torch on CUDA divides a tensor by a scalar as a multiply by the float32 reciprocal (the reference's
+  // amax / E4M3_MAX), so the scale is formed the same way; the values divide by the scale exactly.
+  const float s = fmaxf(amax, 1e-12f) * (1.0f / 448.0f);
+  if (lane == 0) scale[row] = s;
+  __nv_fp8_e4m3* qr = q + row * (int64_t)cols;
+  for (int c = lane * 8; c < cols; c += 256) {
+    float f[8], m[8];
+    load8(xr + c, f);
+    if (mode >= 0) norm_weights(w, mode, c, m);
+    uint8_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float yv = mode >= 0 ? bf16_round((f[i] * inv) * m[i]) : f[i];
+      const float v = fminf(fmaxf(yv / s, -448.0f), 448.0f);
+      b[i] = (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+    }
+    *reinterpret_cast<uint2*>(qr + c) = *reinterpret_cast<uint2*>(b);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ RoPE
+
+__global__ void rope_table_kernel(const float* __restrict__ inv_freq, int rot, int64_t positions,
+                                  float* __restrict__ cos_out, float* __restrict__ sin_out) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= positions * rot) return;
+  const int64_t p = idx / rot;
+  const int i = (int)(idx % rot);
+  const float emb = (float)p * inv_freq[i % (rot / 2)];  // freqs = position x inv_freq in float32, cat(f, f)
+  cos_out[idx] = bf16_round(cosf(emb));
+  sin_out[idx] = bf16_round(sinf(emb));
+}
+
+// One warp per (token, head). Heads 0..Hq-1 are queries, Hq..Hq+Hkv-1 keys, then Hkv values.
+template <int HD>
+__global__ void qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld, int64_t T,
+                                     const int64_t* __restrict__ seqpos, int hq, int hkv, int gated,
+                                     const __nv_bfloat16* __restrict__ qw, const __nv_bfloat16* __restrict__ kw,
+                                     int qk_mode, int v_mode, float eps, const float* __restrict__ cos_tab,
+                                     const float* __restrict__ sin_tab, int rot, __nv_bfloat16* __restrict__ q,
+                                     __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v,
+                                     __nv_bfloat16* __restrict__ gate) {
+  constexpr int PER = HD / 32;  // elements per lane (2, 4 or 8)
+  __shared__ float stage[WARPS][HD];
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const int heads = hq + 2 * hkv;
+  const int64_t item = (int64_t)blockIdx.x * WARPS + warp;
+  if (item >= T * heads) return;
+  const int64_t t = item / heads;
+  const int head = (int)(item % heads);
+  const int q_cols = hq * HD * (gated ? 2 : 1);
+  const __nv_bfloat16* row = qkv + t * ld;
+  const bool is_q = head < hq;
+  const bool is_k = !is_q && head < hq + hkv;
+  const __nv_bfloat16* src;
+  __nv_bfloat16* dst;
+  if (is_q) {
+    src = row + (int64_t)head * HD * (gated ? 2 : 1);
+    dst = q + (t * hq + head) * HD;
+  } else if (is_k) {
+    src = row + q_cols + (int64_t)(head - hq) * HD;
+    dst = k + (t * hkv + (head - hq)) * HD;
+  } else {
+    src = row + q_cols + (int64_t)hkv * HD + (int64_t)(head - hq - hkv) * HD;
+    dst = v + (t * hkv + (head - hq - hkv)) * HD;
+  }
+  float f[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) f[i] = __bfloat162float(src[lane * PER + i]);
+
+  if (is_q && gated) {  // the query's gate half passes through to the output gate buffer
+    const __nv_bfloat16* g = src + HD;
+    __nv_bfloat16* gd = gate + (t * hq + head) * HD;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) gd[lane * PER + i] = g[lane * PER + i];
+  }
+  if (!is_q && !is_k) {  // values: Gemma's v_norm (no weight) or a plain copy (Qwen)
+    if (v_mode >= 0) {
+      float ss = 0.f;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) ss += f[i] * f[i];
+      const float inv = inv_rms(warp_sum(ss), HD, eps);
+#pragma unroll
+      for (int i = 0; i < PER; ++i) f[i] *= inv;
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) dst[lane * PER + i] = __float2bfloat16_rn(f[i]);
+    return;
+  }
+  // q / k: per-head RMSNorm over HD, then rotate-half RoPE on the first `rot` dims.
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) ss += f[i] * f[i];
+  const float inv = inv_rms(warp_sum(ss), HD, eps);
+  const __nv_bfloat16* nw = is_q ? qw : kw;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int d = lane * PER + i;
+    float m = 1.0f;
+    if (qk_mode == KD_NORM_WEIGHT) m = __bfloat162float(nw[d]);
+    if (qk_mode == KD_NORM_ONE_PLUS) m = 1.0f + __bfloat162float(nw[d]);
+    f[i] = (f[i] * inv) * m;
+    if (gated) f[i] = bf16_round(f[i]);  // Qwen: the norm is its own op (rounded), RoPE another
+    stage[warp][d] = f[i];
+  }
+  __syncwarp();
+  const int64_t pos = seqpos[t];
+  const float* ct = cos_tab + (int64_t)pos * rot;
+  const float* st = sin_tab + (int64_t)pos * rot;
+  const int half = rot / 2;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int d = lane * PER + i;
+    float o = f[i];
+    if (d < rot) {
+      const float partner = d < half ? -stage[warp][d + half] : stage[warp][d - half];
+      o = f[i] * ct[d] + partner * st[d];
+    }
+    dst[d] = __float2bfloat16_rn(o);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------ readout
+
+// logits[m, c] = sum_k float(hidden[m, k]) * W[c, k]; cap * tanh(logits / cap) when cap > 0. One warp per (m, c).
+__global__ void readout_kernel(const __nv_bfloat16* __restrict__ hidden, int64_t M, int hs,
+                               const float* __restrict__ W, int codes, float cap, float* __restrict__ logits) {
+  const int64_t item = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (item >= M * codes) return;
+  const int lane = threadIdx.x & 31;
+  const int64_t m = item / codes;
+  const int c = (int)(item % codes);
+  const __nv_bfloat16* hr = hidden + m * hs;
+  const float* wr = W + (int64_t)c * hs;
+  float acc = 0.f;
+  for (int k = lane * 8; k < hs; k += 256) {
+    float f[8];
+    load8(hr + k, f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc += f[i] * wr[k + i];
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) logits[item] = cap > 0.f ? cap * tanhf(acc / cap) : acc;
+}
+
+}  // namespace ew
+}  // namespace kd
+
+using namespace kd;
+using kd::ew::WARPS;
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+static unsigned blocks_for(int64_t items) { return (unsigned)((items + WARPS - 1) / WARPS); }
+
+extern "C" int kd_embed(const int64_t* ids, int64_t T, const void* table, int64_t vocab, int hidden, float scale,
+                        void* out, cudaStream_t stream) {
+  if (T < 0 || vocab <= 0 || hidden <= 0 || hidden % 8) return set_error(KD_ERR_ARGUMENT, "embed: bad sizes");
+  if (T == 0) return KD_OK;
+  if (!ids || !table || !out || !aligned16(table) || !aligned16(out))
+    return set_error(KD_ERR_ARGUMENT, "embed: null or unaligned pointer");
+  const float s = scale == 0.0f ? 0.0f : __bfloat162float(__float2bfloat16_rn(scale));
+  ew::embed_kernel<<<blocks_for(T), 32 * WARPS, 0, stream>>>(ids, T, static_cast<const __nv_bfloat16*>(table), vocab,
+                                                              hidden, s, static_cast<__nv_bfloat16*>(out));
+  return record_cuda_error(cudaGetLastError(), "embed: launch");
+}
+
+static int check_norm(const void* x, const void* out, int mode, const void* w, int cols, const char* what) {
+  if (cols <= 0 || cols % 8) return set_error(KD_ERR_ARGUMENT, "norm: cols must be a positive multiple of 8");
+  if (!x || !out || !aligned16(x) || !aligned16(out)) return set_error(KD_ERR_ARGUMENT, what);
+  if (mode > KD_NORM_NONE && (!w || !aligned16(w))) return set_error(KD_ERR_ARGUMENT, "norm: weight required");
+  if (mode > KD_NORM_ONE_PLUS) return set_error(KD_ERR_ARGUMENT, "norm: unknown norm mode");
+  return KD_OK;
+}
+
+extern "C" int kd_rmsnorm(const void* x, int64_t ldx, const void* weight, int norm_mode, float eps, void* out,
+                          int64_t ldo, int64_t rows, int cols, cudaStream_t stream) {
+  if (rows < 0) return set_error(KD_ERR_ARGUMENT, "rmsnorm: rows < 0");
+  if (rows == 0) return KD_OK;
+  int rc = check_norm(x, out, norm_mode, weight, cols, "rmsnorm: null or unaligned x/out");
+  if (rc) return rc;
+  if (norm_mode < 0) return set_error(KD_ERR_ARGUMENT, "rmsnorm: norm_mode must be KD_NORM_*");
+  if (ldx % 8 || ldo % 8 || ldx < cols || ldo < cols) return set_error(KD_ERR_ARGUMENT, "rmsnorm: bad strides");
+  ew::rmsnorm_kernel<<<blocks_for(rows), 32 * WARPS, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, nullptr, static_cast<const __nv_bfloat16*>(weight), norm_mode, eps,
+      static_cast<__nv_bfloat16*>(out), ldo, rows, cols);
+  return record_cuda_error(cudaGetLastError(), "rmsnorm: launch");
+}
+
+extern "C" int kd_add_rmsnorm(void* h, const void* x, const void* weight, int norm_mode, float eps, void* y,
+                              int64_t rows, int cols, cudaStream_t stream) {
+  if (rows < 0) return set_error(KD_ERR_ARGUMENT, "add_rmsnorm: rows < 0");
+  if (rows == 0) return KD_OK;
+  int rc = check_norm(h, y, norm_mode, weight, cols, "add_rmsnorm: null or unaligned h/y");
+  if (rc) return rc;
+  if (!x || !aligned16(x) || norm_mode < 0) return set_error(KD_ERR_ARGUMENT, "add_rmsnorm: bad x or norm mode");
+  ew::add_rmsnorm_kernel<<<blocks_for(rows), 32 * WARPS, 0, stream>>>(
+      static_cast<__nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(x), static_cast<const __nv_bfloat16*>(weight),
+      norm_mode, eps, static_cast<__nv_bfloat16*>(y), rows, cols);
+  return record_cuda_error(cudaGetLastError(), "add_rmsnorm: launch");
+}
+
+extern "C" int kd_norm_add(const void* h, const void* x, const void* weight, int norm_mode, float eps,
+                           const void* scalar, void* out, int64_t rows, int cols, cudaStream_t stream) {
+  if (rows < 0) return set_error(KD_ERR_ARGUMENT, "norm_add: rows < 0");
+  if (rows == 0) return KD_OK;
+  int rc = check_norm(h, out, norm_mode, weight, cols, "norm_add: null or unaligned h/out");
+  if (rc) return rc;
+  if (!x || !aligned16(x)) return set_error(KD_ERR_ARGUMENT, "norm_add: null or unaligned x");
+  ew::norm_add_kernel<<<blocks_for(rows), 32 * WARPS, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(h), static_cast<const __nv_bfloat16*>(x),
+      static_cast<const __nv_bfloat16*>(weight), norm_mode, eps, static_cast<const __nv_bfloat16*>(scalar),
+      static_cast<__nv_bfloat16*>(out), rows, cols);
+  return record_cuda_error(cudaGetLastError(), "norm_add: launch");
+}
+
+extern "C" int kd_rmsnorm_e4m3(const void* x, int64_t ldx, const void* weight, int norm_mode, float eps, void* q,
+                               float* scale, int64_t rows, int cols, cudaStream_t stream) {
+  if (rows < 0) return set_error(KD_ERR_ARGUMENT, "rmsnorm_e4m3: rows < 0");
+  if (rows == 0) return KD_OK;
+  int rc = check_norm(x, q, norm_mode, weight, cols, "rmsnorm_e4m3: null or unaligned x/q");
+  if (rc) return rc;
+  if (!scale || ldx % 8 || ldx < cols) return set_error(KD_ERR_ARGUMENT, "rmsnorm_e4m3: bad scale or ldx");
+  ew::rmsnorm_e4m3_kernel<<<blocks_for(rows), 32 * WARPS, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(weight), norm_mode, eps,
+      static_cast<__nv_fp8_e4m3*>(q), scale, rows, cols);
+  return record_cuda_error(cudaGetLastError(), "rmsnorm_e4m3: launch");
+}
+
+extern "C" int kd_quantize_rows_e4m3(const void* x, int64_t rows, int cols, void* q, float* scale,
+                                     cudaStream_t stream) {
+  return kd_rmsnorm_e4m3(x, cols, nullptr, -1, 0.0f, q, scale, rows, cols, stream);
+}
+
+extern "C" int kd_rope_table(const float* inv_freq, int rot, int64_t positions, float* cos_out, float* sin_out,
+                             cudaStream_t stream) {
+  if (rot <= 0 || rot % 2 || positions < 0 || !inv_freq || !cos_out || !sin_out)
+    return set_error(KD_ERR_ARGUMENT, "rope_table: bad arguments");
+  const int64_t n = positions * rot;
+  if (n == 0) return KD_OK;
+  ew::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(inv_freq, rot, positions, cos_out, sin_out);
+  return record_cuda_error(cudaGetLastError(), "rope_table: launch");
+}
+
+extern "C" int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* seqpos, int num_heads_q,
+                                int num_heads_kv, int head_dim, int gated, const void* q_norm_w, const void* k_norm_w,
+                                int qk_norm_mode, int v_norm_mode, float eps, const float* cos_tab,
+                                const float* sin_tab, int rot, void* q, void* k, void* v, void* gate,
+                                cudaStream_t stream) {
+  if (T < 0 || num_heads_q <= 0 || num_heads_kv <= 0 || num_heads_q % num_heads_kv)
+    return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: bad head counts");
+  if (T == 0) return KD_OK;
+  if (rot < 0 || rot > head_dim || rot % 2) return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: bad rotary width");
+  if (!qkv || !seqpos || !q || !k || !v || (gated && !gate) || (rot > 0 && (!cos_tab || !sin_tab)))
+    return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: null pointer");
+  if (qk_norm_mode > KD_NORM_NONE && (!q_norm_w || !k_norm_w))
+    return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: q/k norm weights required");
+  const int64_t width = (int64_t)num_heads_q * head_dim * (gated ? 2 : 1) + 2LL * num_heads_kv * head_dim;
+  if (ldqkv < width) return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: ldqkv smaller than the projection width");
+  const int64_t items = T * (num_heads_q + 2 * num_heads_kv);
+  const auto* in = static_cast<const __nv_bfloat16*>(qkv);
+  const auto* qw = static_cast<const __nv_bfloat16*>(q_norm_w);
+  const auto* kw = static_cast<const __nv_bfloat16*>(k_norm_w);
+  auto* qo = static_cast<__nv_bfloat16*>(q);
+  auto* ko = static_cast<__nv_bfloat16*>(k);
+  auto* vo = static_cast<__nv_bfloat16*>(v);
+  auto* go = static_cast<__nv_bfloat16*>(gate);
+#define KD_QKV_CASE(HD)                                                                                          \
+  case HD:                                                                                                       \
+    ew::qkv_norm_rope_kernel<HD><<<blocks_for(items), 32 * WARPS, 0, stream>>>(                                  \
+        in, ldqkv, T, seqpos, num_heads_q, num_heads_kv, gated, qw, kw, qk_norm_mode, v_norm_mode, eps, cos_tab, \
+        sin_tab, rot, qo, ko, vo, go);                                                                           \
+    break;
+  switch (head_dim) {
+    KD_QKV_CASE(64)
+    KD_QKV_CASE(128)
+    KD_QKV_CASE(256)
+    default:
+      return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: head_dim must be 64, 128 or 256");
+  }
+#undef KD_QKV_CASE
+  return record_cuda_error(cudaGetLastError(), "qkv_norm_rope: launch");
+}
+
+extern "C" int kd_marker_norm(const void* h, int hidden, const int64_t* markers, int64_t M, const void* weight,
+                              int norm_mode, float eps, void* out, cudaStream_t stream) {
+  if (M < 0) return set_error(KD_ERR_ARGUMENT, "marker_norm: M < 0");
+  if (M == 0) return KD_OK;
+  int rc = check_norm(h, out, norm_mode, weight, hidden, "marker_norm: null or unaligned h/out");
+  if (rc) return rc;
+  if (!markers || norm_mode < 0) return set_error(KD_ERR_ARGUMENT, "marker_norm: bad markers or norm mode");
+  ew::rmsnorm_kernel<<<blocks_for(M), 32 * WARPS, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(h), hidden, markers, static_cast<const __nv_bfloat16*>(weight), norm_mode,
+      eps, static_cast<__nv_bfloat16*>(out), hidden, M, hidden);
+  return record_cuda_error(cudaGetLastError(), "marker_norm: launch");
+}
+
+extern "C" int kd_readout(const void* hidden, int64_t M, int hidden_size, const float* weight, int codes, float cap,
+                          float* logits, cudaStream_t stream) {
+  if (M < 0 || codes <= 0 || hidden_size <= 0 || hidden_size % 8)
+    return set_error(KD_ERR_ARGUMENT, "readout: bad sizes");
+  if (M == 0) return KD_OK;
+  if (!hidden || !weight || !logits || !aligned16(hidden)) return set_error(KD_ERR_ARGUMENT, "readout: bad pointers");
+  ew::readout_kernel<<<blocks_for(M * codes), 32 * WARPS, 0, stream>>>(static_cast<const __nv_bfloat16*>(hidden), M,
+                                                                     hidden_size, weight, codes, cap, logits);
+  return record_cuda_error(cudaGetLastError(), "readout: launch");
+}

@@ -98,3 +98,150 @@ def gemm_fp8(a: torch.Tensor, scale_a: torch.Tensor, w: torch.Tensor, scale_w: t
          residual.stride(0) if residual is not None else 0, m, n, a.shape[1], epilogue,
          status_word(a.device).data_ptr(), _stream(a))
     return out
+
+
+def embed(ids: torch.Tensor, table: torch.Tensor, scale: float = 0.0, out: torch.Tensor | None = None
+          ) -> torch.Tensor:
+    """``table[ids]`` (times bf16(scale) when scale != 0)."""
+    _require(ids.dtype == torch.int64 and ids.is_contiguous(), "ids must be contiguous int64")
+    _rowmajor(table, "table")
+    t = ids.numel()
+    if out is None:
+        out = torch.empty(t, table.shape[1], dtype=torch.bfloat16, device=table.device)
+    call("kd_embed", ids.data_ptr(), t, table.data_ptr(), table.shape[0], table.shape[1], float(scale),
+         out.data_ptr(), _stream(table))
+    return out
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor | None, mode: int, eps: float,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    _rowmajor(x, "x")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    call("kd_rmsnorm", x.data_ptr(), x.stride(0), _ptr(weight), mode, float(eps), out.data_ptr(), out.stride(0),
+         x.shape[0], x.shape[1], _stream(x))
+    return out
+
+
+def add_rmsnorm(h: torch.Tensor, x: torch.Tensor, weight: torch.Tensor, mode: int, eps: float,
+                y: torch.Tensor | None = None) -> torch.Tensor:
+    """In place ``h = h + x``; returns ``norm(h)``."""
+    _require(h.is_contiguous() and x.is_contiguous() and h.shape == x.shape, "h and x: same contiguous shape")
+    if y is None:
+        y = torch.empty_like(h)
+    call("kd_add_rmsnorm", h.data_ptr(), x.data_ptr(), _ptr(weight), mode, float(eps), y.data_ptr(), h.shape[0],
+         h.shape[1], _stream(h))
+    return y
+
+
+def norm_add(h: torch.Tensor, x: torch.Tensor, weight: torch.Tensor | None, mode: int, eps: float,
+             scalar: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``h + norm(x)``, or ``(h + bf16(norm(x))) * scalar``; ``out`` may be ``h``."""
+    _require(h.is_contiguous() and x.is_contiguous() and h.shape == x.shape, "h and x: same contiguous shape")
+    if out is None:
+        out = torch.empty_like(h)
+    call("kd_norm_add", h.data_ptr(), x.data_ptr(), _ptr(weight), mode, float(eps), _ptr(scalar), out.data_ptr(),
+         h.shape[0], h.shape[1], _stream(h))
+    return out
+
+
+def rmsnorm_e4m3(x: torch.Tensor, weight: torch.Tensor | None, mode: int, eps: float,
+                 q: torch.Tensor | None = None, scale: torch.Tensor | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """``norm(x)`` rounded to bf16 and quantized per row to e4m3 (mode < 0: no norm); returns (q, scale)."""
+    _rowmajor(x, "x")
+    rows, cols = x.shape
+    if q is None:
+        q = torch.empty(rows, cols, dtype=torch.float8_e4m3fn, device=x.device)
+    if scale is None:
+        scale = torch.empty(rows, dtype=torch.float32, device=x.device)
+    call("kd_rmsnorm_e4m3", x.data_ptr(), x.stride(0), _ptr(weight), mode, float(eps), q.data_ptr(),
+         scale.data_ptr(), rows, cols, _stream(x))
+    return q, scale
+
+
+def quantize_rows_e4m3(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-row e4m3 quantization of a bf16 weight (load time): (q (rows, cols) e4m3, scale (rows,) float32)."""
+    _require(x.is_contiguous() and x.dtype == torch.bfloat16, "quantize_rows_e4m3 takes contiguous bf16")
+    rows, cols = x.shape
+    q = torch.empty(rows, cols, dtype=torch.float8_e4m3fn, device=x.device)
+    scale = torch.empty(rows, dtype=torch.float32, device=x.device)
+    call("kd_quantize_rows_e4m3", x.data_ptr(), rows, cols, q.data_ptr(), scale.data_ptr(), _stream(x))
+    return q, scale
+
+
+def rope_table(inv_freq: torch.Tensor, positions: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """(cos, sin) float32 tables (positions, rot), bf16-rounded values; inv_freq float32 (rot / 2,) on the device."""
+    _require(inv_freq.dtype == torch.float32 and inv_freq.is_contiguous(), "inv_freq: contiguous float32")
+    rot = 2 * inv_freq.numel()
+    cos = torch.empty(positions, rot, dtype=torch.float32, device=inv_freq.device)
+    sin = torch.empty_like(cos)
+    call("kd_rope_table", inv_freq.data_ptr(), rot, positions, cos.data_ptr(), sin.data_ptr(), _stream(inv_freq))
+    return cos, sin
+
+
+def qkv_norm_rope(qkv: torch.Tensor, seqpos: torch.Tensor, heads: int, kv_heads: int, head_dim: int, gated: bool,
+                  q_norm: torch.Tensor | None, k_norm: torch.Tensor | None, qk_mode: int, v_mode: int, eps: float,
+                  cos: torch.Tensor, sin: torch.Tensor, out: tuple | None = None) -> tuple:
+    """(q (T, Hq, hd), k (T, Hkv, hd), v (T, Hkv, hd), gate (T, Hq * hd) or None) from the fused QKV output."""
+    _rowmajor(qkv, "qkv")
+    _require(seqpos.dtype == torch.int64 and seqpos.is_contiguous(), "seqpos must be contiguous int64")
+    t = qkv.shape[0]
+    dev = qkv.device
+    if out is None:
+        q = torch.empty(t, heads, head_dim, dtype=torch.bfloat16, device=dev)
+        k = torch.empty(t, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
+        v = torch.empty(t, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
+        gate = torch.empty(t, heads * head_dim, dtype=torch.bfloat16, device=dev) if gated else None
+    else:
+        q, k, v, gate = out
+    rot = cos.shape[1]
+    call("kd_qkv_norm_rope", qkv.data_ptr(), qkv.stride(0), t, seqpos.data_ptr(), heads, kv_heads, head_dim,
+         int(gated), _ptr(q_norm), _ptr(k_norm), qk_mode, v_mode, float(eps), cos.data_ptr(), sin.data_ptr(), rot,
+         q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(gate), _stream(qkv))
+    return q, k, v, gate
+
+
+def attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: torch.Tensor, cu_k: torch.Tensor,
+                     max_q: int, scale: float, window: tuple[int, int], gate: torch.Tensor | None = None,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """Varlen attention (the reference's varlen contract, end-aligned window); q (Tq, Hq, d), k/v (Tk, Hkv, d),
+    int32 boundaries on the device; returns (Tq, Hq * d), gated by sigmoid(gate) when given."""
+    _require(q.dim() == 3 and k.dim() == 3 and v.dim() == 3, "q, k, v must be (rows, heads, head_dim)")
+    _require(q.stride(2) == 1 and k.stride(2) == 1 and v.stride(2) == 1, "head_dim must be contiguous")
+    _require(q.stride(1) == q.shape[2] and k.stride(1) == k.shape[2] and v.stride(1) == v.shape[2],
+             "heads must be packed within a row")
+    _require(cu_q.dtype == torch.int32 and cu_k.dtype == torch.int32, "boundaries must be int32")
+    tq, hq, d = q.shape
+    if out is None:
+        out = torch.empty(tq, hq * d, dtype=torch.bfloat16, device=q.device)
+    call("kd_attention_varlen", q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+         out.data_ptr(), out.stride(0), _ptr(gate), gate.stride(0) if gate is not None else 0, cu_q.data_ptr(),
+         cu_k.data_ptr(), cu_q.numel() - 1, int(max_q), tq, hq, k.shape[1], d, float(scale), int(window[0]),
+         int(window[1]), status_word(q.device).data_ptr(), _stream(q))
+    return out
+
+
+def marker_norm(h: torch.Tensor, markers: torch.Tensor, weight: torch.Tensor, mode: int, eps: float,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``norm(h[markers])`` (M, hidden)."""
+    _require(h.is_contiguous(), "h must be contiguous")
+    _require(markers.dtype == torch.int64 and markers.is_contiguous(), "markers must be contiguous int64")
+    m = markers.numel()
+    if out is None:
+        out = torch.empty(m, h.shape[1], dtype=torch.bfloat16, device=h.device)
+    call("kd_marker_norm", h.data_ptr(), h.shape[1], markers.data_ptr(), m, _ptr(weight), mode, float(eps),
+         out.data_ptr(), _stream(h))
+    return out
+
+
+def readout(hidden: torch.Tensor, weight: torch.Tensor, cap: float | None = None,
+            out: torch.Tensor | None = None) -> torch.Tensor:
+    """float32 ``hidden @ weight.T`` (weight float32 (codes, hidden)), soft-capped when ``cap``."""
+    _require(hidden.is_contiguous() and weight.is_contiguous() and weight.dtype == torch.float32,
+             "readout: contiguous hidden and float32 weight")
+    m, codes = hidden.shape[0], weight.shape[0]
+    if out is None:
+        out = torch.empty(m, codes, dtype=torch.float32, device=hidden.device)
+    call("kd_readout", hidden.data_ptr(), m, hidden.shape[1], weight.data_ptr(), codes, float(cap or 0.0),
+         out.data_ptr(), _stream(hidden))
+    return out

@@ -1,0 +1,355 @@
+"""The packed prefill forward on libkd_b200: a drop-in for the reference's ``families.qwen.Packed`` /
+``families.gemma.Packed`` (``model(pack) -> (M, hidden)``, final-normed hidden states at the markers in pack order)
+and its ``Readout``.
+
+Per layer, on the current CUDA stream (kernel names in parentheses):
+
+Qwen-shaped (families/qwen/packed.py:149-156)            Gemma-shaped (families/gemma/packed.py:262-265)
+  x = norm(h)                        (rmsnorm)            x = norm(h)                               (rmsnorm)
+  qkv = x W_qkv^T                    (gemm)               qkv = x W_qkv^T                           (gemm)
+  q, k, v, gate = qk-norm + RoPE     (qkv_norm_rope)      q, k, v = q/k norm + RoPE, v norm         (qkv_norm_rope)
+  o = attn(q, k, v) * sigmoid(gate)  (attention_varlen)   o = attn(q, k, v), sliding or global      (attention_varlen)
+  h += o W_o^T                       (gemm, residual)     h = h + norm(o W_o^T)                     (gemm, norm_add)
+  y = norm(h)                        (rmsnorm)            z = norm(h)                               (rmsnorm)
+  m = silu(y W_g^T) * (y W_u^T)      (gemm, swiglu)       m = gelu(z W_g^T) * (z W_u^T)             (gemm, geglu)
+  h += m W_d^T                       (gemm, residual)     h = (h + norm(m W_d^T)) * scalar          (gemm, norm_add)
+
+then ``norm(h[markers])`` (marker_norm). With ``fp8`` every projection is an e4m3 GEMM with per-output-row weight
+scales (quantized at load, serve/fp8.py:86-90) and per-token activation scales computed by the kernel that produces
+the activation (rmsnorm_e4m3), as serve/fp8.py and serve/qwen_fp8.py do.
+
+Weights are repacked once at load: q/k/v concatenated into one projection, gate and up interleaved in blocks of 128
+rows (the GEMM's fused activation epilogue reads one gate and one up block per 256-wide tile).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+import torch
+
+from . import ops
+from .synthetic import Spec
+
+#: Qwen's FP8 path keeps projections with fewer outputs in bf16 (serve/qwen_fp8.py:17).
+QWEN_FP8_MIN_FEATURES = 256
+GATE_BLOCK = 128
+
+
+def _tensor(x: Any, device: torch.device, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    if isinstance(x, np.ndarray):
+        x = torch.from_numpy(np.ascontiguousarray(x))
+    return x.detach().to(device=device, dtype=dtype).contiguous()
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """(2 * I_pad, K): blocks of 128 gate rows then the matching 128 up rows (I padded to a multiple of 128 with
+    zero rows, whose activation products are zero)."""
+    inter, k = gate.shape
+    pad = (-inter) % GATE_BLOCK
+    if pad:
+        gate = torch.cat([gate, gate.new_zeros(pad, k)])
+        up = torch.cat([up, up.new_zeros(pad, k)])
+    blocks = gate.shape[0] // GATE_BLOCK
+    return torch.stack([gate.view(blocks, GATE_BLOCK, k), up.view(blocks, GATE_BLOCK, k)], 1).reshape(-1, k)
+
+
+@dataclass
+class Projection:
+    """One projection's weight: bf16 (N, K), or e4m3 (N, K) with float32 per-row scales."""
+
+    weight: torch.Tensor
+    scale: torch.Tensor | None = None
+
+    @property
+    def fp8(self) -> bool:
+        return self.scale is not None
+
+    @staticmethod
+    def of(w: torch.Tensor, fp8: bool) -> Projection:
+        if not fp8:
+            return Projection(w)
+        q, s = ops.quantize_rows_e4m3(w)
+        return Projection(q, s)
+
+
+@dataclass
+class Layer:
+    kind: str  # "full_attention" or "sliding_attention"
+    input_norm: torch.Tensor
+    qkv: list[tuple[Projection, int, int]]  # (projection, first output column, width) into the qkv buffer
+    q_norm: torch.Tensor
+    k_norm: torch.Tensor
+    o: Projection
+    post_attention_norm: torch.Tensor
+    gate_up: Projection
+    down: Projection
+    pre_feedforward_norm: torch.Tensor | None = None
+    post_feedforward_norm: torch.Tensor | None = None
+    scalar: torch.Tensor | None = None
+
+
+class Workspace:
+    """Activation buffers for packs of up to ``capacity`` tokens (allocated once, reused by every layer and pack)."""
+
+    def __init__(self, spec: Spec, capacity: int, device: torch.device, fp8: bool, inter_pad: int) -> None:
+        t, h, hd = capacity, spec.hidden, spec.head_dim
+        bf = dict(dtype=torch.bfloat16, device=device)
+        self.capacity = capacity
+        self.h = torch.empty(t, h, **bf)
+        self.x = torch.empty(t, h, **bf)
+        self.qkv = torch.empty(t, spec.qkv_width, **bf)
+        self.q = torch.empty(t, spec.heads, hd, **bf)
+        self.k = torch.empty(t, spec.kv_heads, hd, **bf)
+        self.v = torch.empty(t, spec.kv_heads, hd, **bf)
+        self.gate = torch.empty(t, spec.heads * hd, **bf) if spec.family == "qwen" else None
+        self.o = torch.empty(t, spec.heads * hd, **bf)
+        self.a = torch.empty(t, h, **bf)
+        self.m = torch.empty(t, inter_pad, **bf)
+        if fp8:
+            width = max(h, spec.heads * hd, inter_pad)
+            self.xq = torch.empty(t * width, dtype=torch.float8_e4m3fn, device=device)
+            self.xs = torch.empty(t, dtype=torch.float32, device=device)
+
+    def e4m3(self, rows: int, cols: int) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.xq[: rows * cols].view(rows, cols), self.xs[:rows]
+
+
+class Packed(torch.nn.Module):
+    """The packed forward of a Qwen-shaped or Gemma-shaped decoder on libkd_b200 kernels (see the module docstring).
+
+    ``Packed(spec, weights, device)``: ``weights`` named as ``synthetic.numpy_weights`` (Transformers module names);
+    ``Packed.from_backbone(backbone, attention)`` takes a loaded Transformers backbone as the reference's
+    ``family.Packed(backbone, attention)`` does (decider.py:35)."""
+
+    def __init__(self, spec: Spec, weights: dict[str, Any], device: torch.device | str = "cuda",
+                 attention: str = "causal", fp8: bool = False) -> None:
+        super().__init__()
+        if attention != "causal":
+            raise NotImplementedError("the B200 path runs causal checkpoints (decision_config attention = causal); "
+                                      "bidirectional attention with the marker-only last layer is not built yet")
+        if spec.head_dim not in (64, 128, 256):
+            raise ValueError(f"head_dim {spec.head_dim} is not one of the kernels' 64, 128, 256")
+        self.spec = spec
+        self.device = torch.device(device)
+        self.attention_mode = attention
+        self.fp8 = fp8
+        self.family = spec.family
+        self.types = spec.layer_types()
+        self.window = spec.window
+        dev = self.device
+        s = spec
+        self.inter_pad = s.intermediate + (-s.intermediate) % GATE_BLOCK
+        self.embed_tokens = _tensor(weights["embed_tokens"], dev)
+        self.norm = _tensor(weights["norm"], dev)
+        self.layers: list[Layer] = []
+        norm_w = (lambda key: _tensor(weights[key], dev))
+        for i in range(s.layers):
+            p = f"layers.{i}."
+            wq, wk, wv = (_tensor(weights[p + n], dev) for n in ("q_proj", "k_proj", "v_proj"))
+            qkv: list[tuple[Projection, int, int]] = []
+            if fp8 and s.family == "qwen" and min(wk.shape[0], wv.shape[0]) < QWEN_FP8_MIN_FEATURES:
+                # Qwen keeps narrow projections in bf16: q on its own, k and v together.
+                qkv.append((Projection.of(wq, wq.shape[0] >= QWEN_FP8_MIN_FEATURES), 0, wq.shape[0]))
+                qkv.append((Projection.of(torch.cat([wk, wv]), False), wq.shape[0], wk.shape[0] + wv.shape[0]))
+            else:
+                qkv.append((Projection.of(torch.cat([wq, wk, wv]), fp8), 0, s.qkv_width))
+            gate_up = interleave_gate_up(_tensor(weights[p + "gate_proj"], dev), _tensor(weights[p + "up_proj"], dev))
+            down = _tensor(weights[p + "down_proj"], dev)
+            if self.inter_pad != s.intermediate:
+                down = torch.cat([down, down.new_zeros(down.shape[0], self.inter_pad - s.intermediate)], 1)
+            layer = Layer(kind=self.types[i], input_norm=norm_w(p + "input_layernorm"), qkv=qkv,
+                          q_norm=norm_w(p + "q_norm"), k_norm=norm_w(p + "k_norm"),
+                          o=Projection.of(_tensor(weights[p + "o_proj"], dev), fp8),
+                          post_attention_norm=norm_w(p + "post_attention_layernorm"),
+                          gate_up=Projection.of(gate_up.contiguous(), fp8), down=Projection.of(down.contiguous(), fp8))
+            if s.family == "gemma":
+                layer.pre_feedforward_norm = norm_w(p + "pre_feedforward_layernorm")
+                layer.post_feedforward_norm = norm_w(p + "post_feedforward_layernorm")
+                layer.scalar = _tensor(np.asarray(weights[p + "layer_scalar"]).reshape(1)
+                                       if not isinstance(weights[p + "layer_scalar"], torch.Tensor)
+                                       else weights[p + "layer_scalar"].reshape(1), dev)
+            self.layers.append(layer)
+        self._inv_freq = {kind: self._inv_freq_of(kind) for kind in set(self.types)}
+        self._tables: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+        self._workspace: Workspace | None = None
+
+    # ---------------------------------------------------------------- construction from a Transformers backbone
+
+    @classmethod
+    def from_backbone(cls, backbone: Any, attention: str = "causal", fp8: bool = False) -> Packed:
+        """From a Transformers ``Qwen3_5Model`` (full-attention layers) or a Gemma 4 text model, as the reference's
+        ``family.Packed(backbone, attention)``; the weights are copied into the kernels' layouts."""
+        lm = getattr(backbone, "language_model", backbone)
+        config = lm.config
+        model_type = getattr(config, "model_type", "")
+        family = "gemma" if "gemma" in model_type else "qwen"
+        weights: dict[str, Any] = {"embed_tokens": lm.embed_tokens.weight, "norm": lm.norm.weight}
+        kinds = []
+        for i, layer in enumerate(lm.layers):
+            p = f"layers.{i}."
+            kind = getattr(layer, "layer_type", getattr(layer, "block_type", "full_attention"))
+            if family == "qwen" and kind != "full_attention":
+                raise NotImplementedError("Gated DeltaNet (linear-attention) layers are not built on the B200 path")
+            kinds.append(kind)
+            a = layer.self_attn
+            for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
+                if getattr(a, name, None) is None:
+                    raise NotImplementedError("layers whose keys and values share one projection are not built")
+                weights[p + name] = getattr(a, name).weight
+            weights[p + "q_norm"] = a.q_norm.weight
+            weights[p + "k_norm"] = a.k_norm.weight
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                weights[p + name] = getattr(layer.mlp, name).weight
+            weights[p + "input_layernorm"] = layer.input_layernorm.weight
+            weights[p + "post_attention_layernorm"] = layer.post_attention_layernorm.weight
+            if family == "gemma":
+                weights[p + "pre_feedforward_layernorm"] = layer.pre_feedforward_layernorm.weight
+                weights[p + "post_feedforward_layernorm"] = layer.post_feedforward_layernorm.weight
+                weights[p + "layer_scalar"] = layer.layer_scalar
+        heads, kv_heads = config.num_attention_heads, config.num_key_value_heads
+        head_dim = getattr(config, "head_dim", None) or config.hidden_size // heads
+        if family == "qwen":
+            rope = config.rope_parameters
+            spec = Spec("qwen", len(lm.layers), config.hidden_size, heads, kv_heads, head_dim,
+                        config.intermediate_size, config.vocab_size, eps=config.rms_norm_eps,
+                        rope_theta=rope["rope_theta"], partial_rotary=rope.get("partial_rotary_factor", 1.0))
+        else:
+            rope = config.rope_parameters
+            every = 6
+            spec = Spec("gemma", len(lm.layers), config.hidden_size, heads, kv_heads, head_dim,
+                        config.intermediate_size, config.vocab_size, eps=config.rms_norm_eps,
+                        rope_theta=rope["full_attention"]["rope_theta"],
+                        rope_theta_local=rope["sliding_attention"]["rope_theta"], window=config.sliding_window,
+                        global_every=every, logit_cap=config.final_logit_softcapping)
+            if kinds != spec.layer_types():
+                raise NotImplementedError(f"layer pattern {kinds} is not 5 sliding : 1 global")
+        device = next(lm.parameters()).device
+        if device.type != "cuda":
+            device = torch.device("cuda")
+        return cls(spec, weights, device, attention, fp8)
+
+    # ---------------------------------------------------------------- rotary tables
+
+    def _inv_freq_of(self, kind: str) -> torch.Tensor:
+        """Transformers' default inv_freq (computed in float32 on the host, as the backbone's rotary module does)."""
+        s = self.spec
+        if s.family == "qwen":
+            theta, rot = s.rope_theta, int(s.head_dim * s.partial_rotary)
+        else:
+            theta = s.rope_theta if kind == "full_attention" else s.rope_theta_local
+            rot = s.head_dim
+        inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
+        return inv.to(self.device)
+
+    def tables(self, kind: str, positions: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """cos/sin tables covering positions [0, positions) (grown in powers of two)."""
+        have = self._tables.get(kind)
+        if have is None or have[0].shape[0] < positions:
+            size = 1 << max(10, math.ceil(math.log2(max(positions, 1))))
+            self._tables[kind] = ops.rope_table(self._inv_freq[kind], size)
+        return self._tables[kind]
+
+    def workspace(self, tokens: int) -> Workspace:
+        if self._workspace is None or self._workspace.capacity < tokens:
+            self._workspace = None
+            self._workspace = Workspace(self.spec, tokens, self.device, self.fp8, self.inter_pad)
+        return self._workspace
+
+    # ---------------------------------------------------------------- forward
+
+    def _project(self, proj: Projection, x: torch.Tensor, x8: tuple | None, out: torch.Tensor,
+                 epilogue: int = ops.EPI_STORE, residual: torch.Tensor | None = None) -> torch.Tensor:
+        if proj.fp8:
+            return ops.gemm_fp8(x8[0], x8[1], proj.weight, proj.scale, out=out, epilogue=epilogue, residual=residual)
+        return ops.gemm(x, proj.weight, out=out, epilogue=epilogue, residual=residual)
+
+    def _quantized(self, ws: Workspace, x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        q, s = ws.e4m3(x.shape[0], x.shape[1])
+        return ops.rmsnorm_e4m3(x, None, -1, 0.0, q=q, scale=s)
+
+    def _normed(self, ws: Workspace, h: torch.Tensor, weight: torch.Tensor, mode: int, want_bf16: bool,
+                want_fp8: bool) -> tuple[torch.Tensor | None, tuple | None]:
+        """norm(h) as bf16 and/or as its e4m3 quantization (one fused kernel for the latter)."""
+        t = h.shape[0]
+        x = ops.rmsnorm(h, weight, mode, self.spec.eps, out=ws.x[:t]) if want_bf16 else None
+        x8 = None
+        if want_fp8:
+            q, s = ws.e4m3(t, h.shape[1])
+            x8 = ops.rmsnorm_e4m3(h, weight, mode, self.spec.eps, q=q, scale=s)
+        return x, x8
+
+    def forward(self, p: Any) -> torch.Tensor:
+        """(M, hidden) final-normalized hidden states at the markers, in pack order."""
+        s = self.spec
+        if p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
+            raise NotImplementedError("branched block layouts (a shared block and branches) are not built yet")
+        t = int(p.input_ids.numel())
+        ws = self.workspace(t)
+        n_seqs = int(p.cu.numel()) - 1
+        max_len = int(p.max_length)
+        qwen = s.family == "qwen"
+        mode = ops.NORM_ONE_PLUS if qwen else ops.NORM_WEIGHT
+        eps = s.eps
+        h = ops.embed(p.input_ids, self.embed_tokens, 0.0 if qwen else math.sqrt(s.hidden), out=ws.h[:t])
+        seqpos = p.seqpos if p.seqpos.dtype == torch.int64 else p.seqpos.long()
+        positions = int(max_len)
+        if p.segment_ids_cpu is not None:  # block layouts carry their own positions
+            positions = max(positions, int(seqpos.max().item()) + 1)
+        for layer in self.layers:
+            fp8_qkv = any(proj.fp8 for proj, _, _ in layer.qkv)
+            bf16_qkv = any(not proj.fp8 for proj, _, _ in layer.qkv)
+            x, x8 = self._normed(ws, h, layer.input_norm, mode, bf16_qkv, fp8_qkv)
+            qkv = ws.qkv[:t]
+            for proj, col, width in layer.qkv:
+                self._project(proj, x, x8, qkv[:, col:col + width] if width != qkv.shape[1] else qkv)
+            cos, sin = self.tables(layer.kind, positions)
+            q, k, v, gate = ops.qkv_norm_rope(
+                qkv, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm, mode,
+                -1 if qwen else ops.NORM_NONE, eps, cos, sin,
+                out=(ws.q[:t], ws.k[:t], ws.v[:t], ws.gate[:t] if qwen else None))
+            if layer.kind == "sliding_attention":
+                window = (self.window - 1, 0)
+            else:
+                window = (-1, 0)
+            scale = s.head_dim ** -0.5 if qwen else 1.0
+            o = ops.attention_varlen(q, k, v, p.cu, p.cu, max_len, scale, window, gate=gate, out=ws.o[:t])
+            o8 = self._quantized(ws, o) if layer.o.fp8 else None
+            if qwen:
+                self._project(layer.o, o, o8, h, ops.EPI_RESIDUAL, residual=h)  # h += o W_o^T
+                y, y8 = self._normed(ws, h, layer.post_attention_norm, mode, not layer.gate_up.fp8,
+                                     layer.gate_up.fp8)
+                m = self._project(layer.gate_up, y, y8, ws.m[:t], ops.EPI_SWIGLU)
+                m8 = self._quantized(ws, m) if layer.down.fp8 else None
+                self._project(layer.down, m, m8, h, ops.EPI_RESIDUAL, residual=h)  # h += m W_d^T
+            else:
+                a = self._project(layer.o, o, o8, ws.a[:t])
+                ops.norm_add(h, a, layer.post_attention_norm, mode, eps, out=h)  # h = h + norm(a)
+                z, z8 = self._normed(ws, h, layer.pre_feedforward_norm, mode, not layer.gate_up.fp8,
+                                     layer.gate_up.fp8)
+                m = self._project(layer.gate_up, z, z8, ws.m[:t], ops.EPI_GEGLU)
+                m8 = self._quantized(ws, m) if layer.down.fp8 else None
+                d = self._project(layer.down, m, m8, ws.a[:t])
+                ops.norm_add(h, d, layer.post_feedforward_norm, mode, eps, scalar=layer.scalar, out=h)
+        return ops.marker_norm(h, p.markers, self.norm, mode, eps)
+
+
+class Readout(torch.nn.Module):
+    """``hidden @ weight.T`` in float32, soft-capped as ``cap * tanh(logits / cap)`` when ``cap`` is set: the
+    reference's ``Readout`` (model/readout.py:12-33) on the readout kernel."""
+
+    def __init__(self, weight: Any, cap: float | None = None, device: torch.device | str = "cuda") -> None:
+        super().__init__()
+        self.weight = _tensor(weight, torch.device(device), torch.float32)
+        self.cap = cap
+
+    @classmethod
+    def from_reference(cls, head: Any) -> Readout:
+        """From the reference's ``Readout`` module (its rows and cap)."""
+        return cls(head.weight.detach().float(), head.cap, head.weight.device if head.weight.is_cuda else "cuda")
+
+    def forward(self, hidden: torch.Tensor) -> torch.Tensor:
+        return ops.readout(hidden.contiguous(), self.weight, self.cap)

@@ -95,9 +95,14 @@ def numpy_weights(spec: Spec, seed: int = 0, std: float = 0.02) -> dict[str, np.
     def normal(*shape, scale=std):
         return _bf16_exact(rng.standard_normal(shape, dtype=np.float32) * np.float32(scale))
 
-    def norm_weight(n):
+    def norm_weight(n, base=1.0):
         w = rng.standard_normal(n, dtype=np.float32) * np.float32(0.1)
-        return _bf16_exact(w if spec.family == "qwen" else 1.0 + w)
+        return _bf16_exact(w if spec.family == "qwen" else base * (1.0 + w))
+
+    # Gemma's attention has scale 1.0 over q/k normalized to unit RMS: with identity-like q/k norm weights a random
+    # model's logits have std sqrt(head_dim) and its softmax is one-hot, chaotic under any rounding. Trained
+    # checkpoints learn small q/k norm weights; the synthetic ones are scaled to head_dim^-1/4 (logit std ~ 1).
+    qk_base = spec.head_dim ** -0.25 if spec.family == "gemma" else 1.0
 
     w: dict[str, np.ndarray] = {"embed_tokens": normal(spec.vocab, h)}
     for i in range(spec.layers):
@@ -106,8 +111,8 @@ def numpy_weights(spec: Spec, seed: int = 0, std: float = 0.02) -> dict[str, np.
         w[p + "q_proj"] = normal(spec.q_width, h)
         w[p + "k_proj"] = normal(hkv * hd, h)
         w[p + "v_proj"] = normal(hkv * hd, h)
-        w[p + "q_norm"] = norm_weight(hd)
-        w[p + "k_norm"] = norm_weight(hd)
+        w[p + "q_norm"] = norm_weight(hd, qk_base)
+        w[p + "k_norm"] = norm_weight(hd, qk_base)
         w[p + "o_proj"] = normal(h, hq * hd)
         w[p + "post_attention_layernorm"] = norm_weight(h)
         w[p + "gate_proj"] = normal(inter, h)
@@ -131,9 +136,11 @@ def device_weights(spec: Spec, seed: int, device: torch.device, std: float = 0.0
     def normal(*shape, scale=std):
         return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * scale).bfloat16()
 
-    def norm_weight(n):
+    def norm_weight(n, base=1.0):
         w = torch.randn(n, generator=gen, device=device, dtype=torch.float32) * 0.1
-        return (w if spec.family == "qwen" else 1.0 + w).bfloat16()
+        return (w if spec.family == "qwen" else base * (1.0 + w)).bfloat16()
+
+    qk_base = spec.head_dim ** -0.25 if spec.family == "gemma" else 1.0
 
     w: dict[str, torch.Tensor] = {"embed_tokens": normal(spec.vocab, h)}
     for i in range(spec.layers):
@@ -142,8 +149,8 @@ def device_weights(spec: Spec, seed: int, device: torch.device, std: float = 0.0
         w[p + "q_proj"] = normal(spec.q_width, h)
         w[p + "k_proj"] = normal(hkv * hd, h)
         w[p + "v_proj"] = normal(hkv * hd, h)
-        w[p + "q_norm"] = norm_weight(hd)
-        w[p + "k_norm"] = norm_weight(hd)
+        w[p + "q_norm"] = norm_weight(hd, qk_base)
+        w[p + "k_norm"] = norm_weight(hd, qk_base)
         w[p + "o_proj"] = normal(h, hq * hd)
         w[p + "post_attention_layernorm"] = norm_weight(h)
         w[p + "gate_proj"] = normal(inter, h)

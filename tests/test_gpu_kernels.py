@@ -1,0 +1,271 @@
+"""Each libkd_b200 kernel on the GPU against a float32 reference of the same op: the numpy oracle (oracle/) for the
+reference's pointwise and attention math, plain float32 matmuls for the GEMMs. Inputs are seeded; sizes cover
+partial tiles, ragged sequences, GQA ratios and every head size the kernels take."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from karpo_decision_b200 import ops
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def bf16(x: np.ndarray) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(x, dtype=np.float32)).to(DEV).bfloat16()
+
+
+def rng(seed=0):
+    return np.random.default_rng(seed)
+
+
+# ------------------------------------------------------------------------------------------------ GEMM
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (128, 256, 64), (300, 768, 256), (1000, 1024, 1024),
+                                   (513, 6144, 1024), (77, 96, 200), (4096, 2560, 2560)])
+def test_gemm_bf16_matches_fp32(m, n, k):
+    g = rng(m + n + k)
+    a = bf16(g.standard_normal((m, k)))
+    w = bf16(g.standard_normal((n, k)) * 0.05)
+    got = ops.gemm(a, w).float()
+    want = a.float() @ w.float().T
+    torch.cuda.synchronize()
+    # fp32 accumulation in another order, one bf16 rounding of the output
+    assert (got - want).abs().max().item() <= 2 ** -8 * want.abs().max().item() + 1e-3
+    ops.check_status(DEV)
+
+
+def test_gemm_residual_epilogue_in_place():
+    g = rng(1)
+    a, w = bf16(g.standard_normal((700, 512))), bf16(g.standard_normal((1024, 512)) * 0.05)
+    h = bf16(g.standard_normal((700, 1024)))
+    want = h.float() + (a.float() @ w.float().T).bfloat16().float()
+    ops.gemm(a, w, out=h, epilogue=ops.EPI_RESIDUAL, residual=h)
+    assert (h.float() - want).abs().max().item() <= 2 ** -7 * want.abs().max().item()
+
+
+@pytest.mark.parametrize("epilogue", [ops.EPI_SWIGLU, ops.EPI_GEGLU])
+def test_gemm_gated_epilogues(epilogue):
+    from karpo_decision_b200.packed import interleave_gate_up
+
+    g = rng(2)
+    m, k, inter = 333, 256, 384
+    a = bf16(g.standard_normal((m, k)))
+    gate, up = bf16(g.standard_normal((inter, k)) * 0.1), bf16(g.standard_normal((inter, k)) * 0.1)
+    got = ops.gemm(a, interleave_gate_up(gate, up).contiguous(), epilogue=epilogue).float()
+    gf = (a.float() @ gate.float().T).bfloat16().float()
+    uf = (a.float() @ up.float().T).bfloat16().float()
+    act = torch.nn.functional.silu(gf) if epilogue == ops.EPI_SWIGLU else \
+        torch.nn.functional.gelu(gf, approximate="tanh")
+    want = act * uf
+    assert got.shape == (m, inter)
+    assert (got - want).abs().max().item() <= 2 ** -7 * want.abs().max().item() + 1e-3
+
+
+def test_gemm_fp8_matches_dequantized_product():
+    g = rng(3)
+    m, n, k = 517, 1024, 768
+    a = bf16(g.standard_normal((m, k)))
+    w = bf16(g.standard_normal((n, k)) * 0.05)
+    qa, sa = ops.quantize_rows_e4m3(a)
+    qw, sw = ops.quantize_rows_e4m3(w)
+    got = ops.gemm_fp8(qa, sa, qw, sw).float()
+    want = (qa.float() @ qw.float().T) * sa[:, None] * sw[None, :]
+    assert (got - want).abs().max().item() <= 2 ** -8 * want.abs().max().item() + 1e-3
+
+
+def test_quantize_rows_e4m3_bit_exact():
+    """The per-row e4m3 quantization of serve/fp8.py:21-24, bit for bit (same bf16 input, same float32 math)."""
+    g = rng(4)
+    x = bf16(g.standard_normal((257, 1024)) * 3)
+    q, s = ops.quantize_rows_e4m3(x)
+    scale = x.float().abs().amax(-1, keepdim=True).clamp(min=1e-12) / 448.0  # torch CUDA: times float(1/448)
+    ref = (x.float() / scale).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(s, scale[:, 0])
+    assert torch.equal(q.view(torch.uint8), ref.view(torch.uint8))
+
+
+# ------------------------------------------------------------------------------------------------ pointwise
+
+
+@pytest.mark.parametrize("mode,one_plus", [(ops.NORM_ONE_PLUS, True), (ops.NORM_WEIGHT, False)])
+def test_rmsnorm_matches_oracle(mode, one_plus):
+    g = rng(5)
+    x = g.standard_normal((301, 1024)).astype(np.float32)
+    w = g.standard_normal(1024).astype(np.float32) * 0.1 + (0.0 if one_plus else 1.0)
+    xb, wb = bf16(x), bf16(w)
+    got = ops.rmsnorm(xb, wb, mode, 1e-6).float().cpu().numpy()
+    want = oracle.rms_norm(xb.float().cpu().numpy(), wb.float().cpu().numpy(), 1e-6, one_plus)
+    assert np.abs(got - want).max() <= 2 ** -8 * np.abs(want).max()
+
+
+def test_add_rmsnorm_and_norm_add():
+    g = rng(6)
+    h = bf16(g.standard_normal((64, 512)))
+    x = bf16(g.standard_normal((64, 512)))
+    w = bf16(g.standard_normal(512) * 0.1)
+    hn, xn, wn = (t.float().cpu().numpy() for t in (h, x, w))
+    h2 = h.clone()
+    y = ops.add_rmsnorm(h2, x, w, ops.NORM_ONE_PLUS, 1e-6)
+    s = oracle.bf16(hn + xn)
+    assert np.array_equal(h2.float().cpu().numpy(), s)
+    assert np.abs(y.float().cpu().numpy() - oracle.rms_norm(s, wn, 1e-6, True)).max() <= 2 ** -8 * 4
+    w1 = bf16(1.0 + g.standard_normal(512) * 0.1)
+    out = ops.norm_add(h, x, w1, ops.NORM_WEIGHT, 1e-6)
+    want = hn + oracle.rms_norm(xn, w1.float().cpu().numpy(), 1e-6, False)
+    assert np.abs(out.float().cpu().numpy() - want).max() <= 2 ** -7 * np.abs(want).max()
+    scalar = bf16(np.array([0.875]))
+    out = ops.norm_add(h, x, w1, ops.NORM_WEIGHT, 1e-6, scalar=scalar)
+    want = (hn + oracle.bf16(oracle.rms_norm(xn, w1.float().cpu().numpy(), 1e-6, False))) * 0.875
+    assert np.abs(out.float().cpu().numpy() - want).max() <= 2 ** -7 * np.abs(want).max()
+
+
+def test_rmsnorm_e4m3_equals_norm_then_quantize():
+    g = rng(7)
+    x = bf16(g.standard_normal((129, 768)))
+    w = bf16(1.0 + g.standard_normal(768) * 0.1)
+    y = ops.rmsnorm(x, w, ops.NORM_WEIGHT, 1e-6)
+    q1, s1 = ops.quantize_rows_e4m3(y)
+    q2, s2 = ops.rmsnorm_e4m3(x, w, ops.NORM_WEIGHT, 1e-6)
+    assert torch.equal(s1, s2) and torch.equal(q1.view(torch.uint8), q2.view(torch.uint8))
+
+
+def test_embed_and_scaled_embed():
+    g = rng(8)
+    table = bf16(g.standard_normal((1000, 256)) * 0.02)
+    ids = torch.from_numpy(g.integers(0, 1000, 777)).to(DEV)
+    assert torch.equal(ops.embed(ids, table), table[ids])
+    scaled = ops.embed(ids, table, math.sqrt(256))
+    want = table[ids] * torch.tensor(16.0).bfloat16()
+    assert torch.equal(scaled, want)
+
+
+def test_rope_table_matches_transformers_formula():
+    theta, rot, n = 1e6, 128, 5000
+    inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
+    cos, sin = ops.rope_table(inv.to(DEV), n)
+    freqs = torch.arange(n, dtype=torch.float32)[:, None] * inv[None, :]
+    emb = torch.cat([freqs, freqs], -1)
+    # cosf/sinf against the host's float32 cos/sin: equal after bf16 rounding except at rare rounding boundaries
+    diff = (cos.cpu() - emb.cos().bfloat16().float()).abs()
+    assert (diff > 0).float().mean().item() < 1e-3 and diff.max().item() <= 2 ** -8
+    diff = (sin.cpu() - emb.sin().bfloat16().float()).abs()
+    assert (diff > 0).float().mean().item() < 1e-3 and diff.max().item() <= 2 ** -8
+
+
+@pytest.mark.parametrize("family,hd,partial", [("qwen", 128, 1.0), ("qwen", 64, 0.5), ("gemma", 256, 1.0),
+                                               ("gemma", 128, 1.0)])
+def test_qkv_norm_rope_matches_oracle(family, hd, partial):
+    g = rng(9)
+    t, hq, hkv = 97, 4, 2
+    gated = family == "qwen"
+    width = hq * hd * (2 if gated else 1) + 2 * hkv * hd
+    qkv = bf16(g.standard_normal((t, width)))
+    seqpos = torch.from_numpy(np.concatenate([np.arange(40), np.arange(57)])).to(DEV)
+    one_plus = gated
+    qn = bf16(g.standard_normal(hd) * 0.1 + (0 if one_plus else 1))
+    kn = bf16(g.standard_normal(hd) * 0.1 + (0 if one_plus else 1))
+    mode = ops.NORM_ONE_PLUS if one_plus else ops.NORM_WEIGHT
+    rot = int(hd * partial)
+    inv = 1.0 / (1e6 ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
+    cos, sin = ops.rope_table(inv.to(DEV), 128)
+    q, k, v, gate = ops.qkv_norm_rope(qkv, seqpos, hq, hkv, hd, gated, qn, kn, mode, -1 if gated else ops.NORM_NONE,
+                                      1e-6, cos, sin)
+    # oracle
+    x = qkv.float().cpu().numpy()
+    pos = seqpos.cpu().numpy()
+    c, s_ = cos.cpu().numpy()[pos], sin.cpu().numpy()[pos]
+    qw = hq * hd * (2 if gated else 1)
+    qraw = x[:, :qw].reshape(t, hq, -1)
+    if gated:
+        qraw, graw = qraw[..., :hd], qraw[..., hd:].reshape(t, -1)
+    kraw = x[:, qw:qw + hkv * hd].reshape(t, hkv, hd)
+    vraw = x[:, qw + hkv * hd:].reshape(t, hkv, hd)
+    qnn, knn = qn.float().cpu().numpy(), kn.float().cpu().numpy()
+    rq = oracle.rms_norm(qraw, qnn, 1e-6, one_plus)
+    rk = oracle.rms_norm(kraw, knn, 1e-6, one_plus)
+    if gated:
+        rq, rk = oracle.bf16(rq), oracle.bf16(rk)
+    want_q = oracle.packed.apply_rope(rq, c, s_)
+    want_k = oracle.packed.apply_rope(rk, c, s_)
+    want_v = vraw if gated else oracle.rms_norm(vraw, None, 1e-6, False)
+    for got, want in ((q, want_q), (k, want_k), (v, want_v)):
+        assert np.abs(got.float().cpu().numpy() - want).max() <= 2 ** -7 * max(np.abs(want).max(), 1.0)
+    if gated:
+        assert np.array_equal(gate.float().cpu().numpy(), graw)
+
+
+# ------------------------------------------------------------------------------------------------ attention
+
+
+def attention_case(lengths, hq, hkv, hd, window, scale, gated=False, seed=10):
+    g = rng(seed)
+    t = sum(lengths)
+    q = bf16(g.standard_normal((t, hq, hd)))
+    k = bf16(g.standard_normal((t, hkv, hd)))
+    v = bf16(g.standard_normal((t, hkv, hd)))
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    cu_t = torch.from_numpy(cu).to(DEV)
+    gate = bf16(g.standard_normal((t, hq * hd))) if gated else None
+    got = ops.attention_varlen(q, k, v, cu_t, cu_t, max(lengths), scale, window, gate=gate)
+    want = oracle.attention_varlen(*(x.float().cpu().numpy() for x in (q, k, v)), cu, cu, scale, window)
+    want = oracle.bf16(want).reshape(t, hq * hd)
+    if gated:
+        gn = gate.float().cpu().numpy()
+        want = want * (1.0 / (1.0 + np.exp(-gn)))
+    return got.float().cpu().numpy(), want
+
+
+@pytest.mark.parametrize("lengths", [[1], [7, 130, 64, 1, 300], [513], [128, 128]])
+@pytest.mark.parametrize("hd,hq,hkv", [(128, 16, 8), (64, 4, 2), (256, 4, 1)])
+def test_attention_causal_matches_oracle(lengths, hd, hq, hkv):
+    got, want = attention_case(lengths, hq, hkv, hd, (-1, 0), hd ** -0.5)
+    # P is rounded to bf16 before the PV product (flash attention); outputs are O(1)
+    assert np.abs(got - want).max() <= 2e-2
+
+
+@pytest.mark.parametrize("window", [(15, 0), (63, 0), (-1, -1)])
+def test_attention_window_and_bidirectional(window):
+    got, want = attention_case([200, 17, 90], 4, 2, 128, window, 1.0)
+    assert np.abs(got - want).max() <= 3e-2
+
+
+def test_attention_output_gate():
+    got, want = attention_case([100, 60], 4, 2, 128, (-1, 0), 128 ** -0.5, gated=True)
+    assert np.abs(got - want).max() <= 2e-2
+
+
+def test_attention_sequences_do_not_see_each_other():
+    """A sequence's outputs are the same alone and packed with others (tests/gpu/test_packed_qwen.py:114-122)."""
+    g = rng(11)
+    lengths = [50, 90, 70]
+    t = sum(lengths)
+    q, k, v = (bf16(g.standard_normal((t, 4, 128))) for _ in range(3))
+    cu = torch.tensor([0, 50, 140, 210], dtype=torch.int32, device=DEV)
+    together = ops.attention_varlen(q, k, v, cu, cu, 90, 0.1, (-1, 0))
+    cu1 = torch.tensor([0, 90], dtype=torch.int32, device=DEV)
+    alone = ops.attention_varlen(q[50:140], k[50:140], v[50:140], cu1, cu1, 90, 0.1, (-1, 0))
+    assert torch.equal(together[50:140], alone)
+
+
+# ------------------------------------------------------------------------------------------------ head
+
+
+def test_marker_norm_and_readout():
+    g = rng(12)
+    h = bf16(g.standard_normal((500, 256)))
+    markers = torch.tensor([3, 99, 499, 0], device=DEV)
+    w = bf16(g.standard_normal(256) * 0.1)
+    out = ops.marker_norm(h, markers, w, ops.NORM_ONE_PLUS, 1e-6)
+    want = oracle.rms_norm(h.float().cpu().numpy()[[3, 99, 499, 0]], w.float().cpu().numpy(), 1e-6, True)
+    assert np.abs(out.float().cpu().numpy() - want).max() <= 2 ** -8 * np.abs(want).max()
+    head = torch.from_numpy(g.standard_normal((5, 256)).astype(np.float32) * 0.02).to(DEV)
+    for cap in (None, 30.0, 0.5):
+        logits = ops.readout(out, head, cap).cpu().numpy()
+        ref = oracle.readout(out.float().cpu().numpy(), head.cpu().numpy(), cap)
+        assert np.abs(logits - ref).max() <= 1e-5

@@ -1,0 +1,83 @@
+"""The whole packed forward and readout on the GPU against the reference's own outputs (golden fixtures from the
+reference's float32 CPU path, tests/golden/) and against the oracle run with bf16 rounding at the reference's bf16
+storage points, on the same seeded weights and packs.
+
+Bounds: readout logits within 2e-2 (max-abs) of the reference and the same top answer; the bf16
+noise floor of the reference itself (its bf16 path against its float32 path, from the oracle) is asserted beside it.
+FP8: a random deep model turns single e4m3 rounding flips into visible output changes, so the whole FP8 forward is
+compared by cosine like the reference's own tests (tests/gpu/test_cuda_qwen_fast.py:60-72), while each FP8 kernel is
+checked exactly in test_gpu_kernels.py."""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from golden_cases import load
+from karpo_decision_b200 import Packed, Readout, from_arrays
+
+pytestmark = pytest.mark.gpu
+DEV = torch.device("cuda")
+
+
+def run_b200(name):
+    spec, weights, arrays, expected = load(name)
+    fp8 = name.endswith("_fp8")
+    model = Packed(spec, weights, DEV, fp8=fp8)
+    head = Readout(weights["readout"], spec.logit_cap, DEV)
+    p = from_arrays(arrays, DEV)
+    hidden = model(p)
+    logits = head(hidden)
+    torch.cuda.synchronize()
+    return spec, weights, arrays, expected, hidden.float().cpu().numpy(), logits.cpu().numpy()
+
+
+@pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny"])
+def test_bf16_forward_matches_reference(name):
+    spec, weights, arrays, expected, hidden, logits = run_b200(name)
+    assert hidden.shape == expected["hidden"].shape
+    forward = oracle.qwen_forward if spec.family == "qwen" else oracle.gemma_forward
+    noise = forward(weights, spec.as_dict(), arrays, mode="bf16")
+    noise_logits = oracle.readout(noise, weights["readout"], spec.logit_cap)
+    floor = np.abs(noise_logits - expected["logits"]).max()
+    err = np.abs(logits - expected["logits"]).max()
+    print(f"{name}: readout max-abs vs reference {err:.3g} (reference bf16 noise floor {floor:.3g})")
+    assert err <= 2e-2
+    assert (logits.argmax(-1) == expected["logits"].argmax(-1)).mean() >= 0.999 or err <= floor * 2
+    cosine = (hidden * expected["hidden"]).sum(-1) / (np.linalg.norm(hidden, axis=-1) *
+                                                      np.linalg.norm(expected["hidden"], axis=-1))
+    assert cosine.min() > 0.995, cosine
+
+
+@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny"])
+def test_bf16_forward_tracks_bf16_oracle(name):
+    """Against the oracle with the reference's bf16 rounding points: closer than to the float32 reference."""
+    spec, weights, arrays, expected, hidden, logits = run_b200(name)
+    forward = oracle.qwen_forward if spec.family == "qwen" else oracle.gemma_forward
+    want = forward(weights, spec.as_dict(), arrays, mode="bf16")
+    rel = np.abs(hidden - want).max() / np.abs(want).max()
+    assert rel < 0.05, rel
+
+
+@pytest.mark.parametrize("name", ["qwen_tiny_fp8", "gemma_tiny_fp8"])
+def test_fp8_forward_tracks_reference_fp8(name):
+    spec, weights, arrays, expected, hidden, logits = run_b200(name)
+    a, b = hidden.ravel(), expected["hidden"].ravel()
+    cosine = float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+    print(f"{name}: cosine vs reference FP8 {cosine:.4f}")
+    assert cosine > 0.9
+
+
+def test_pack_composition_does_not_change_a_sequence():
+    """A sequence's readouts are the same alone and packed with others (tests/gpu/test_packed_qwen.py:114-122)."""
+    spec, weights, arrays, _ = load("qwen_tiny")
+    model = Packed(spec, weights, DEV)
+    full = model(from_arrays(arrays, DEV)).float()
+    cu, mcu = arrays["cu"], arrays["marker_cu"]
+    a, b = int(cu[2]), int(cu[3])
+    alone = {
+        "input_ids": arrays["input_ids"][a:b], "seqpos": arrays["seqpos"][a:b], "cu": np.array([0, b - a]),
+        "markers": arrays["markers"][mcu[2]:mcu[3]] - a, "marker_cu": np.array([0, mcu[3] - mcu[2]]),
+    }
+    one = model(from_arrays(alone, DEV)).float()
+    assert torch.allclose(full[mcu[2]:mcu[3]], one, atol=2e-2, rtol=2e-2)
