@@ -119,12 +119,14 @@ int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* s
  * i.e. the contract of torch varlen_attn / flash attention with end alignment (families/qwen/packed.py:123-124,
  * families/gemma/sliding_attention.py:183-191, the reference test contract tests/test_gemma_blocks.py:28-43).
  * q (Tq, Hq, hd), k/v (Tk, Hkv, hd) with row strides in elements; cu_q/cu_k int32 [num_seqs + 1] on the device
- * (read when the kernel runs). max_q bounds every Lq. When gate != NULL, out = bf16(bf16(o) * sigmoid(gate))
+ * (read when the kernel runs); q holds total_q rows and k/v total_k rows. max_q bounds every Lq. When gate != NULL,
+ * out = bf16(bf16(o) * sigmoid(gate))
  * (Qwen's output gate, families/qwen/fused.py:38-39). head_dim 64, 128 or 256. */
 int kd_attention_varlen(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* out,
                         int64_t ldo, const void* gate, int64_t ldg, const int32_t* cu_q, const int32_t* cu_k,
-                        int num_seqs, int max_q, int64_t total_q, int num_heads_q, int num_heads_kv, int head_dim,
-                        float scale, int window_left, int window_right, int* status, cudaStream_t stream);
+                        int num_seqs, int max_q, int64_t total_q, int64_t total_k, int num_heads_q,
+                        int num_heads_kv, int head_dim, float scale, int window_left, int window_right, int* status,
+                        cudaStream_t stream);
 
 /* The head: out[m, :] = norm(h[markers[m], :]) (final norm at the readout markers).
  * Replaces families/qwen/packed.py:173-176 and families/gemma/packed.py:297-303. */

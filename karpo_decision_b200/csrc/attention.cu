@@ -1,99 +1,85 @@
-// Varlen block-diagonal attention forward (GQA, causal / sliding window / bidirectional), flash-attention style:
-// one CTA per (query tile of one sequence, query head), K/V tiles streamed through a double-buffered shared-memory
-// ring with cp.async, S = Q K^T and O += P V on the tensor cores (warp-level bf16 MMA, fp32 accumulation), online
-// softmax in registers, optional fused output gate.
+// Varlen block-diagonal attention forward (GQA, causal / sliding window / bidirectional) on the 5th-generation tensor
+// cores: S = Q K^T and O += P V are tcgen05.mma with the scores S, the probabilities P and the output O in tensor
+// memory; Q, K and V tiles arrive by TMA (128-byte swizzle).
 //
 // Replaces torch varlen_attn / flash-attention calls: families/qwen/packed.py:123-124 (causal, scale hd^-0.5, GQA),
 // families/gemma/sliding_attention.py:183-191 (window (W-1, 0), scale 1.0) and the global layers' causal attention
 // (families/gemma/packed.py:196-220). The visibility rule is the varlen contract with end alignment (the reference's
 // tests/test_gemma_blocks.py:28-43): query i of a sequence sees key j iff
-//   i + (Lk - Lq) - left <= j <= i + (Lk - Lq) + right.
-// Sequence boundaries (cu_q, cu_k) are read from device memory when the kernel runs, so a captured graph serves any
-// pack composition of the same token count.
+//   i + (Lk - Lq) - left <= j <= i + (Lk - Lq) + right        (left/right < 0: unbounded).
+// Sequence boundaries are read from device memory when the kernel runs, so a captured graph serves any pack
+// composition with the same token count.
+//
+// One CTA per (128-query tile of one sequence, query head); 6 warps:
+//   warp 0      TMA producer: the Q tile once, then K and V tiles through a 2-stage ring;
+//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers, then O += P_j V_j with
+//               P_j read from TMEM (A operand) and V_j as an MN-major B operand from shared memory;
+//   warps 2..5  softmax, one query row per thread (its TMEM lane): scores -> masked, scaled, exp2 against a running
+//               maximum, bf16 probabilities stored back to TMEM. O is rescaled only when the row maximum grows by
+//               more than 2^8 (the exponent base stays stale otherwise, which is exact: O and the row sum share it);
+//               at the end they normalize O, apply the optional output gate and store bf16 rows.
 #include "common.cuh"
 #include "kd_internal.h"
 
 namespace kd {
-namespace attn {
+namespace fa {
 
-constexpr int BN = 64;  // keys per tile
+template <int HD>
+struct Cfg {
+  static constexpr int BM = 128;                    // query rows per CTA = TMEM lanes
+  static constexpr int BN = HD == 256 ? 64 : 128;   // keys per tile
+  static constexpr int CHUNKS = HD / 64;            // 128-byte swizzle chunks along the head dim
+  static constexpr int Q_CHUNK = BM * 128;          // bytes of one Q chunk (BM rows x 128 B)
+  static constexpr int KV_CHUNK = BN * 128;         // bytes of one K or V chunk
+  static constexpr int Q_BYTES = Q_CHUNK * CHUNKS;
+  static constexpr int KV_BYTES = KV_CHUNK * CHUNKS;
+  static constexpr int STAGES = 2;
+  static constexpr int SMEM = Q_BYTES + STAGES * 2 * KV_BYTES + 1024 + 256;
+  // Tensor-memory columns (fp32): O [0, HD), two score buffers of BN, two probability buffers of BN / 2 (bf16 pairs).
+  static constexpr int O_COL = 0;
+  static constexpr int S_COL = HD;
+  static constexpr int P_COL = HD + 2 * BN;
+  static constexpr int TMEM_COLS = 512;
+  static_assert(P_COL + BN <= TMEM_COLS, "tensor memory budget");
+};
 
 struct Args {
-  const __nv_bfloat16* q;
-  const __nv_bfloat16* k;
-  const __nv_bfloat16* v;
-  __nv_bfloat16* out;
   const __nv_bfloat16* gate;
-  int64_t ldq, ldk, ldv, ldo, ldg;
+  __nv_bfloat16* out;
+  int64_t ldo, ldg;
   const int32_t* cu_q;
   const int32_t* cu_k;
   int num_seqs;
   int hq, hkv;
   float scale_log2;  // softmax scale * log2(e)
   int left, right;
+  int* status;
 };
 
-KD_DEVICE void cp_async16(uint32_t dst, const void* src, bool valid) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0) : "memory");
-}
-KD_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-KD_DEVICE void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
+constexpr int THREADS = 192;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale O when the row maximum grows by more than 2^8
 
-KD_DEVICE void ldmatrix_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-KD_DEVICE void ldmatrix_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-
-KD_DEVICE void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%0, %1, %2, %3};"
-      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
-// Byte offset of 16-byte chunk `chunk` of row `row` in a [rows][HD] bf16 tile, chunks XOR-swizzled by row % 8 so that
-// the 8 rows an ldmatrix reads hit 8 different bank groups.
 template <int HD>
-KD_DEVICE uint32_t swz(int row, int chunk) {
-  return (uint32_t)(row * HD * 2 + ((chunk ^ (row & 7)) << 4));
-}
+__global__ void __launch_bounds__(THREADS, 1)
+    attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
+                     const __grid_constant__ CUtensorMap map_v, Args a) {
+  using C = Cfg<HD>;
+  constexpr int BM = C::BM, BN = C::BN;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* s_q = smem;
+  uint8_t* s_kv = smem + C::Q_BYTES;  // stage s: K at s * 2 * KV_BYTES, V right after
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::Q_BYTES + C::STAGES * 2 * C::KV_BYTES);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;                  // [STAGES]
+  uint64_t* v_full = k_full + C::STAGES;        // [STAGES]
+  uint64_t* kv_empty = v_full + C::STAGES;      // [STAGES]
+  uint64_t* s_full = kv_empty + C::STAGES;      // [2]
+  uint64_t* p_full = s_full + 2;                // [2]
+  uint64_t* pv_done = p_full + 2;               // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
 
-// Loads rows [r0, r0 + ROWS) of a [T, ld] bf16 matrix (head columns at `col`) into a swizzled tile; rows >= limit
-// are zero-filled.
-template <int HD, int ROWS, int THREADS>
-KD_DEVICE void load_tile(uint32_t smem, const __nv_bfloat16* base, int64_t ld, int r0, int limit) {
-  constexpr int CHUNKS = HD / 8;
-  for (int i = threadIdx.x; i < ROWS * CHUNKS; i += THREADS) {
-    const int row = i / CHUNKS;
-    const int chunk = i % CHUNKS;
-    const bool valid = r0 + row < limit;
-    const __nv_bfloat16* src = base + (int64_t)(valid ? r0 + row : 0) * ld + chunk * 8;
-    cp_async16(smem + swz<HD>(row, chunk), src, valid);
-  }
-}
-
-template <int HD, int BM>
-__global__ void __launch_bounds__(BM * 2, 1) attention_kernel(Args a) {
-  constexpr int WARPS = BM / 16;
-  constexpr int THREADS = WARPS * 32;
-  constexpr int DT = HD / 8;  // 8-wide output tiles along the head dim
-  constexpr int NT = BN / 8;  // 8-wide score tiles along the keys
-  extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t s_q = smem_u32(smem);
-  const uint32_t s_kv = s_q + BM * HD * 2;  // [stage][K | V], each BN x HD
-  constexpr uint32_t KV_TILE = BN * HD * 2;
-
-  // ---- find this CTA's (sequence, query tile): tiles are numbered sequence by sequence from the device bounds.
+  // ---- this CTA's (sequence, query tile), numbered sequence by sequence from the device bounds
   int tile = blockIdx.x;
   int seq = -1, qs = 0, lq = 0, lk = 0, q0 = 0, k0 = 0;
   for (int s = 0; s < a.num_seqs; ++s) {
@@ -105,227 +91,281 @@ __global__ void __launch_bounds__(BM * 2, 1) attention_kernel(Args a) {
       lq = qb - qa;
       k0 = a.cu_k[s];
       lk = a.cu_k[s + 1] - k0;
-      qs = (n - 1 - tile) * BM;  // the last (most expensive when causal) tiles first
+      qs = (n - 1 - tile) * BM;  // the last (most expensive when causal) tiles of a sequence first
       break;
     }
     tile -= n;
   }
-  if (seq < 0) return;
+  if (seq < 0) return;  // uniform across the CTA: nothing allocated yet
   const int head = blockIdx.y;
   const int kvh = head / (a.hq / a.hkv);
-  const int off = lk - lq;  // end alignment
+  const int off = lk - lq;  // end alignment of queries to keys
   const int qe = min(qs + BM, lq);
-
-  // Key range any query of this tile may see.
   int kmin = 0, kmax = lk - 1;
   if (a.left >= 0) kmin = max(0, qs + off - a.left);
   if (a.right >= 0) kmax = min(lk - 1, qe - 1 + off + a.right);
+  const int first_tile = kmin / BN;
+  const int n_tiles = kmax < kmin ? 0 : kmax / BN - first_tile + 1;
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
-  const int g = lane >> 2, t = lane & 3;
-
-  const __nv_bfloat16* qbase = a.q + (int64_t)q0 * a.ldq + (int64_t)head * HD;
-  const __nv_bfloat16* kbase = a.k + (int64_t)k0 * a.ldk + (int64_t)kvh * HD;
-  const __nv_bfloat16* vbase = a.v + (int64_t)k0 * a.ldv + (int64_t)kvh * HD;
-
-  float o[DT][4];
-#pragma unroll
-  for (int i = 0; i < DT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY};
-  float l_run[2] = {0.f, 0.f};
-
-  const int first_tile = kmax < kmin ? 1 : kmin / BN;
-  const int last_tile = kmax < kmin ? 0 : kmax / BN;
-
-  load_tile<HD, BM, THREADS>(s_q, qbase, a.ldq, qs, lq);
-  if (first_tile <= last_tile) {
-    load_tile<HD, BN, THREADS>(s_kv, kbase, a.ldk, first_tile * BN, lk);
-    load_tile<HD, BN, THREADS>(s_kv + KV_TILE, vbase, a.ldv, first_tile * BN, lk);
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&s_full[b], 1);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&pv_done[b], 1);
+    }
+    fence_barrier_init();
   }
-  cp_async_commit();
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
 
-  const int row_a = qs + warp * 16 + g;  // this thread's two query rows (within the sequence)
-  const int row_b = row_a + 8;
-
-  for (int kt = first_tile; kt <= last_tile; ++kt) {
-    const int stage = (kt - first_tile) & 1;
-    if (kt < last_tile) {  // prefetch the next K/V tile into the other stage
-      const uint32_t nxt = s_kv + (stage ^ 1) * 2 * KV_TILE;
-      load_tile<HD, BN, THREADS>(nxt, kbase, a.ldk, (kt + 1) * BN, lk);
-      load_tile<HD, BN, THREADS>(nxt + KV_TILE, vbase, a.ldv, (kt + 1) * BN, lk);
-    }
-    cp_async_commit();
-    cp_async_wait<1>();
-    __syncthreads();
-
-    const uint32_t sk = s_kv + stage * 2 * KV_TILE;
-    const uint32_t sv = sk + KV_TILE;
-
-    // ---- S = Q K^T for this warp's 16 rows x BN keys
-    float s[NT][4];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
-#pragma unroll
-    for (int kk = 0; kk < HD / 16; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      {
-        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = kk * 2 + (lane >> 4);
-        ldmatrix_x4(s_q + swz<HD>(r, c), a0, a1, a2, a3);
-      }
-#pragma unroll
-      for (int j = 0; j < NT; j += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int r = j * 8 + (lane & 7) + (lane >> 4) * 8;
-        const int c = kk * 2 + ((lane >> 3) & 1);
-        ldmatrix_x4(sk + swz<HD>(r, c), b0, b1, b2, b3);
-        mma_bf16(s[j], a0, a1, a2, a3, b0, b1);
-        mma_bf16(s[j + 1], a0, a1, a2, a3, b2, b3);
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (n_tiles > 0 && elect_one()) {
+      tma_prefetch_desc(&map_q);
+      tma_prefetch_desc(&map_k);
+      tma_prefetch_desc(&map_v);
+      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+      for (int c = 0; c < C::CHUNKS; ++c)
+        tma_load_2d(&map_q, q_full, s_q + c * C::Q_CHUNK, head * HD + c * 64, q0 + qs);
+      for (int j = 0; j < n_tiles; ++j) {
+        const int st = j % C::STAGES;
+        const uint32_t ph = (j / C::STAGES) & 1;
+        if (!mbar_wait(&kv_empty[st], ph ^ 1, a.status)) goto done;
+        const int row = k0 + (first_tile + j) * BN;
+        uint8_t* sk = s_kv + st * 2 * C::KV_BYTES;
+        uint8_t* sv = sk + C::KV_BYTES;
+        mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
+        for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(&map_k, &k_full[st], sk + c * C::KV_CHUNK, kvh * HD + c * 64, row);
+        mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
+        for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + c * 64, row);
       }
     }
-
-    // ---- mask (only tiles that cross a boundary), online softmax
-    const int n0 = kt * BN;
-    const bool edge = (n0 + BN - 1 > qs + off + (a.right >= 0 ? a.right : lk)) ||
-                      (a.left >= 0 && n0 < qe - 1 + off - a.left) || (n0 + BN > lk);
-    float mx[2] = {m_run[0], m_run[1]};
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (n_tiles > 0 && elect_one()) {
+      constexpr uint32_t idesc_s = mma_idesc(1, BM, BN);          // bf16, K-major A and B
+      constexpr uint32_t idesc_o = mma_idesc(1, BM, HD, 1);       // bf16, A from TMEM, MN-major B (V)
+      const uint32_t sq = smem_u32(s_q);
+      if (!mbar_wait(q_full, 0, a.status)) goto done;
+      auto issue_s = [&](int j) -> bool {
+        const int st = j % C::STAGES;
+        if (!mbar_wait(&k_full[st], (j / C::STAGES) & 1, a.status)) return false;
+        tc_fence_after();
+        const uint32_t sk = smem_u32(s_kv + st * 2 * C::KV_BYTES);
+        const uint32_t d = tmem + C::S_COL + (j & 1) * BN;
 #pragma unroll
-    for (int j = 0; j < NT; ++j) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float x = s[j][e] * a.scale_log2;
-        if (edge) {
-          const int key = n0 + j * 8 + 2 * t + (e & 1);
-          const int qi = (e < 2 ? row_a : row_b) + off;
-          bool ok = key < lk;
-          if (a.right >= 0) ok = ok && key <= qi + a.right;
-          if (a.left >= 0) ok = ok && key >= qi - a.left;
-          if (!ok) x = -INFINITY;
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const int c = kk / 4, w = (kk % 4) * 32;
+          mma_f16_ss(d, sw128_kmajor_desc(sq + c * C::Q_CHUNK + w), sw128_kmajor_desc(sk + c * C::KV_CHUNK + w),
+                     idesc_s, kk > 0);
         }
-        s[j][e] = x;
-        mx[e >> 1] = fmaxf(mx[e >> 1], x);
+        mma_commit(&s_full[j & 1]);
+        return true;
+      };
+      if (!issue_s(0)) goto done;
+      for (int j = 0; j < n_tiles; ++j) {
+        // S_{j+1} first, so the softmax of tile j+1 can start while P_j V_j runs. Its score buffer was last read
+        // by the softmax of tile j-1, which released it with p_full[(j-1) & 1] (waited for below, one step ago).
+        if (j + 1 < n_tiles && !issue_s(j + 1)) goto done;
+        const int st = j % C::STAGES;
+        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, a.status)) goto done;
+        if (!mbar_wait(&v_full[st], (j / C::STAGES) & 1, a.status)) goto done;
+        tc_fence_after();
+        const uint32_t sv = smem_u32(s_kv + st * 2 * C::KV_BYTES + C::KV_BYTES);
+        const uint32_t p = tmem + C::P_COL + (j & 1) * (BN / 2);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per instruction: 8 columns of bf16 pairs, 2 KB of V rows
+          mma_f16_ts(tmem + C::O_COL, p + kk * 8, sw128_mnmajor_desc(sv + kk * 2048, C::KV_CHUNK), idesc_o,
+                     (j | kk) != 0);
+        mma_commit(&kv_empty[st]);
+        mma_commit(&pv_done[j & 1]);
       }
     }
+  } else {
+    // ------------------------------------------------------------ softmax + epilogue (warps 2..5)
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
+    const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+    const int qi = qs + r + off;  // the row's position on the key axis
+    float m_used = -INFINITY, l_sum = 0.f;
+    for (int j = 0; j < n_tiles; ++j) {
+      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.status)) goto done;
+      tc_fence_after();
+      float sv[BN];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
-    }
-    float corr[2], base[2];
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t t[32];
+        tmem_ld32(lane_base + C::S_COL + (j & 1) * BN + c, t);
+        tmem_ld_wait_regs(t);
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      base[r] = mx[r] == -INFINITY ? 0.f : mx[r];  // a fully masked row so far keeps zeros
-      corr[r] = exp2f(m_run[r] - base[r]);
-      m_run[r] = mx[r];
-    }
-    float rs[2] = {0.f, 0.f};
-    uint32_t p[NT][2];
-#pragma unroll
-    for (int j = 0; j < NT; ++j) {
-      const float p0 = exp2f(s[j][0] - base[0]);
-      const float p1 = exp2f(s[j][1] - base[0]);
-      const float p2 = exp2f(s[j][2] - base[1]);
-      const float p3 = exp2f(s[j][3] - base[1]);
-      rs[0] += p0 + p1;
-      rs[1] += p2 + p3;
-      p[j][0] = pack_bf16x2(p0, p1);
-      p[j][1] = pack_bf16x2(p2, p3);
-    }
-#pragma unroll
-    for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * corr[r] + rs[r];
-#pragma unroll
-    for (int i = 0; i < DT; ++i) {
-      o[i][0] *= corr[0];
-      o[i][1] *= corr[0];
-      o[i][2] *= corr[1];
-      o[i][3] *= corr[1];
-    }
-
-    // ---- O += P V
-#pragma unroll
-    for (int kk = 0; kk < BN / 16; ++kk) {
-      const uint32_t a0 = p[2 * kk][0], a1 = p[2 * kk][1], a2 = p[2 * kk + 1][0], a3 = p[2 * kk + 1][1];
-#pragma unroll
-      for (int i = 0; i < DT; i += 2) {
-        uint32_t b0, b1, b2, b3;
-        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = i + (lane >> 4);
-        ldmatrix_x4_trans(sv + swz<HD>(r, c), b0, b1, b2, b3);
-        mma_bf16(o[i], a0, a1, a2, a3, b0, b1);
-        mma_bf16(o[i + 1], a0, a1, a2, a3, b2, b3);
+        for (int e = 0; e < 32; ++e) sv[c + e] = __uint_as_float(t[e]);
       }
+      const int n0 = (first_tile + j) * BN;
+      float mt = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) {
+        const int key = n0 + e;
+        bool ok = key < lk;
+        if (a.right >= 0) ok = ok && key <= qi + a.right;
+        if (a.left >= 0) ok = ok && key >= qi - a.left;
+        const float x = ok ? sv[e] * a.scale_log2 : -INFINITY;
+        sv[e] = x;
+        mt = fmaxf(mt, x);
+      }
+      const float m_new = fmaxf(m_used, mt);
+      const bool need = m_new > m_used + RESCALE_THRESHOLD || (m_used == -INFINITY && m_new != -INFINITY);
+      const float f = !need ? 1.f : (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new));
+      // tcgen05.ld/st are warp-collective: the warp rescales its O rows together (factor 1 where a row needs none).
+      if (j > 0 && __any_sync(0xffffffffu, need && m_used != -INFINITY)) {
+        // O holds P_{0..j-1} V: wait for the last product before rescaling it in place.
+        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status)) goto done;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < HD; c += 32) {
+          uint32_t t[32];
+          tmem_ld32(lane_base + C::O_COL + c, t);
+          tmem_ld_wait_regs(t);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) t[e] = __float_as_uint(__uint_as_float(t[e]) * f);
+          tmem_st32(lane_base + C::O_COL + c, t);
+        }
+        tmem_st_wait();
+      }
+      if (need) {
+        l_sum *= f;
+        m_used = m_new;
+      }
+      const float base = m_used == -INFINITY ? 0.f : m_used;
+      // P_j goes to probability buffer j & 1, last read by P_{j-2} V_{j-2}.
+      if (j >= 2 && !mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, a.status)) goto done;
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN; c += 64) {
+        uint32_t pk[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const float p0 = exp2f(sv[c + 2 * e] - base);
+          const float p1 = exp2f(sv[c + 2 * e + 1] - base);
+          rs += p0 + p1;
+          pk[e] = pack_bf16x2(p0, p1);
+        }
+        tmem_st32(lane_base + C::P_COL + (j & 1) * (BN / 2) + c / 2, pk);
+      }
+      l_sum += rs;
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[j & 1]);
     }
-    __syncthreads();  // this stage is overwritten by the prefetch two iterations on
-  }
-  cp_async_wait<0>();
-
-  // ---- normalize, gate, store
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
-    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
-  }
-  const float inv[2] = {l_run[0] > 0.f ? 1.f / l_run[0] : 0.f, l_run[1] > 0.f ? 1.f / l_run[1] : 0.f};
-#pragma unroll
-  for (int r = 0; r < 2; ++r) {
-    const int row = r == 0 ? row_a : row_b;
-    if (row >= lq) continue;
+    // ---- epilogue: O / l, optional gate, bf16 row
+    if (n_tiles > 0) {
+      if (!mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, a.status)) goto done;
+      tc_fence_after();
+    }
+    const int row = qs + r;
+    const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
     __nv_bfloat16* orow = a.out + (int64_t)(q0 + row) * a.ldo + (int64_t)head * HD;
     const __nv_bfloat16* grow = a.gate ? a.gate + (int64_t)(q0 + row) * a.ldg + (int64_t)head * HD : nullptr;
+#pragma unroll 1
+    for (int c = 0; c < HD; c += 32) {
+      uint32_t t[32];
+      if (n_tiles > 0) {
+        tmem_ld32(lane_base + C::O_COL + c, t);  // warp-collective: every lane loads, valid rows store
+        tmem_ld_wait_regs(t);
+      } else {
 #pragma unroll
-    for (int i = 0; i < DT; ++i) {
-      const int d = i * 8 + 2 * t;
-      float v0 = bf16_round(o[i][2 * r] * inv[r]);
-      float v1 = bf16_round(o[i][2 * r + 1] * inv[r]);
-      if (grow) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
-        const float2 gv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(grow + d));
-        v0 *= sigmoid(gv.x);
-        v1 *= sigmoid(gv.y);
+        for (int e = 0; e < 32; ++e) t[e] = 0u;
       }
-      *reinterpret_cast<uint32_t*>(orow + d) = pack_bf16x2(v0, v1);
+      if (row < lq) {
+        uint32_t packed[16];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float v0 = bf16_round(__uint_as_float(t[2 * e]) * inv);
+          float v1 = bf16_round(__uint_as_float(t[2 * e + 1]) * inv);
+          if (grow) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
+            const float2 gv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(grow + c + 2 * e));
+            v0 *= sigmoid(gv.x);
+            v1 *= sigmoid(gv.y);
+          }
+          packed[e] = pack_bf16x2(v0, v1);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+          *reinterpret_cast<uint4*>(orow + c + 8 * q4) =
+              make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+      }
     }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) {
+    __syncwarp();
+    tmem_dealloc(tmem, C::TMEM_COLS);
   }
 }
 
-template <int HD, int BM>
-int launch(const Args& a, int64_t total_q, int num_seqs, cudaStream_t stream) {
-  constexpr int SMEM = BM * HD * 2 + 2 * 2 * BN * HD * 2;
-  auto kernel = attention_kernel<HD, BM>;
+template <int HD>
+int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, int64_t tq, int64_t tk,
+           const Args& a, int64_t total_q, cudaStream_t stream) {
+  using C = Cfg<HD>;
+  CUtensorMap mq, mk, mv;
+  const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  int rc = make_tma_2d(&mq, q, dt, 2, (uint64_t)ldq, (uint64_t)tq, (uint64_t)ldq, 64, C::BM,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_tma_2d(&mk, k, dt, 2, (uint64_t)ldk, (uint64_t)tk, (uint64_t)ldk, 64, C::BN,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!rc) rc = make_tma_2d(&mv, v, dt, 2, (uint64_t)ldv, (uint64_t)tk, (uint64_t)ldv, 64, C::BN,
+                            CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  auto kernel = attention_kernel<HD>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return KD_ERR_ARGUMENT;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     if (e != cudaSuccess) return record_cuda_error(e, "attention: cudaFuncSetAttribute");
     configured[dev] = true;
   }
   // Upper bound on query tiles over all sequences: sum(ceil(Lq / BM)) <= total_q / BM + num_seqs.
-  const int64_t tiles = total_q / BM + num_seqs;
+  const int64_t tiles = total_q / C::BM + a.num_seqs;
   if (tiles > 0x7fffffff) return set_error(KD_ERR_ARGUMENT, "attention: too many query tiles");
   dim3 grid((unsigned)tiles, (unsigned)a.hq);
-  kernel<<<grid, BM * 2, SMEM, stream>>>(a);
+  kernel<<<grid, THREADS, C::SMEM, stream>>>(mq, mk, mv, a);
   return record_cuda_error(cudaGetLastError(), "attention: launch");
 }
 
-}  // namespace attn
+}  // namespace fa
 }  // namespace kd
 
 using namespace kd;
 
 extern "C" int kd_attention_varlen(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv,
                                    void* out, int64_t ldo, const void* gate, int64_t ldg, const int32_t* cu_q,
-                                   const int32_t* cu_k, int num_seqs, int max_q, int64_t total_q, int num_heads_q,
-                                   int num_heads_kv, int head_dim, float scale, int window_left, int window_right,
-                                   int* status, cudaStream_t stream) {
+                                   const int32_t* cu_k, int num_seqs, int max_q, int64_t total_q, int64_t total_k,
+                                   int num_heads_q, int num_heads_kv, int head_dim, float scale, int window_left,
+                                   int window_right, int* status, cudaStream_t stream) {
   (void)max_q;
-  (void)status;
-  if (num_seqs < 0 || total_q < 0) return set_error(KD_ERR_ARGUMENT, "attention: negative sizes");
+  if (num_seqs < 0 || total_q < 0 || total_k < 0) return set_error(KD_ERR_ARGUMENT, "attention: negative sizes");
   if (num_seqs == 0 || total_q == 0) return KD_OK;
   if (num_heads_q <= 0 || num_heads_kv <= 0 || num_heads_q % num_heads_kv)
     return set_error(KD_ERR_ARGUMENT, "attention: query heads must be a multiple of key/value heads");
-  if (!q || !k || !v || !out || !cu_q || !cu_k) return set_error(KD_ERR_ARGUMENT, "attention: null pointer");
+  if (!q || !k || !v || !out || !cu_q || !cu_k || !status) return set_error(KD_ERR_ARGUMENT, "attention: null pointer");
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!a16(q) || !a16(k) || !a16(v) || !a16(out) || (gate && !a16(gate)) || ldq % 8 || ldk % 8 || ldv % 8 ||
       ldo % 8 || (gate && ldg % 8))
@@ -333,15 +373,9 @@ extern "C" int kd_attention_varlen(const void* q, int64_t ldq, const void* k, in
   if (ldq < (int64_t)num_heads_q * head_dim || ldo < (int64_t)num_heads_q * head_dim ||
       ldk < (int64_t)num_heads_kv * head_dim || ldv < (int64_t)num_heads_kv * head_dim)
     return set_error(KD_ERR_ARGUMENT, "attention: row strides smaller than heads x head_dim");
-  attn::Args a;
-  a.q = static_cast<const __nv_bfloat16*>(q);
-  a.k = static_cast<const __nv_bfloat16*>(k);
-  a.v = static_cast<const __nv_bfloat16*>(v);
-  a.out = static_cast<__nv_bfloat16*>(out);
+  fa::Args a;
   a.gate = static_cast<const __nv_bfloat16*>(gate);
-  a.ldq = ldq;
-  a.ldk = ldk;
-  a.ldv = ldv;
+  a.out = static_cast<__nv_bfloat16*>(out);
   a.ldo = ldo;
   a.ldg = ldg;
   a.cu_q = cu_q;
@@ -352,13 +386,15 @@ extern "C" int kd_attention_varlen(const void* q, int64_t ldq, const void* k, in
   a.scale_log2 = scale * 1.4426950408889634f;
   a.left = window_left;
   a.right = window_right;
+  a.status = status;
+  const int64_t tk = total_k;
   switch (head_dim) {
     case 64:
-      return attn::launch<64, 128>(a, total_q, num_seqs, stream);
+      return fa::launch<64>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
     case 128:
-      return attn::launch<128, 128>(a, total_q, num_seqs, stream);
+      return fa::launch<128>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
     case 256:
-      return attn::launch<256, 64>(a, total_q, num_seqs, stream);
+      return fa::launch<256>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
     default:
       return set_error(KD_ERR_ARGUMENT, "attention: head_dim must be 64, 128 or 256");
   }

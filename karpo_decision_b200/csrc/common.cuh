@@ -134,10 +134,11 @@ KD_DEVICE uint64_t sw128_kmajor_desc(uint32_t addr) {
 
 // Instruction descriptor of a dense tcgen05.mma with fp32 accumulation and K-major A and B.
 // ab_format: kind::f16 -> 0 f16, 1 bf16; kind::f8f6f4 -> 0 e4m3, 1 e5m2.
-__host__ __device__ constexpr uint32_t mma_idesc(uint32_t ab_format, uint32_t m, uint32_t n) {
+__host__ __device__ constexpr uint32_t mma_idesc(uint32_t ab_format, uint32_t m, uint32_t n, uint32_t b_mn_major = 0) {
   return (1u << 4)                 // D format: f32
          | (ab_format << 7)        // A format
          | (ab_format << 10)       // B format
+         | (b_mn_major << 16)      // B major-ness: 0 K-major, 1 MN-major
          | ((n >> 3) << 17)        // N >> 3
          | ((m >> 4) << 24);       // M >> 4
 }
@@ -242,6 +243,32 @@ KD_DEVICE void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
       : "memory");
 }
 KD_DEVICE void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// 32 lanes x 32 consecutive columns stored from registers.
+KD_DEVICE void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Shared-memory descriptor of an MN-major operand tile stored with 128-byte swizzling: 64 bf16 of the M/N dimension
+// per 128-byte row, one row per K index, 8-row (1024-byte) groups along K; consecutive 64-wide M/N blocks are
+// `mn_block_bytes` apart. `addr` is the shared address of the first K row in use (a multiple of 1024 bytes into the
+// block).
+KD_DEVICE uint64_t sw128_mnmajor_desc(uint32_t addr, uint32_t mn_block_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr & 0x3FFFFu) >> 4);             // start address
+  d |= (uint64_t)((mn_block_bytes >> 4) & 0x3FFFu) << 16;  // leading byte offset: next 64-wide M/N block
+  d |= (uint64_t)(1024u >> 4) << 32;                   // stride byte offset: next 8 K rows
+  d |= (uint64_t)1u << 46;                             // descriptor version
+  d |= (uint64_t)2u << 61;                             // 128-byte swizzle
+  return d;
+}
 
 // ------------------------------------------------------------------------------------------------ numerics
 

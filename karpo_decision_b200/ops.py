@@ -216,7 +216,7 @@ def attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: to
         out = torch.empty(tq, hq * d, dtype=torch.bfloat16, device=q.device)
     call("kd_attention_varlen", q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
          out.data_ptr(), out.stride(0), _ptr(gate), gate.stride(0) if gate is not None else 0, cu_q.data_ptr(),
-         cu_k.data_ptr(), cu_q.numel() - 1, int(max_q), tq, hq, k.shape[1], d, float(scale), int(window[0]),
+         cu_k.data_ptr(), cu_q.numel() - 1, int(max_q), tq, k.shape[0], hq, k.shape[1], d, float(scale), int(window[0]),
          int(window[1]), status_word(q.device).data_ptr(), _stream(q))
     return out
 
