@@ -39,6 +39,7 @@ extern "C" {
 #define KD_EPI_RESIDUAL 1 /* C = bf16(R + bf16(acc)); R may alias C (h += x) */
 #define KD_EPI_SWIGLU 2   /* B rows interleaved per 256: [128 gate | 128 up]; C[:, j] = silu(gate_j) * up_j */
 #define KD_EPI_GEGLU 3    /* as SWIGLU with gelu_tanh (gelu_pytorch_tanh) */
+#define KD_EPI_QKV 4      /* internal: the epilogue of kd_qkv_projection (not accepted by kd_gemm_*) */
 
 /* ---------------------------------------------------------------------------------------------- norm weights */
 #define KD_NORM_NONE 0    /* x * rsqrt(mean(x^2) + eps)                 (Gemma4RMSNorm without scale: v_norm) */
@@ -64,6 +65,30 @@ int kd_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C
 int kd_gemm_fp8(const void* A, int64_t lda, const float* scale_a, const void* B, int64_t ldb, const float* scale_b,
                 void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K, int epilogue, int* status,
                 cudaStream_t stream);
+
+/* The attention inputs straight from the QKV projection: the GEMM qkv = A W^T (W = [W_q; W_k; W_v], N = its
+ * width, a multiple of 256) whose epilogue applies what kd_qkv_norm_rope does (per-head RMSNorm over head_dim, RoPE on
+ * the first `rot` dims (rot % 32 == 0), Gemma's v norm) and writes q[M, Hq, hd], k/v[M, Hkv, hd] and, for gated
+ * queries, gate[M, Hq * hd]; the projection itself is never stored. rope_cs is the pack's rotary table from
+ * kd_rope_gather ([rot / 2][M]).
+ * Replaces families/qwen/packed.py:108-121 (_qkv, q/k norm, fused.rope) and families/gemma/packed.py:183-193. */
+int kd_qkv_projection(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+                      const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,
+                      const void* q_norm_w, const void* k_norm_w, int qk_norm_mode, int v_norm_mode, float eps,
+                      const uint32_t* rope_cs, int rot, void* q, void* k, void* v, void* gate, int* status,
+                      cudaStream_t stream);
+
+/* The same with e4m3 A and W and per-row scales (the FP8 path: serve/fp8.py:92-101, serve/qwen_fp8.py:38-42). */
+int kd_qkv_projection_fp8(const void* A, int64_t lda, const float* scale_a, const void* W, int64_t ldw,
+                          const float* scale_w, int M, int N, int K, const int64_t* seqpos, int num_heads_q,
+                          int num_heads_kv, int head_dim, int gated, const void* q_norm_w, const void* k_norm_w,
+                          int qk_norm_mode, int v_norm_mode, float eps, const uint32_t* rope_cs, int rot, void* q,
+                          void* k, void* v, void* gate, int* status, cudaStream_t stream);
+
+/* A pack's rotary factors for kd_qkv_projection: cs[i * T + t] = bf16 cos[seqpos[t], i] | bf16 sin[seqpos[t], i] << 16
+ * for the rot / 2 distinct pairs i (tables from kd_rope_table). One gather per pack and rotary kind. */
+int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab, int rot,
+                   uint32_t* cs, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------- pointwise
  * out[t, :] = table[ids[t], :] (times bf16(scale) when scale != 0: Gemma's scaled embedding, sqrt(hidden)).

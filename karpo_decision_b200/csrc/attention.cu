@@ -10,10 +10,11 @@
 // Sequence boundaries are read from device memory when the kernel runs, so a captured graph serves any pack
 // composition with the same token count.
 //
-// One CTA per (128-query tile of one sequence, query head); 6 warps:
+// One CTA per (128-query tile of one sequence, query head), two CTAs per SM where memory allows (head dim <= 128);
+// 6 warps:
 //   warp 0      TMA producer: the Q tile once, then K and V tiles through a 2-stage ring;
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers, then O += P_j V_j with
-//               P_j read from TMEM (A operand) and V_j as an MN-major B operand from shared memory;
+//               P_j read from TMEM (A operand, written over S_j) and V_j as an MN-major B operand from shared memory;
 //   warps 2..5  softmax, one query row per thread (its TMEM lane): scores -> masked, scaled, exp2 against a running
 //               maximum, bf16 probabilities stored back to TMEM. O is rescaled only when the row maximum grows by
 //               more than 2^8 (the exponent base stays stale otherwise, which is exact: O and the row sum share it);
@@ -27,7 +28,7 @@ namespace fa {
 template <int HD>
 struct Cfg {
   static constexpr int BM = 128;                    // query rows per CTA = TMEM lanes
-  static constexpr int BN = HD == 256 ? 64 : 128;   // keys per tile
+  static constexpr int BN = 64;                     // keys per tile
   static constexpr int CHUNKS = HD / 64;            // 128-byte swizzle chunks along the head dim
   static constexpr int Q_CHUNK = BM * 128;          // bytes of one Q chunk (BM rows x 128 B)
   static constexpr int KV_CHUNK = BN * 128;         // bytes of one K or V chunk
@@ -35,12 +36,14 @@ struct Cfg {
   static constexpr int KV_BYTES = KV_CHUNK * CHUNKS;
   static constexpr int STAGES = 2;
   static constexpr int SMEM = Q_BYTES + STAGES * 2 * KV_BYTES + 1024 + 256;
-  // Tensor-memory columns (fp32): O [0, HD), two score buffers of BN, two probability buffers of BN / 2 (bf16 pairs).
+  // Tensor-memory columns (fp32): O [0, HD), then two score buffers of BN; the bf16 probabilities P_j overwrite the
+  // first BN / 2 columns of their own score buffer once the softmax has read it.
   static constexpr int O_COL = 0;
   static constexpr int S_COL = HD;
-  static constexpr int P_COL = HD + 2 * BN;
-  static constexpr int TMEM_COLS = 512;
-  static_assert(P_COL + BN <= TMEM_COLS, "tensor memory budget");
+  static constexpr int TMEM_COLS = HD + 2 * BN <= 256 ? 256 : 512;
+  // Two CTAs per SM (their softmax and MMA phases interleave) when shared and tensor memory allow it.
+  static constexpr int CTAS_PER_SM = (2 * SMEM <= 227 * 1024 && 2 * TMEM_COLS <= 512) ? 2 : 1;
+  static_assert(S_COL + 2 * BN <= TMEM_COLS, "tensor memory budget");
 };
 
 struct Args {
@@ -59,8 +62,15 @@ struct Args {
 constexpr int THREADS = 192;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale O when the row maximum grows by more than 2^8
 
+// 2^x with the hardware exponential (ex2.approx: relative error ~2^-22; the probabilities are rounded to bf16).
+KD_DEVICE float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 template <int HD>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, Args a) {
   using C = Cfg<HD>;
@@ -178,15 +188,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       };
       if (!issue_s(0)) goto done;
       for (int j = 0; j < n_tiles; ++j) {
-        // S_{j+1} first, so the softmax of tile j+1 can start while P_j V_j runs. Its score buffer was last read
-        // by the softmax of tile j-1, which released it with p_full[(j-1) & 1] (waited for below, one step ago).
-        if (j + 1 < n_tiles && !issue_s(j + 1)) goto done;
+        // S_{j+1} first, so the softmax of tile j+1 can start while P_j V_j runs. Its score buffer last held
+        // P_{j-1}, read by P_{j-1} V_{j-1}: that product must have completed.
+        if (j + 1 < n_tiles) {
+          if (j >= 1 && !mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status)) goto done;
+          if (!issue_s(j + 1)) goto done;
+        }
         const int st = j % C::STAGES;
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, a.status)) goto done;
         if (!mbar_wait(&v_full[st], (j / C::STAGES) & 1, a.status)) goto done;
         tc_fence_after();
         const uint32_t sv = smem_u32(s_kv + st * 2 * C::KV_BYTES + C::KV_BYTES);
-        const uint32_t p = tmem + C::P_COL + (j & 1) * (BN / 2);
+        const uint32_t p = tmem + C::S_COL + (j & 1) * BN;  // P_j over the first BN / 2 columns of S_j
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per instruction: 8 columns of bf16 pairs, 2 KB of V rows
           mma_f16_ts(tmem + C::O_COL, p + kk * 8, sw128_mnmajor_desc(sv + kk * 2048, C::KV_CHUNK), idesc_o,
@@ -201,34 +214,42 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
     const int qi = qs + r + off;  // the row's position on the key axis
-    float m_used = -INFINITY, l_sum = 0.f;
+    float m_used = -INFINITY, l_sum = 0.f;  // running maximum (log2 units, possibly stale) and row sum
     for (int j = 0; j < n_tiles; ++j) {
       if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.status)) goto done;
       tc_fence_after();
+      const uint32_t s_addr = lane_base + C::S_COL + (j & 1) * BN;
       float sv[BN];
 #pragma unroll
       for (int c = 0; c < BN; c += 32) {
         uint32_t t[32];
-        tmem_ld32(lane_base + C::S_COL + (j & 1) * BN + c, t);
+        tmem_ld32(s_addr + c, t);
         tmem_ld_wait_regs(t);
 #pragma unroll
         for (int e = 0; e < 32; ++e) sv[c + e] = __uint_as_float(t[e]);
       }
       const int n0 = (first_tile + j) * BN;
-      float mt = -INFINITY;
+      // Only tiles that cross the causal diagonal, the window's left edge or the sequence end need a mask; the
+      // condition is the same for every row of the CTA.
+      const bool edge = (n0 + BN > lk) || (a.right >= 0 && n0 + BN - 1 > qs + off + a.right) ||
+                        (a.left >= 0 && n0 < qe - 1 + off - a.left);
+      if (edge) {
 #pragma unroll
-      for (int e = 0; e < BN; ++e) {
-        const int key = n0 + e;
-        bool ok = key < lk;
-        if (a.right >= 0) ok = ok && key <= qi + a.right;
-        if (a.left >= 0) ok = ok && key >= qi - a.left;
-        const float x = ok ? sv[e] * a.scale_log2 : -INFINITY;
-        sv[e] = x;
-        mt = fmaxf(mt, x);
+        for (int e = 0; e < BN; ++e) {
+          const int key = n0 + e;
+          bool ok = key < lk;
+          if (a.right >= 0) ok = ok && key <= qi + a.right;
+          if (a.left >= 0) ok = ok && key >= qi - a.left;
+          if (!ok) sv[e] = -INFINITY;
+        }
       }
+      float mraw = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < BN; ++e) mraw = fmaxf(mraw, sv[e]);
+      const float mt = mraw * a.scale_log2;  // the scale is positive: max commutes with it
       const float m_new = fmaxf(m_used, mt);
       const bool need = m_new > m_used + RESCALE_THRESHOLD || (m_used == -INFINITY && m_new != -INFINITY);
-      const float f = !need ? 1.f : (m_used == -INFINITY ? 0.f : exp2f(m_used - m_new));
+      const float f = !need ? 1.f : (m_used == -INFINITY ? 0.f : fast_exp2(m_used - m_new));
       // tcgen05.ld/st are warp-collective: the warp rescales its O rows together (factor 1 where a row needs none).
       if (j > 0 && __any_sync(0xffffffffu, need && m_used != -INFINITY)) {
         // O holds P_{0..j-1} V: wait for the last product before rescaling it in place.
@@ -249,21 +270,19 @@ __global__ void __launch_bounds__(THREADS, 1)
         l_sum *= f;
         m_used = m_new;
       }
-      const float base = m_used == -INFINITY ? 0.f : m_used;
-      // P_j goes to probability buffer j & 1, last read by P_{j-2} V_{j-2}.
-      if (j >= 2 && !mbar_wait(&pv_done[j & 1], ((j - 2) >> 1) & 1, a.status)) goto done;
+      const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
       float rs = 0.f;
 #pragma unroll
       for (int c = 0; c < BN; c += 64) {
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float p0 = exp2f(sv[c + 2 * e] - base);
-          const float p1 = exp2f(sv[c + 2 * e + 1] - base);
+          const float p0 = fast_exp2(fmaf(sv[c + 2 * e], a.scale_log2, neg_base));
+          const float p1 = fast_exp2(fmaf(sv[c + 2 * e + 1], a.scale_log2, neg_base));
           rs += p0 + p1;
           pk[e] = pack_bf16x2(p0, p1);
         }
-        tmem_st32(lane_base + C::P_COL + (j & 1) * (BN / 2) + c / 2, pk);
+        tmem_st32(s_addr + c / 2, pk);  // P_j over the score columns this thread has already read
       }
       l_sum += rs;
       tmem_st_wait();

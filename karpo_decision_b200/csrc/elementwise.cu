@@ -253,6 +253,18 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int rot, i
   sin_out[idx] = bf16_round(sinf(emb));
 }
 
+// cs[i * T + t] = bf16 cos | bf16 sin << 16 of rotary pair i at seqpos[t] (t fastest: coalesced writes).
+__global__ void rope_gather_kernel(const int64_t* __restrict__ seqpos, int64_t T, const float* __restrict__ cos_tab,
+                                   const float* __restrict__ sin_tab, int rot, uint32_t* __restrict__ cs) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int half = rot / 2;
+  if (idx >= T * half) return;
+  const int i = (int)(idx / T);
+  const int64_t t = idx % T;
+  const int64_t off = seqpos[t] * rot + i;
+  cs[idx] = pack_bf16x2(cos_tab[off], sin_tab[off]);
+}
+
 // One warp per (token, head). Heads 0..Hq-1 are queries, Hq..Hq+Hkv-1 keys, then Hkv values.
 template <int HD>
 __global__ void qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int64_t ld, int64_t T,
@@ -526,4 +538,14 @@ extern "C" int kd_readout(const void* hidden, int64_t M, int hidden_size, const 
   ew::readout_kernel<<<blocks_for(M * codes), 32 * WARPS, 0, stream>>>(static_cast<const __nv_bfloat16*>(hidden), M,
                                                                      hidden_size, weight, codes, cap, logits);
   return record_cuda_error(cudaGetLastError(), "readout: launch");
+}
+
+extern "C" int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab, int rot,
+                              uint32_t* cs, cudaStream_t stream) {
+  if (T < 0 || rot <= 0 || rot % 2) return set_error(KD_ERR_ARGUMENT, "rope_gather: bad sizes");
+  if (T == 0) return KD_OK;
+  if (!seqpos || !cos_tab || !sin_tab || !cs) return set_error(KD_ERR_ARGUMENT, "rope_gather: null pointer");
+  const int64_t n = T * (rot / 2);
+  ew::rope_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(seqpos, T, cos_tab, sin_tab, rot, cs);
+  return record_cuda_error(cudaGetLastError(), "rope_gather: launch");
 }

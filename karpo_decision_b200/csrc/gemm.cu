@@ -31,6 +31,22 @@ constexpr int TMEM_COLS = 512;  // two 128 x 256 fp32 accumulators
 constexpr int THREADS = 192;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
 
+// The fused attention-input epilogue (KD_EPI_QKV): the projection's columns are [q heads][k heads][v heads] (Qwen's
+// gated queries: [q_h | gate_h] per head); each output row's heads are normalized, rotated and scattered to q, k, v
+// and gate, as kd_qkv_norm_rope does from a stored projection.
+struct Qkv {
+  const int64_t* seqpos;
+  const uint32_t* cs;  // per token and rotary pair: bf16 cos | bf16 sin << 16, laid out [rot / 2][M] (coalesced)
+  const __nv_bfloat16* q_norm;
+  const __nv_bfloat16* k_norm;
+  __nv_bfloat16* q;
+  __nv_bfloat16* k;
+  __nv_bfloat16* v;
+  __nv_bfloat16* gate;
+  int hq, hkv, hd, rot, gated, qk_mode, v_mode;
+  float eps;
+};
+
 struct Args {
   int M, N, K;
   __nv_bfloat16* C;
@@ -40,7 +56,149 @@ struct Args {
   const float* scale_a;  // FP8: one scale per A row
   const float* scale_b;  // FP8: one scale per B row (output column)
   int* status;
+  Qkv qkv;
 };
+
+// 16 accumulator columns of one row as the projection's bf16 outputs (FP8: scaled first).
+template <bool FP8>
+KD_DEVICE void load16(const Args& a, uint32_t taddr, int col, float sa, float (&x)[16]) {
+  uint32_t r[16];
+  tmem_ld16(taddr, r);
+  tmem_ld_wait_regs(r);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float v = __uint_as_float(r[j]);
+    if constexpr (FP8) v = v * sa * a.scale_b[col + j];
+    x[j] = bf16_round(v);
+  }
+}
+
+KD_DEVICE void store16(__nv_bfloat16* dst, const float (&x)[16]) {
+  uint32_t p[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) p[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(p[0], p[1], p[2], p[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
+}
+
+// The norm multipliers of 16 consecutive head dims (none, w or 1 + w), from two 16-byte loads.
+KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
+  if (mode != KD_NORM_WEIGHT && mode != KD_NORM_ONE_PLUS) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) m[j] = 1.0f;
+    return;
+  }
+  const uint4 lo = *reinterpret_cast<const uint4*>(w + d);
+  const uint4 hi = *reinterpret_cast<const uint4*>(w + d + 8);
+  const uint32_t words[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const float2 f = unpack_bf16x2(words[j]);
+    m[2 * j] = mode == KD_NORM_ONE_PLUS ? 1.0f + f.x : f.x;
+    m[2 * j + 1] = mode == KD_NORM_ONE_PLUS ? 1.0f + f.y : f.y;
+  }
+}
+
+// One row's heads inside the 256 columns [n0, n0 + 256) of the QKV projection: per-head RMSNorm over head_dim, then
+// rotate-half RoPE on the first `rot` dims (q, k); Gemma's weightless v norm; gate and plain v copied. Two passes
+// over tensor memory: the sum of squares, then the normalized, rotated head in 16-column pieces (a piece below rot / 2
+// together with its rotation partner rot / 2 further on). The rotary factors come from the per-pack table `cs`
+// ([rot / 2][M]: the lanes of a warp read consecutive rows, one coalesced 128-byte line per pair index).
+template <bool FP8>
+KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, float sa) {
+  const Qkv& g = a.qkv;
+  const int hd = g.hd;
+  const int q_cols = g.hq * hd * (g.gated ? 2 : 1);
+  const int k_end = q_cols + g.hkv * hd;
+  const int crow = row < a.M ? row : a.M - 1;  // rows past M compute (warp-collective loads) but store nothing
+  const uint32_t* cs = g.cs + crow;
+  for (int h0 = 0; h0 < BN; h0 += hd) {
+    const int c0 = n0 + h0;  // first column of this head slice
+    if (c0 >= a.N) break;
+    const uint32_t th = t_row + h0;
+    int kind;  // 0 q, 1 gate, 2 k, 3 v
+    int head;
+    if (c0 < q_cols) {
+      if (g.gated) {
+        head = c0 / (2 * hd);
+        kind = (c0 % (2 * hd)) == 0 ? 0 : 1;
+      } else {
+        head = c0 / hd;
+        kind = 0;
+      }
+    } else if (c0 < k_end) {
+      head = (c0 - q_cols) / hd;
+      kind = 2;
+    } else {
+      head = (c0 - k_end) / hd;
+      kind = 3;
+    }
+    __nv_bfloat16* dst = kind == 0   ? g.q + ((int64_t)row * g.hq + head) * hd
+                         : kind == 1 ? g.gate + ((int64_t)row * g.hq + head) * hd
+                         : kind == 2 ? g.k + ((int64_t)row * g.hkv + head) * hd
+                                     : g.v + ((int64_t)row * g.hkv + head) * hd;
+    const bool normed = kind == 0 || kind == 2 || (kind == 3 && g.v_mode >= 0);
+    float inv = 1.0f;
+    if (normed) {
+      float ss = 0.f;
+      for (int d = 0; d < hd; d += 16) {
+        float x[16];
+        load16<FP8>(a, th + d, c0 + d, sa, x);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) ss += x[j] * x[j];
+      }
+      inv = 1.0f / sqrtf(ss / (float)hd + g.eps);
+    }
+    if (kind == 1 || kind == 3) {  // gate, v: no rotation
+      for (int d = 0; d < hd; d += 16) {
+        float x[16];
+        load16<FP8>(a, th + d, c0 + d, sa, x);
+        if (normed) {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) x[j] *= inv;
+        }
+        if (row < a.M) store16(dst + d, x);
+      }
+      continue;
+    }
+    const __nv_bfloat16* w = kind == 0 ? g.q_norm : g.k_norm;
+    const int half = g.rot / 2;
+    for (int d = 0; d < hd; d += 16) {
+      if (d >= half && d < g.rot) continue;  // written with its partner
+      float x[16], m[16];
+      load16<FP8>(a, th + d, c0 + d, sa, x);
+      norm16(w, g.qk_mode, d, m);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        x[j] = (x[j] * inv) * m[j];
+        if (g.gated) x[j] = bf16_round(x[j]);  // Qwen: the norm is its own op (rounded), RoPE another
+      }
+      if (d < half) {
+        uint32_t f[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) f[j] = cs[(int64_t)(d + j) * a.M];
+        float y[16];
+        load16<FP8>(a, th + d + half, c0 + d + half, sa, y);
+        norm16(w, g.qk_mode, d + half, m);
+        float ox[16], oy[16];
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          y[j] = (y[j] * inv) * m[j];
+          if (g.gated) y[j] = bf16_round(y[j]);
+          const float2 c_s = unpack_bf16x2(f[j]);  // cos and sin of pair d + j (the same for d + j + half)
+          ox[j] = x[j] * c_s.x - y[j] * c_s.y;
+          oy[j] = y[j] * c_s.x + x[j] * c_s.y;
+        }
+        if (row < a.M) {
+          store16(dst + d, ox);
+          store16(dst + d + half, oy);
+        }
+      } else if (row < a.M) {
+        store16(dst + d, x);
+      }
+    }
+  }
+}
 
 template <int EPI>
 KD_DEVICE void store_chunk(const Args& a, int row, int col0, const float (&v)[32]) {
@@ -194,7 +352,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       float sa = 1.0f;
       if constexpr (FP8) sa = (row < args.M) ? args.scale_a[row] : 0.0f;
-      if constexpr (EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU) {
+      if constexpr (EPI == KD_EPI_QKV) {
+        qkv_epilogue<FP8>(args, row, n0, t_row, sa);
+      } else if constexpr (EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU) {
         // Columns [0,128) of the tile are gate rows, [128,256) the matching up rows (weights interleaved at load):
         // out[:, n0/2 + c] = act(gate) * up, each operand rounded to bf16 first as the reference's Linear outputs are.
         for (int c = 0; c < BN / 2; c += 32) {
@@ -282,7 +442,7 @@ using namespace kd;
 
 static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
                        int64_t ldr, const float* scale_a, const float* scale_b, int M, int N, int K, int epilogue,
-                       int fp8, int* status, cudaStream_t stream) {
+                       int fp8, int* status, cudaStream_t stream, const gemm::Qkv* qkv = nullptr) {
   if (M < 0 || N <= 0 || K <= 0) return set_error(KD_ERR_ARGUMENT, "gemm: M >= 0, N > 0 and K > 0 required");
   if (M == 0) return KD_OK;
   if (!A || !B || !C || !status) return set_error(KD_ERR_ARGUMENT, "gemm: null pointer");
@@ -320,6 +480,7 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
   args.scale_a = scale_a;
   args.scale_b = scale_b;
   args.status = status;
+  args.qkv = qkv ? *qkv : gemm::Qkv{};
 
 #define KD_GEMM_CASE(E)                                                         \
   case E:                                                                       \
@@ -330,20 +491,86 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
     KD_GEMM_CASE(KD_EPI_RESIDUAL)
     KD_GEMM_CASE(KD_EPI_SWIGLU)
     KD_GEMM_CASE(KD_EPI_GEGLU)
+    KD_GEMM_CASE(KD_EPI_QKV)
     default:
       return set_error(KD_ERR_ARGUMENT, "gemm: unknown epilogue");
   }
 #undef KD_GEMM_CASE
 }
 
+static int qkv_common(const void* A, int64_t lda, const float* scale_a, const void* W, int64_t ldw,
+                      const float* scale_w, int M, int N, int K, const int64_t* seqpos, int num_heads_q,
+                      int num_heads_kv, int head_dim, int gated, const void* q_norm_w, const void* k_norm_w,
+                      int qk_norm_mode, int v_norm_mode, float eps, const uint32_t* rope_cs, int rot, void* q,
+                      void* k, void* v, void* gate, int fp8, int* status, cudaStream_t stream) {
+  if (num_heads_q <= 0 || num_heads_kv <= 0 || num_heads_q % num_heads_kv)
+    return set_error(KD_ERR_ARGUMENT, "qkv_projection: bad head counts");
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return set_error(KD_ERR_ARGUMENT, "qkv_projection: head_dim must be 64, 128 or 256");
+  const int64_t width = (int64_t)num_heads_q * head_dim * (gated ? 2 : 1) + 2LL * num_heads_kv * head_dim;
+  if (N != width || N % gemm::BN)
+    return set_error(KD_ERR_ARGUMENT, "qkv_projection: N must equal the q/k/v width and be a multiple of 256");
+  if (rot < 0 || rot > head_dim || rot % 32)
+    return set_error(KD_ERR_ARGUMENT, "qkv_projection: rotary width must be a multiple of 32 within head_dim");
+  if (M > 0 && (!seqpos || !q || !k || !v || (gated && !gate) || (rot > 0 && !rope_cs) ||
+                (qk_norm_mode > KD_NORM_NONE && (!q_norm_w || !k_norm_w))))
+    return set_error(KD_ERR_ARGUMENT, "qkv_projection: null pointer");
+  auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!a16(q) || !a16(k) || !a16(v) || (gate && !a16(gate)))
+    return set_error(KD_ERR_ARGUMENT, "qkv_projection: outputs must be 16-byte aligned");
+  gemm::Qkv g;
+  g.seqpos = seqpos;
+  g.cs = rope_cs;
+  g.q_norm = static_cast<const __nv_bfloat16*>(q_norm_w);
+  g.k_norm = static_cast<const __nv_bfloat16*>(k_norm_w);
+  g.q = static_cast<__nv_bfloat16*>(q);
+  g.k = static_cast<__nv_bfloat16*>(k);
+  g.v = static_cast<__nv_bfloat16*>(v);
+  g.gate = static_cast<__nv_bfloat16*>(gate);
+  g.hq = num_heads_q;
+  g.hkv = num_heads_kv;
+  g.hd = head_dim;
+  g.rot = rot;
+  g.gated = gated;
+  g.qk_mode = qk_norm_mode;
+  g.v_mode = v_norm_mode;
+  g.eps = eps;
+  // C is unused by this epilogue; q stands in for the pointer checks.
+  return gemm_common(A, lda, W, ldw, q, N, nullptr, 0, scale_a, scale_w, M, N, K, KD_EPI_QKV, fp8, status, stream,
+                     &g);
+}
+
+extern "C" int kd_qkv_projection(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+                                 const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,
+                                 const void* q_norm_w, const void* k_norm_w, int qk_norm_mode, int v_norm_mode,
+                                 float eps, const uint32_t* rope_cs, int rot, void* q, void* k, void* v,
+                                 void* gate, int* status, cudaStream_t stream) {
+  return qkv_common(A, lda, nullptr, W, ldw, nullptr, M, N, K, seqpos, num_heads_q, num_heads_kv, head_dim, gated,
+                    q_norm_w, k_norm_w, qk_norm_mode, v_norm_mode, eps, rope_cs, rot, q, k, v, gate, 0,
+                    status, stream);
+}
+
+extern "C" int kd_qkv_projection_fp8(const void* A, int64_t lda, const float* scale_a, const void* W, int64_t ldw,
+                                     const float* scale_w, int M, int N, int K, const int64_t* seqpos,
+                                     int num_heads_q, int num_heads_kv, int head_dim, int gated, const void* q_norm_w,
+                                     const void* k_norm_w, int qk_norm_mode, int v_norm_mode, float eps,
+                                     const uint32_t* rope_cs, int rot, void* q, void* k, void* v, void* gate,
+                                     int* status, cudaStream_t stream) {
+  return qkv_common(A, lda, scale_a, W, ldw, scale_w, M, N, K, seqpos, num_heads_q, num_heads_kv, head_dim, gated,
+                    q_norm_w, k_norm_w, qk_norm_mode, v_norm_mode, eps, rope_cs, rot, q, k, v, gate, 1,
+                    status, stream);
+}
+
 extern "C" int kd_gemm_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc,
                             const void* R, int64_t ldr, int M, int N, int K, int epilogue, int* status,
                             cudaStream_t stream) {
+  if (epilogue == KD_EPI_QKV) return set_error(KD_ERR_ARGUMENT, "gemm: the QKV epilogue is kd_qkv_projection");
   return gemm_common(A, lda, B, ldb, C, ldc, R, ldr, nullptr, nullptr, M, N, K, epilogue, 0, status, stream);
 }
 
 extern "C" int kd_gemm_fp8(const void* A, int64_t lda, const float* scale_a, const void* B, int64_t ldb,
                            const float* scale_b, void* C, int64_t ldc, const void* R, int64_t ldr, int M, int N, int K,
                            int epilogue, int* status, cudaStream_t stream) {
+  if (epilogue == KD_EPI_QKV) return set_error(KD_ERR_ARGUMENT, "gemm: the QKV epilogue is kd_qkv_projection_fp8");
   return gemm_common(A, lda, B, ldb, C, ldc, R, ldr, scale_a, scale_b, M, N, K, epilogue, 1, status, stream);
 }

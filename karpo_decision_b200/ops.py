@@ -11,7 +11,8 @@ from ._lib import EPI_GEGLU, EPI_RESIDUAL, EPI_STORE, EPI_SWIGLU, NORM_NONE, NOR
 
 __all__ = ["EPI_GEGLU", "EPI_RESIDUAL", "EPI_STORE", "EPI_SWIGLU", "NORM_NONE", "NORM_ONE_PLUS", "NORM_WEIGHT",
            "add_rmsnorm", "attention_varlen", "check_status", "embed", "gemm", "gemm_fp8", "marker_norm",
-           "norm_add", "qkv_norm_rope", "quantize_rows_e4m3", "readout", "rmsnorm", "rmsnorm_e4m3", "rope_table",
+           "norm_add", "qkv_norm_rope", "qkv_projection", "quantize_rows_e4m3", "readout", "rmsnorm", "rmsnorm_e4m3",
+           "rope_gather", "rope_table",
            "status_word"]
 
 _STATUS: dict[int, torch.Tensor] = {}
@@ -245,3 +246,46 @@ def readout(hidden: torch.Tensor, weight: torch.Tensor, cap: float | None = None
     call("kd_readout", hidden.data_ptr(), m, hidden.shape[1], weight.data_ptr(), codes, float(cap or 0.0),
          out.data_ptr(), _stream(hidden))
     return out
+
+
+def rope_gather(seqpos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor | None = None
+                ) -> torch.Tensor:
+    """The pack's rotary factors for ``qkv_projection``: int32 (rot / 2, T) of packed bf16 (cos, sin) pairs."""
+    _require(seqpos.dtype == torch.int64 and seqpos.is_contiguous(), "seqpos must be contiguous int64")
+    t, rot = seqpos.numel(), cos.shape[1]
+    if out is None:
+        out = torch.empty(rot // 2, t, dtype=torch.int32, device=seqpos.device)
+    call("kd_rope_gather", seqpos.data_ptr(), t, cos.data_ptr(), sin.data_ptr(), rot, out.data_ptr(), _stream(cos))
+    return out
+
+
+def qkv_projection(a: torch.Tensor, w: torch.Tensor, seqpos: torch.Tensor, heads: int, kv_heads: int,
+                   head_dim: int, gated: bool, q_norm: torch.Tensor | None, k_norm: torch.Tensor | None, qk_mode: int,
+                   v_mode: int, eps: float, cs: torch.Tensor, rot: int, out: tuple | None = None,
+                   scale_a: torch.Tensor | None = None, scale_w: torch.Tensor | None = None) -> tuple:
+    """The QKV projection with q/k norms, RoPE and the v norm in its epilogue: (q, k, v, gate or None). bf16 ``a`` and
+    ``w``, or e4m3 with per-row scales ``scale_a`` / ``scale_w``; ``cs`` from ``rope_gather`` over the same rows."""
+    _rowmajor(a, "a")
+    _rowmajor(w, "w")
+    _require(seqpos.dtype == torch.int64 and seqpos.is_contiguous(), "seqpos must be contiguous int64")
+    t, dev = a.shape[0], a.device
+    _require(cs.dtype == torch.int32 and cs.is_contiguous() and cs.shape == (rot // 2, t), "cs: (rot / 2, rows)")
+    if out is None:
+        q = torch.empty(t, heads, head_dim, dtype=torch.bfloat16, device=dev)
+        k = torch.empty(t, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
+        v = torch.empty(t, kv_heads, head_dim, dtype=torch.bfloat16, device=dev)
+        gate = torch.empty(t, heads * head_dim, dtype=torch.bfloat16, device=dev) if gated else None
+    else:
+        q, k, v, gate = out
+    tail = (seqpos.data_ptr(), heads, kv_heads, head_dim, int(gated), _ptr(q_norm), _ptr(k_norm), qk_mode, v_mode,
+            float(eps), cs.data_ptr(), rot, q.data_ptr(), k.data_ptr(), v.data_ptr(), _ptr(gate),
+            status_word(dev).data_ptr(), _stream(a))
+    if scale_a is None:
+        _require(a.dtype == torch.bfloat16 and w.dtype == torch.bfloat16, "bf16 operands")
+        call("kd_qkv_projection", a.data_ptr(), a.stride(0), w.data_ptr(), w.stride(0), t, w.shape[0], a.shape[1],
+             *tail)
+    else:
+        _require(a.dtype == torch.float8_e4m3fn and w.dtype == torch.float8_e4m3fn, "e4m3 operands")
+        call("kd_qkv_projection_fp8", a.data_ptr(), a.stride(0), scale_a.data_ptr(), w.data_ptr(), w.stride(0),
+             scale_w.data_ptr(), t, w.shape[0], a.shape[1], *tail)
+    return q, k, v, gate

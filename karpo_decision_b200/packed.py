@@ -95,13 +95,20 @@ class Layer:
 class Workspace:
     """Activation buffers for packs of up to ``capacity`` tokens (allocated once, reused by every layer and pack)."""
 
-    def __init__(self, spec: Spec, capacity: int, device: torch.device, fp8: bool, inter_pad: int) -> None:
+    def __init__(self, spec: Spec, capacity: int, device: torch.device, fp8: bool, inter_pad: int,
+                 stored_qkv: bool) -> None:
         t, h, hd = capacity, spec.hidden, spec.head_dim
         bf = dict(dtype=torch.bfloat16, device=device)
         self.capacity = capacity
         self.h = torch.empty(t, h, **bf)
         self.x = torch.empty(t, h, **bf)
-        self.qkv = torch.empty(t, spec.qkv_width, **bf)
+        # the stored projection, only for the unfused QKV path
+        self.qkv = torch.empty(t, spec.qkv_width, **bf) if stored_qkv else None
+        rot = int(hd * spec.partial_rotary) if spec.family == "qwen" else hd
+        # per rotary kind, the pack's rotary factors: (rot / 2, T) contiguous, viewed from a flat buffer per pack
+        self.rot_half = rot // 2
+        self._cs = {kind: torch.empty(self.rot_half * t, dtype=torch.int32, device=device)
+                    for kind in set(spec.layer_types())}
         self.q = torch.empty(t, spec.heads, hd, **bf)
         self.k = torch.empty(t, spec.kv_heads, hd, **bf)
         self.v = torch.empty(t, spec.kv_heads, hd, **bf)
@@ -116,6 +123,9 @@ class Workspace:
 
     def e4m3(self, rows: int, cols: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.xq[: rows * cols].view(rows, cols), self.xs[:rows]
+
+    def cs(self, kind: str, tokens: int) -> torch.Tensor:
+        return self._cs[kind][: self.rot_half * tokens].view(self.rot_half, tokens)
 
 
 class Packed(torch.nn.Module):
@@ -174,6 +184,10 @@ class Packed(torch.nn.Module):
                                        else weights[p + "layer_scalar"].reshape(1), dev)
             self.layers.append(layer)
         self._inv_freq = {kind: self._inv_freq_of(kind) for kind in set(self.types)}
+        rot = int(s.head_dim * s.partial_rotary) if s.family == "qwen" else s.head_dim
+        #: The QKV projection's epilogue does the norms and RoPE (kd_qkv_projection) when its shape allows:
+        #: width a multiple of 256 and rotary width a multiple of 32; otherwise GEMM + kd_qkv_norm_rope.
+        self.fused_qkv = s.qkv_width % 256 == 0 and rot % 32 == 0
         self._tables: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
         self._workspace: Workspace | None = None
 
@@ -256,7 +270,8 @@ class Packed(torch.nn.Module):
     def workspace(self, tokens: int) -> Workspace:
         if self._workspace is None or self._workspace.capacity < tokens:
             self._workspace = None
-            self._workspace = Workspace(self.spec, tokens, self.device, self.fp8, self.inter_pad)
+            stored = not self.fused_qkv or any(len(layer.qkv) > 1 for layer in self.layers)
+            self._workspace = Workspace(self.spec, tokens, self.device, self.fp8, self.inter_pad, stored)
         return self._workspace
 
     # ---------------------------------------------------------------- forward
@@ -299,18 +314,30 @@ class Packed(torch.nn.Module):
         positions = int(max_len)
         if p.segment_ids_cpu is not None:  # block layouts carry their own positions
             positions = max(positions, int(seqpos.max().item()) + 1)
+        rope_cs: dict[str, torch.Tensor] = {}  # per rotary kind, gathered once per pack
         for layer in self.layers:
             fp8_qkv = any(proj.fp8 for proj, _, _ in layer.qkv)
             bf16_qkv = any(not proj.fp8 for proj, _, _ in layer.qkv)
             x, x8 = self._normed(ws, h, layer.input_norm, mode, bf16_qkv, fp8_qkv)
-            qkv = ws.qkv[:t]
-            for proj, col, width in layer.qkv:
-                self._project(proj, x, x8, qkv[:, col:col + width] if width != qkv.shape[1] else qkv)
             cos, sin = self.tables(layer.kind, positions)
-            q, k, v, gate = ops.qkv_norm_rope(
-                qkv, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm, mode,
-                -1 if qwen else ops.NORM_NONE, eps, cos, sin,
-                out=(ws.q[:t], ws.k[:t], ws.v[:t], ws.gate[:t] if qwen else None))
+            heads_out = (ws.q[:t], ws.k[:t], ws.v[:t], ws.gate[:t] if qwen else None)
+            v_mode = -1 if qwen else ops.NORM_NONE
+            if self.fused_qkv and len(layer.qkv) == 1:
+                # one GEMM whose epilogue normalizes, rotates and scatters the heads (kd_qkv_projection)
+                if layer.kind not in rope_cs:
+                    rope_cs[layer.kind] = ops.rope_gather(seqpos, cos, sin, out=ws.cs(layer.kind, t))
+                proj = layer.qkv[0][0]
+                a_in, sa = (x8[0], x8[1]) if proj.fp8 else (x, None)
+                q, k, v, gate = ops.qkv_projection(
+                    a_in, proj.weight, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm,
+                    mode, v_mode, eps, rope_cs[layer.kind], cos.shape[1], out=heads_out, scale_a=sa,
+                    scale_w=proj.scale)
+            else:
+                qkv = ws.qkv[:t]
+                for proj, col, width in layer.qkv:
+                    self._project(proj, x, x8, qkv[:, col:col + width] if width != qkv.shape[1] else qkv)
+                q, k, v, gate = ops.qkv_norm_rope(qkv, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm,
+                                                  layer.k_norm, mode, v_mode, eps, cos, sin, out=heads_out)
             if layer.kind == "sliding_attention":
                 window = (self.window - 1, 0)
             else:

@@ -12,7 +12,8 @@ import torch
 from . import _lib
 
 #: Argument positions of (M, N, K) in the GEMM entry points.
-_GEMM_MNK = {"kd_gemm_bf16": (8, 9, 10), "kd_gemm_fp8": (10, 11, 12)}
+_GEMM_MNK = {"kd_gemm_bf16": (8, 9, 10), "kd_gemm_fp8": (10, 11, 12), "kd_qkv_projection": (4, 5, 6),
+             "kd_qkv_projection_fp8": (6, 7, 8)}
 
 
 class KernelTimes:

@@ -269,3 +269,45 @@ def test_marker_norm_and_readout():
         logits = ops.readout(out, head, cap).cpu().numpy()
         ref = oracle.readout(out.float().cpu().numpy(), head.cpu().numpy(), cap)
         assert np.abs(logits - ref).max() <= 1e-5
+
+
+@pytest.mark.parametrize("family,hd,partial,fp8", [("qwen", 128, 1.0, False), ("qwen", 64, 0.5, False),
+                                                   ("gemma", 256, 1.0, False), ("gemma", 128, 1.0, False),
+                                                   ("qwen", 128, 1.0, True), ("gemma", 128, 1.0, True)])
+def test_qkv_projection_equals_gemm_then_norm_rope(family, hd, partial, fp8):
+    """The fused QKV epilogue against the stored projection followed by kd_qkv_norm_rope (one bf16 ulp: the sums of
+    squares run in another order)."""
+    g = rng(13)
+    t, hq, hkv, hidden = 301, 4, 2, 256
+    gated = family == "qwen"
+    width = hq * hd * (2 if gated else 1) + 2 * hkv * hd
+    x = bf16(g.standard_normal((t, hidden)))
+    w = bf16(g.standard_normal((width, hidden)) * 0.05)
+    seqpos = torch.from_numpy(np.concatenate([np.arange(200), np.arange(101)])).to(DEV)
+    one_plus = gated
+    mode = ops.NORM_ONE_PLUS if one_plus else ops.NORM_WEIGHT
+    qn = bf16(g.standard_normal(hd) * 0.1 + (0 if one_plus else 1))
+    kn = bf16(g.standard_normal(hd) * 0.1 + (0 if one_plus else 1))
+    rot = int(hd * partial)
+    inv = 1.0 / (1e6 ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
+    cos, sin = ops.rope_table(inv.to(DEV), 256)
+    v_mode = -1 if gated else ops.NORM_NONE
+    if fp8:
+        xq, xs = ops.quantize_rows_e4m3(x)
+        wq, ws = ops.quantize_rows_e4m3(w)
+        qkv = ops.gemm_fp8(xq, xs, wq, ws)
+        cs = ops.rope_gather(seqpos, cos, sin)
+        fused = ops.qkv_projection(xq, wq, seqpos, hq, hkv, hd, gated, qn, kn, mode, v_mode, 1e-6, cs, rot,
+                                   scale_a=xs, scale_w=ws)
+    else:
+        qkv = ops.gemm(x, w)
+        cs = ops.rope_gather(seqpos, cos, sin)
+        fused = ops.qkv_projection(x, w, seqpos, hq, hkv, hd, gated, qn, kn, mode, v_mode, 1e-6, cs, rot)
+    split = ops.qkv_norm_rope(qkv, seqpos, hq, hkv, hd, gated, qn, kn, mode, v_mode, 1e-6, cos, sin)
+    for a_, b_ in zip(fused, split, strict=True):
+        if a_ is None:
+            assert b_ is None
+            continue
+        diff = (a_.float() - b_.float()).abs().max().item()
+        assert diff <= 2 ** -7 * max(b_.float().abs().max().item(), 1.0), diff
+    ops.check_status(DEV)

@@ -1,0 +1,74 @@
+"""Host-side logic of the B200 path that needs no GPU: weight repacking, workspace layout, packing, shapes."""
+
+import numpy as np
+import torch
+
+from karpo_decision_b200.pack import from_arrays, pack
+from karpo_decision_b200.packed import GATE_BLOCK, Workspace, interleave_gate_up
+from karpo_decision_b200.synthetic import CONFIGS, Spec, numpy_weights, synthetic_lengths, synthetic_pack_arrays
+
+
+def test_interleave_gate_up_blocks_and_padding():
+    gate = torch.arange(300 * 4, dtype=torch.float32).view(300, 4)
+    up = -gate
+    w = interleave_gate_up(gate, up)
+    assert w.shape == (2 * 384, 4)  # 300 padded to 3 blocks of 128
+    assert torch.equal(w[:128], gate[:128]) and torch.equal(w[128:256], up[:128])
+    assert torch.equal(w[512:512 + 44], gate[256:300]) and w[512 + 44:640].abs().sum() == 0
+    assert torch.equal(w[640:640 + 44], up[256:300]) and w[640 + 44:].abs().sum() == 0
+    assert GATE_BLOCK == 128
+
+
+def test_workspace_views_are_contiguous():
+    spec = CONFIGS["tiny"]
+    ws = Workspace(spec, 1000, torch.device("cpu"), fp8=True, inter_pad=1024, stored_qkv=False)
+    cs = ws.cs("full_attention", 700)
+    assert cs.shape == (32, 700) and cs.is_contiguous()
+    q, s = ws.e4m3(700, 256)
+    assert q.shape == (700, 256) and q.is_contiguous() and s.shape == (700,)
+    assert ws.q.shape == (1000, 4, 64) and ws.gate.shape == (1000, 256) and ws.qkv is None
+
+
+def test_synthetic_lengths_fill_exactly():
+    lengths = synthetic_lengths(65536, 128, 8192, seed=3)
+    assert sum(lengths) == 65536 and min(lengths) >= 1 and max(lengths) <= 8192
+
+
+def test_pack_arrays_and_from_arrays_agree_with_pack():
+    arrays = synthetic_pack_arrays([5, 9, 3], 100, seed=1, markers_per_seq=(1, 3))
+    assert arrays["cu"].tolist() == [0, 5, 14, 17]
+    assert (np.diff(arrays["marker_cu"]) >= 1).all()
+    # the last token of every sequence is a marker
+    ends = set((arrays["cu"][1:] - 1).tolist())
+    assert ends <= set(arrays["markers"].tolist())
+    p = from_arrays(arrays, torch.device("cpu"))
+    assert p.cu.dtype == torch.int32 and p.markers.dtype == torch.int64 and p.max_length == 9
+
+    class Seq:
+        def __init__(self, ids, markers):
+            self.input_ids, self.markers = ids, markers
+
+    seqs = [Seq(torch.from_numpy(arrays["input_ids"][a:b]), torch.from_numpy(
+        arrays["markers"][arrays["marker_cu"][i]:arrays["marker_cu"][i + 1]] - a))
+        for i, (a, b) in enumerate(zip(arrays["cu"][:-1], arrays["cu"][1:]))]
+    q = pack(seqs, torch.device("cpu"))
+    assert torch.equal(q.markers, p.markers) and torch.equal(q.cu, p.cu) and torch.equal(q.seqpos, p.seqpos)
+
+
+def test_spec_flops_and_gemma_layer_pattern():
+    spec = CONFIGS["qwen-0.8b"]
+    assert spec.qkv_width == 6144
+    # QKV 1024x6144, o 2048x1024, gate-up 1024x6144, down 3072x1024 -> ~1 GFLOP per token (28 layers)
+    assert abs(spec.gemm_flops_per_token() / 1e9 - 0.998) < 0.01
+    g = Spec("gemma", 62, 64, 2, 1, 64, 64, 10)
+    types = g.layer_types()
+    assert types[5] == "full_attention" and types[4] == "sliding_attention" and types[-1] == "full_attention"
+
+
+def test_numpy_weights_are_bf16_exact_and_seeded():
+    spec = CONFIGS["tiny"]
+    a, b = numpy_weights(spec, 3), numpy_weights(spec, 3)
+    for key in a:
+        assert np.array_equal(a[key], b[key])
+    w = a["layers.0.q_proj"]
+    assert np.array_equal(torch.from_numpy(w).bfloat16().float().numpy(), w)
