@@ -49,13 +49,16 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--fp8", action="store_true")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the baseline sample")
+    ap.add_argument("--tokens", type=int, default=0, help="tokens per pack (default: the configuration's; smaller "
+                                                          "packs are for profiling captures)")
     return ap.parse_args()
 
 
-def workload(config: str, seed: int) -> dict:
+def workload(config: str, seed: int, tokens: int = 0) -> dict:
     from karpo_decision_b200.synthetic import CONFIGS, synthetic_lengths, synthetic_pack_arrays
 
-    tokens, (low, high), log = WORKLOADS[config]
+    default, (low, high), log = WORKLOADS[config]
+    tokens = tokens or default
     spec = CONFIGS[config]
     lengths = synthetic_lengths(tokens, low, high, seed, log_uniform=log)
     return synthetic_pack_arrays(lengths, spec.vocab, seed + 1, (1, 4))
@@ -127,6 +130,7 @@ def run_reference(args: argparse.Namespace) -> None:
 
 def config_block(args: argparse.Namespace, world: int) -> dict:
     tokens, (low, high), log = WORKLOADS[args.config]
+    tokens = args.tokens or tokens
     return {"workload": f"{args.config} packed prefill, packs of {tokens} tokens, lengths "
                         f"{'log-uniform' if log else 'uniform'} [{low},{high}], 1-4 markers/sequence, causal"
                         + (", FP8 projections" if args.fp8 else ""),
@@ -217,7 +221,7 @@ def run_ours(args: argparse.Namespace) -> None:
     model = Packed(spec, weights, dev, fp8=args.fp8)
     head = Readout(weights["readout"].float(), spec.logit_cap, dev)
     del weights
-    arrays = workload(args.config, seed=1000 + rank)
+    arrays = workload(args.config, seed=1000 + rank, tokens=args.tokens)
     tokens = len(arrays["input_ids"])
     p = from_arrays(arrays, dev)
     torch.cuda.synchronize()
@@ -278,7 +282,6 @@ def run_ours(args: argparse.Namespace) -> None:
 
     if rank == 0:
         gemm = prof.summary("gemm")
-        flops = spec.gemm_flops_per_token() * tokens / spec.layers  # per layer; one launch set per layer
         peaks = peak_numbers()
         launches = prof.launches // args.steps
         per_launch_flops = gemm["flops_per_launch"]
@@ -297,7 +300,6 @@ def run_ours(args: argparse.Namespace) -> None:
             "kernel_shares": prof.shares(),
             "clocks": clocks.summary(),
         }
-        del flops
         if world == 1 and os.environ.get("KD_BENCH_NO_CPU") != "1":
             line["cpu_baseline"] = cpu_sample_rate(args.config, args.cpu_seconds, args.fp8)
         print(json.dumps(line), flush=True)
