@@ -281,11 +281,29 @@ def run_ours(args: argparse.Namespace) -> None:
     e2e_value = tokens * world / (e2e_ms / 1000.0)
 
     if rank == 0:
-        gemm = prof.summary("gemm")
         peaks = peak_numbers()
         launches = prof.launches // args.steps
-        per_launch_flops = gemm["flops_per_launch"]
-        achieved = per_launch_flops / (gemm["mean_ms"] / 1000.0) / 1e12 if gemm["mean_ms"] else None
+        # GEMMs (projections, the fused QKV one included): FLOPs from each launch's M, N, K
+        gemm = prof.summary("gemm")
+        qkv = prof.summary("qkv_projection")
+        g_ms = (gemm["mean_ms"] or 0) * gemm["launches"] + (qkv["mean_ms"] or 0) * qkv["launches"]
+        g_flops = gemm["flops_per_launch"] * gemm["launches"] + qkv["flops_per_launch"] * qkv["launches"]
+        gemm_tf = g_flops / (g_ms / 1000.0) / 1e12 if g_ms else None
+        # attention: algorithmic FLOPs of the pack's visible (query, key) pairs, 4 * head_dim per pair and head
+        attn = prof.summary("attention")
+        a_ms = (attn["mean_ms"] or 0) * attn["launches"]
+        a_flops = attention_flops(spec, np.diff(arrays["cu"])) * args.steps
+        attn_tf = a_flops / (a_ms / 1000.0) / 1e12 if a_ms else None
+        kernels = {
+            "attention": {"kernel": "kd_attention_varlen", "bound": "tensor", "achieved": attn_tf,
+                          "ms_per_step": a_ms / args.steps, "traffic": traffic("attention", args, tokens)},
+            "gemm": {"kernel": "kd_gemm_bf16 + kd_qkv_projection" if not args.fp8 else
+                     "kd_gemm_fp8 + kd_qkv_projection_fp8", "bound": "tensor", "achieved": gemm_tf,
+                     "ms_per_step": g_ms / args.steps, "traffic": None},
+        }
+        dominant = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
+        top = kernels[dominant]
+        achieved = top["achieved"]
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
@@ -293,10 +311,11 @@ def run_ours(args: argparse.Namespace) -> None:
             "config": config_block(args, world),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
-            "roofline": {"bound": "tensor", "kernel": "kd_gemm_bf16" if not args.fp8 else "kd_gemm_fp8",
-                         "achieved": achieved, "peak": peaks[0], "unit": "TFLOP/s",
-                         "frac": achieved / peaks[0] if achieved else None, "traffic": None,
-                         "peak_source": peaks[1]},
+            "roofline": {"bound": "tensor", "kernel": top["kernel"], "achieved": achieved, "peak": peaks[0],
+                         "unit": "TFLOP/s", "frac": achieved / peaks[0] if achieved else None,
+                         "traffic": top["traffic"], "peak_source": peaks[1]},
+            "roofline_kernels": {k: {**v, "frac": v["achieved"] / peaks[0] if v["achieved"] else None}
+                                 for k, v in kernels.items()},
             "kernel_shares": prof.shares(),
             "clocks": clocks.summary(),
         }
@@ -305,6 +324,32 @@ def run_ours(args: argparse.Namespace) -> None:
         print(json.dumps(line), flush=True)
     if group is not None:
         group.destroy_process_group()
+
+
+def attention_flops(spec, lengths) -> float:
+    """FLOPs of one forward's attention over a pack: per layer, 4 * head_dim * heads per visible (query, key) pair;
+    causal pairs L (L + 1) / 2 per sequence, sliding-window pairs sum_i min(i + 1, W)."""
+    total = 0.0
+    lengths = [int(n) for n in lengths]
+    causal = sum(n * (n + 1) / 2 for n in lengths)
+    w = spec.window
+    sliding = sum((min(n, w) * (min(n, w) + 1)) / 2 + max(0, n - w) * w for n in lengths)
+    for kind in spec.layer_types():
+        total += 4.0 * spec.head_dim * spec.heads * (causal if kind == "full_attention" else sliding)
+    return total
+
+
+#: DRAM bytes per launch from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) on a smaller pack of the
+#: same configuration, scaled by the tokens a launch processes (Q, K, V and O each move once per launch).
+TRAFFIC_CAPTURES = {("qwen-0.8b", "attention"): (8192, 100.748032e6 + 13.882112e6)}
+
+
+def traffic(kernel: str, args, tokens: int) -> float | None:
+    capture = TRAFFIC_CAPTURES.get((args.config, kernel))
+    if capture is None or args.fp8:
+        return None
+    captured_tokens, nbytes = capture
+    return nbytes * tokens / captured_tokens
 
 
 def from_pinned(pinned: dict, dev, arrays: dict):
