@@ -85,6 +85,19 @@ int kd_qkv_projection_fp8(const void* A, int64_t lda, const float* scale_a, cons
                           int qk_norm_mode, int v_norm_mode, float eps, const uint32_t* rope_cs, int rot, void* q,
                           void* k, void* v, void* gate, int* status, cudaStream_t stream);
 
+/* kd_qkv_projection for callers that cannot allocate device memory (a plugin host that owns every allocation and
+ * passes only inputs and outputs, a runtime that forbids side allocations): the per-pack rotary scratch lives in a
+ * static device array of the library (4 Mi uint32 entries, 16 MiB per device that loads the library, held until exit)
+ * instead of a caller buffer. Takes the rotary tables of kd_rope_table; calls needing more than 4 Mi entries
+ * ((rot / 2) * M) are rejected. All calls on a device share the array (overlapping calls race); the first call on a
+ * device looks up the array's address and should come before any stream capture. Allocates nothing.
+ * No counterpart in the reference: an addition of this library for allocation-free callers. */
+int kd_qkv_projection_noalloc(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+                              const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,
+                              const void* q_norm_w, const void* k_norm_w, int qk_norm_mode, int v_norm_mode, float eps,
+                              const float* cos_tab, const float* sin_tab, int rot, void* q, void* k, void* v,
+                              void* gate, int* status, cudaStream_t stream);
+
 /* A pack's rotary factors for kd_qkv_projection: cs[i * T + t] = bf16 cos[seqpos[t], i] | bf16 sin[seqpos[t], i] << 16
  * for the rot / 2 distinct pairs i (tables from kd_rope_table). One gather per pack and rotary kind. */
 int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab, int rot,
