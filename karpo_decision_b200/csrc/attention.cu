@@ -72,7 +72,7 @@ KD_DEVICE float fast_exp2(float x) {
 template <int HD>
 __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
-                     const __grid_constant__ CUtensorMap map_v, Args a) {
+                     const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_g, Args a) {
   using C = Cfg<HD>;
   constexpr int BM = C::BM, BN = C::BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -87,7 +87,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
   uint64_t* s_full = kv_empty + C::STAGES;      // [2]
   uint64_t* p_full = s_full + 2;                // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(pv_done + 2);
+  uint64_t* q_free = pv_done + 2;              // the last S has read Q: its buffer takes the gate tile
+  uint64_t* g_full = q_free + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
 
   // ---- this CTA's (sequence, query tile), numbered sequence by sequence from the device bounds
   int tile = blockIdx.x;
@@ -131,6 +133,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
       mbar_init(&p_full[b], 128);
       mbar_init(&pv_done[b], 1);
     }
+    mbar_init(q_free, 1);
+    mbar_init(g_full, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -163,6 +167,14 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
         mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
         for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + c * 64, row);
       }
+      if (a.gate) {
+        // Qwen's output gate tile, into the Q buffer once the last S = Q K^T has read it: the epilogue then reads
+        // its row from shared memory instead of scattered global loads.
+        if (!mbar_wait(q_free, 0, a.status)) goto done;
+        mbar_arrive_expect_tx(g_full, C::Q_BYTES);
+        for (int c = 0; c < C::CHUNKS; ++c)
+          tma_load_2d(&map_g, g_full, s_q + c * C::Q_CHUNK, head * HD + c * 64, q0 + qs);
+      }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
@@ -184,6 +196,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
                      idesc_s, kk > 0);
         }
         mma_commit(&s_full[j & 1]);
+        if (j == n_tiles - 1) mma_commit(q_free);  // Q is free once the last S has completed
         return true;
       };
       if (!issue_s(0)) goto done;
@@ -294,10 +307,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
       if (!mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, a.status)) goto done;
       tc_fence_after();
     }
+    // The gate tile sits in the Q buffer (128-byte swizzled rows); without visible keys the output is 0 and needs
+    // no gate.
+    const bool gated = a.gate != nullptr && n_tiles > 0;
+    if (gated && !mbar_wait(g_full, 0, a.status)) goto done;
     const int row = qs + r;
     const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
     __nv_bfloat16* orow = a.out + (int64_t)(q0 + row) * a.ldo + (int64_t)head * HD;
-    const __nv_bfloat16* grow = a.gate ? a.gate + (int64_t)(q0 + row) * a.ldg + (int64_t)head * HD : nullptr;
 #pragma unroll 1
     for (int c = 0; c < HD; c += 32) {
       uint32_t t[32];
@@ -309,13 +325,25 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
         for (int e = 0; e < 32; ++e) t[e] = 0u;
       }
       if (row < lq) {
+        uint32_t gw[16];
+        if (gated) {  // this row's 32 gate values: four 16-byte pieces of its swizzled 128-byte row
+          const uint8_t* grow = s_q + (c / 64) * C::Q_CHUNK + r * 128;
+#pragma unroll
+          for (int k4 = 0; k4 < 4; ++k4) {
+            const uint4 g4 = *reinterpret_cast<const uint4*>(grow + ((((c % 64) / 8 + k4) ^ (r & 7)) << 4));
+            gw[4 * k4] = g4.x;
+            gw[4 * k4 + 1] = g4.y;
+            gw[4 * k4 + 2] = g4.z;
+            gw[4 * k4 + 3] = g4.w;
+          }
+        }
         uint32_t packed[16];
 #pragma unroll
         for (int e = 0; e < 16; ++e) {
           float v0 = bf16_round(__uint_as_float(t[2 * e]) * inv);
           float v1 = bf16_round(__uint_as_float(t[2 * e + 1]) * inv);
-          if (grow) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
-            const float2 gv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(grow + c + 2 * e));
+          if (gated) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
+            const float2 gv = unpack_bf16x2(gw[e]);
             v0 *= sigmoid(gv.x);
             v1 *= sigmoid(gv.y);
           }
@@ -350,6 +378,10 @@ int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v
                             CU_TENSOR_MAP_SWIZZLE_128B);
   if (!rc) rc = make_tma_2d(&mv, v, dt, 2, (uint64_t)ldv, (uint64_t)tk, (uint64_t)ldv, 64, C::BN,
                             CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap mg = mq;  // the gate tile has the Q tile's shape (unused without a gate)
+  if (!rc && a.gate)
+    rc = make_tma_2d(&mg, a.gate, dt, 2, (uint64_t)a.ldg, (uint64_t)tq, (uint64_t)a.ldg, 64, C::BM,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
   auto kernel = attention_kernel<HD>;
   static bool configured[64] = {false};
@@ -365,7 +397,7 @@ int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v
   const int64_t tiles = total_q / C::BM + a.num_seqs;
   if (tiles > 0x7fffffff) return set_error(KD_ERR_ARGUMENT, "attention: too many query tiles");
   dim3 grid((unsigned)tiles, (unsigned)a.hq);
-  kernel<<<grid, THREADS, C::SMEM, stream>>>(mq, mk, mv, a);
+  kernel<<<grid, THREADS, C::SMEM, stream>>>(mq, mk, mv, mg, a);
   return record_cuda_error(cudaGetLastError(), "attention: launch");
 }
 
