@@ -71,6 +71,9 @@ def dist_env() -> tuple[int, int, int]:
 # ------------------------------------------------------------------------------------------------ CPU baseline
 
 
+_CPU_WEIGHTS: dict = {}
+
+
 def cpu_sample_rate(config: str, seconds: float, fp8: bool = False) -> dict:
     """The reference algorithm on the host cores (the oracle port, float32, all BLAS threads): packs of a few short
     sequences of the same model until about ``seconds`` of CPU work; returns tokens/s and what the sample was."""
@@ -78,7 +81,9 @@ def cpu_sample_rate(config: str, seconds: float, fp8: bool = False) -> dict:
     from karpo_decision_b200.synthetic import CONFIGS, numpy_weights, synthetic_lengths, synthetic_pack_arrays
 
     spec = CONFIGS[config]
-    weights = numpy_weights(spec, 0)
+    if config not in _CPU_WEIGHTS:  # drawn once per process: a full-size draw takes seconds
+        _CPU_WEIGHTS[config] = numpy_weights(spec, 0)
+    weights = _CPU_WEIGHTS[config]
     forward = oracle.qwen_forward if spec.family == "qwen" else oracle.gemma_forward
     tokens_done, elapsed, packs = 0, 0.0, 0
     seed = 100

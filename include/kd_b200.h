@@ -166,6 +166,12 @@ int kd_attention_varlen(const void* q, int64_t ldq, const void* k, int64_t ldk, 
                         int num_heads_kv, int head_dim, float scale, int window_left, int window_right, int* status,
                         cudaStream_t stream);
 
+/* dst[i, :] = src[rows[i], :] for n bf16 rows of `width` elements (width % 8 == 0): the key and value rows of a
+ * branched block layout's virtual sequences (the shared block, or its last window - 1 rows, then the branch).
+ * Replaces _gather / index_select in families/gemma/packed.py:222-226. */
+int kd_gather_rows(const void* src, int64_t ld_src, const int64_t* rows, int64_t n, int width, void* dst,
+                   int64_t ld_dst, cudaStream_t stream);
+
 /* The head: out[m, :] = norm(h[markers[m], :]) (final norm at the readout markers).
  * Replaces families/qwen/packed.py:173-176 and families/gemma/packed.py:297-303. */
 int kd_marker_norm(const void* h, int hidden, const int64_t* markers, int64_t M, const void* weight, int norm_mode,

@@ -42,6 +42,7 @@ SIGNATURES: dict[str, list] = {
                          c_int, P, P, P, P, P],
     "kd_attention_varlen": [P, c_int64, P, c_int64, P, c_int64, P, c_int64, P, c_int64, P, P, c_int, c_int, c_int64,
                             c_int64, c_int, c_int, c_int, c_float, c_int, c_int, P, P],
+    "kd_gather_rows": [P, c_int64, P, c_int64, c_int, P, c_int64, P],
     "kd_marker_norm": [P, c_int, P, c_int64, P, c_int, c_float, P, P],
     "kd_readout": [P, c_int64, c_int, P, c_int, c_float, P, P],
 }

@@ -4,13 +4,14 @@ stream. Each op is one entry point of libkd_b200; none has a fallback.
 
 from __future__ import annotations
 
+import numpy as np
 import torch
 
 from . import _lib
 from ._lib import EPI_GEGLU, EPI_RESIDUAL, EPI_STORE, EPI_SWIGLU, NORM_NONE, NORM_ONE_PLUS, NORM_WEIGHT, call
 
 __all__ = ["EPI_GEGLU", "EPI_RESIDUAL", "EPI_STORE", "EPI_SWIGLU", "NORM_NONE", "NORM_ONE_PLUS", "NORM_WEIGHT",
-           "add_rmsnorm", "attention_varlen", "check_status", "embed", "gemm", "gemm_fp8", "marker_norm",
+           "add_rmsnorm", "attention_varlen", "check_status", "embed", "gather_rows", "gemm", "gemm_fp8", "marker_norm",
            "norm_add", "qkv_norm_rope", "qkv_projection", "quantize_rows_e4m3", "readout", "rmsnorm", "rmsnorm_e4m3",
            "rope_gather", "rope_table",
            "status_word"]
@@ -289,3 +290,15 @@ def qkv_projection(a: torch.Tensor, w: torch.Tensor, seqpos: torch.Tensor, heads
         call("kd_qkv_projection_fp8", a.data_ptr(), a.stride(0), scale_a.data_ptr(), w.data_ptr(), w.stride(0),
              scale_w.data_ptr(), t, w.shape[0], a.shape[1], *tail)
     return q, k, v, gate
+
+
+def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``src[rows]`` for bf16 rows (src (T, ...) with contiguous rows; rows int64 on the device)."""
+    _require(src.dtype == torch.bfloat16 and src.is_contiguous(), "gather_rows: contiguous bf16 source")
+    _require(rows.dtype == torch.int64 and rows.is_contiguous(), "gather_rows: contiguous int64 rows")
+    width = src[0].numel() if src.shape[0] else int(np.prod(src.shape[1:]))
+    n = rows.numel()
+    if out is None:
+        out = torch.empty((n, *src.shape[1:]), dtype=src.dtype, device=src.device)
+    call("kd_gather_rows", src.data_ptr(), width, rows.data_ptr(), n, width, out.data_ptr(), width, _stream(src))
+    return out

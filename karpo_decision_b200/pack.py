@@ -68,7 +68,8 @@ def pack(sequences: Sequence[Any], device: torch.device, blocks: bool = False) -
 
 def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: bool = False) -> Pack:
     """A pack from host arrays (``synthetic.synthetic_pack_arrays`` layout: input_ids, seqpos, cu, markers,
-    marker_cu); ``pinned`` stages them in page-locked memory so the copies are asynchronous."""
+    marker_cu, and segment_ids for block layouts); ``pinned`` stages them in page-locked memory so the copies are
+    asynchronous."""
 
     def host(a, dtype):
         t = torch.from_numpy(np.ascontiguousarray(a)).to(dtype)
@@ -77,6 +78,8 @@ def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: boo
     cu = arrays["cu"]
     lengths = np.diff(cu)
     counts = np.diff(arrays["marker_cu"])
+    segments = arrays.get("segment_ids")
+    seg_cpu = None if segments is None else torch.from_numpy(np.asarray(segments, dtype=np.int32))
     return Pack(
         input_ids=host(arrays["input_ids"], torch.int64).to(device, non_blocking=True),
         seqpos=host(arrays["seqpos"], torch.int64).to(device, non_blocking=True),
@@ -86,4 +89,6 @@ def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: boo
         markers=host(arrays["markers"], torch.int64).to(device, non_blocking=True),
         marker_cu=host(arrays["marker_cu"], torch.int32).to(device, non_blocking=True),
         max_markers=int(counts.max()),
+        segment_ids=None if seg_cpu is None else seg_cpu.to(device, non_blocking=True),
+        segment_ids_cpu=seg_cpu,
     )

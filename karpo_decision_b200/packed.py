@@ -32,6 +32,7 @@ import numpy as np
 import torch
 
 from . import ops
+from .plan import block_plan
 from .synthetic import Spec
 
 #: Qwen's FP8 path keeps projections with fewer outputs in bf16 (serve/qwen_fp8.py:17).
@@ -300,8 +301,12 @@ class Packed(torch.nn.Module):
     def forward(self, p: Any) -> torch.Tensor:
         """(M, hidden) final-normalized hidden states at the markers, in pack order."""
         s = self.spec
+        plan = None
         if p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
-            raise NotImplementedError("branched block layouts (a shared block and branches) are not built yet")
+            if s.family != "gemma":  # families/qwen/packed.py:180-181
+                raise ValueError("the Qwen family reads joint layouts, not block layouts")
+            # branched block layouts: virtual sequences with gathered keys, planned once before any layer is queued
+            plan = block_plan(p.cu_cpu, p.segment_ids_cpu, self.window, self.device)
         t = int(p.input_ids.numel())
         ws = self.workspace(t)
         n_seqs = int(p.cu.numel()) - 1
@@ -311,9 +316,7 @@ class Packed(torch.nn.Module):
         eps = s.eps
         h = ops.embed(p.input_ids, self.embed_tokens, 0.0 if qwen else math.sqrt(s.hidden), out=ws.h[:t])
         seqpos = p.seqpos if p.seqpos.dtype == torch.int64 else p.seqpos.long()
-        positions = int(max_len)
-        if p.segment_ids_cpu is not None:  # block layouts carry their own positions
-            positions = max(positions, int(seqpos.max().item()) + 1)
+        positions = int(max_len)  # a position (block layouts included) is below its sequence's length
         rope_cs: dict[str, torch.Tensor] = {}  # per rotary kind, gathered once per pack
         for layer in self.layers:
             fp8_qkv = any(proj.fp8 for proj, _, _ in layer.qkv)
@@ -343,7 +346,14 @@ class Packed(torch.nn.Module):
             else:
                 window = (-1, 0)
             scale = s.head_dim ** -0.5 if qwen else 1.0
-            o = ops.attention_varlen(q, k, v, p.cu, p.cu, max_len, scale, window, gate=gate, out=ws.o[:t])
+            if plan is None:
+                o = ops.attention_varlen(q, k, v, p.cu, p.cu, max_len, scale, window, gate=gate, out=ws.o[:t])
+            else:  # each virtual sequence's keys: the shared block (or its window tail), then its own rows
+                rows, k_cu = (plan.s_rows, plan.s_cu) if layer.kind == "sliding_attention" else \
+                    (plan.g_rows, plan.g_cu)
+                kg, vg = ops.gather_rows(k, rows), ops.gather_rows(v, rows)
+                o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, scale, window, gate=gate,
+                                         out=ws.o[:t])
             o8 = self._quantized(ws, o) if layer.o.fp8 else None
             if qwen:
                 self._project(layer.o, o, o8, h, ops.EPI_RESIDUAL, residual=h)  # h += o W_o^T

@@ -211,3 +211,40 @@ def synthetic_pack_arrays(lengths: list[int], vocab: int, seed: int, markers_per
 def small(spec: Spec, **changes) -> Spec:
     """``spec`` with some fields changed (test-sized variants)."""
     return replace(spec, **changes)
+
+
+def synthetic_block_arrays(layouts: list[tuple[int, list[int]]], vocab: int, seed: int) -> dict[str, np.ndarray]:
+    """A pack of block layouts (the reference's blocks.py:194-214): per sequence ``(shared, branches)``. A sequence
+    without branches is one block: positions 0..n-1, segment 0, one marker at its last token. With branches, the
+    shared block (segment 0, positions 0..shared-1) is followed by branch k (segment k, positions restarting at
+    ``shared``), and each branch's last token is a marker."""
+    rng = np.random.default_rng(seed)
+    ids, pos, seg, markers, counts, cu = [], [], [], [], [], [0]
+    for shared, branches in layouts:
+        start = cu[-1]
+        if not branches:
+            pos.append(np.arange(shared))
+            seg.append(np.zeros(shared, dtype=np.int64))
+            markers.append(np.array([start + shared - 1]))
+            counts.append(1)
+            n = shared
+        else:
+            p, s, m, at = [np.arange(shared)], [np.zeros(shared, dtype=np.int64)], [], shared
+            for k, length in enumerate(branches, start=1):
+                p.append(np.arange(shared, shared + length))
+                s.append(np.full(length, k, dtype=np.int64))
+                at += length
+                m.append(start + at - 1)
+            pos.append(np.concatenate(p))
+            seg.append(np.concatenate(s))
+            markers.append(np.array(m))
+            counts.append(len(branches))
+            n = at
+        ids.append(rng.integers(0, vocab, size=n, dtype=np.int64))
+        cu.append(start + n)
+    return {
+        "input_ids": np.concatenate(ids), "seqpos": np.concatenate(pos).astype(np.int64),
+        "segment_ids": np.concatenate(seg), "cu": np.array(cu, dtype=np.int64),
+        "markers": np.concatenate(markers).astype(np.int64),
+        "marker_cu": np.concatenate([[0], np.cumsum(counts)]).astype(np.int64),
+    }

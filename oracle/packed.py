@@ -243,9 +243,42 @@ def gemma_layer_types(spec: dict) -> list[str]:
     return ["full_attention" if (i + 1) % every == 0 or i == n - 1 else "sliding_attention" for i in range(n)]
 
 
+def block_plan(cu: np.ndarray, segment_ids: np.ndarray, window: int) -> dict:
+    """The virtual sequences of a pack of block layouts (families/gemma/packed.py:103-151): per sequence its shared
+    block (queries and keys: the shared rows), then each branch (queries: the branch rows; keys: the whole shared block
+    then the branch rows for global layers, the shared block's last window - 1 rows then the branch rows for sliding
+    layers). Returns query bounds and, per layer kind, the key rows gathered in order with their bounds."""
+    q_cu, g_rows, g_cu, s_rows, s_cu = [0], [], [0], [], [0]
+    for a, b in zip(cu[:-1].tolist(), cu[1:].tolist(), strict=True):
+        seg = np.asarray(segment_ids[a:b])
+        change = (np.flatnonzero(seg[1:] != seg[:-1]) + 1).tolist()
+        starts, ends = [0, *change], [*change, b - a]
+        labels = [int(seg[i]) for i in starts]
+        if labels != list(range(len(labels))):
+            raise ValueError(f"segments {labels} are not a shared block followed by branches 1, 2, ...")
+        shared = ends[0]
+        own = np.arange(a, a + shared)
+        tail = own[max(0, shared - (window - 1)):]
+        q_cu.append(a + shared)
+        g_rows.append(own)
+        s_rows.append(own)
+        g_cu.append(g_cu[-1] + shared)
+        s_cu.append(s_cu[-1] + shared)
+        for start, end in zip(starts[1:], ends[1:], strict=True):
+            rows = np.arange(a + start, a + end)
+            q_cu.append(a + end)
+            g_rows.append(np.concatenate([own, rows]))
+            s_rows.append(np.concatenate([tail, rows]))
+            g_cu.append(g_cu[-1] + shared + len(rows))
+            s_cu.append(s_cu[-1] + len(tail) + len(rows))
+    return {"q_cu": np.array(q_cu), "g_rows": np.concatenate(g_rows), "g_cu": np.array(g_cu),
+            "s_rows": np.concatenate(s_rows), "s_cu": np.array(s_cu)}
+
+
 def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8: bool = False) -> np.ndarray:
     """(M, hidden) at the markers: families/gemma/packed.py:305-323 over single-block sequences (each virtual sequence
-    is a whole sequence: ``block_plan`` :103-151 without branches). Layer :262-265: attention :228-254 (q/k norm +
+    is a whole sequence) or over block layouts with branches (``block_plan`` :103-151, virtual sequences whose keys
+    are gathered: ``block_plan`` below). Layer :262-265: attention :228-254 (q/k norm +
     RoPE, v norm without weight, scale 1.0; sliding layers window (W-1, 0) :171, global layers causal), residual
     ``h + norm(attn)`` (fused.py:29-30), MLP ``norm(down(gelu_tanh(gate z) * up z))`` with z = norm(h) (:258-260),
     ``(h + mlp) * layer_scalar`` (fused.py:33-34). Embeddings scaled by bf16(sqrt(hidden)) (:283-285). With ``fp8``,
@@ -266,6 +299,8 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
         "full_attention": rope_tables(seqpos, hd, spec["rope_theta"], 1.0, mode),
     }
     causal_global = spec.get("attention", "causal") == "causal"
+    segs = pack.get("segment_ids")
+    plan = block_plan(cu, segs, w_len) if segs is not None and np.any(segs != 0) else None
 
     def normed(x, w):  # the norm (and, for fp8, the quantization fused into it: serve/fp8.py:57-69, :92-99)
         y = _round(rms_norm(x, w, eps, False), mode)
@@ -285,7 +320,13 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
             window = (w_len - 1, 0)
         else:
             window = (-1, 0) if causal_global else (-1, -1)
-        o = _round(attention_varlen(q, k, v, cu, cu, 1.0, window), mode).reshape(t, hq * hd)
+        if plan is None:
+            o = attention_varlen(q, k, v, cu, cu, 1.0, window)
+        else:  # branched layouts: per virtual sequence, its gathered keys (end-aligned with its queries)
+            rows, k_cu = (plan["s_rows"], plan["s_cu"]) if types[i] == "sliding_attention" else \
+                (plan["g_rows"], plan["g_cu"])
+            o = attention_varlen(q, k[rows], v[rows], plan["q_cu"], k_cu, 1.0, window)
+        o = _round(o, mode).reshape(t, hq * hd)
         a = linear(o, weights[p + "o_proj"], mode, fp8)
         h = _round(h + rms_norm(a, weights[p + "post_attention_layernorm"], eps, False), mode)
         z, zq = normed(h, weights[p + "pre_feedforward_layernorm"])

@@ -36,7 +36,8 @@ import torch.nn.functional as F
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 
-from karpo_decision_b200.synthetic import CONFIGS, Spec, numpy_weights, small, synthetic_pack_arrays  # noqa: E402
+from karpo_decision_b200.synthetic import (  # noqa: E402
+    CONFIGS, Spec, numpy_weights, small, synthetic_block_arrays, synthetic_pack_arrays)
 
 
 def varlen_contract(q, k, v, cu_q, cu_k, max_q, max_k, scale=None, window_size=(-1, -1), enable_gqa=False):
@@ -166,7 +167,10 @@ def encoded(arrays: dict[str, np.ndarray], blocks: bool):
         local = torch.from_numpy(markers[mcu[s]:mcu[s + 1]] - a)
         n = b - a
         kw = {}
-        if blocks:
+        if blocks and "segment_ids" in arrays:  # block layouts with branches (synthetic_block_arrays)
+            kw = dict(positions=torch.from_numpy(arrays["seqpos"][a:b].copy()),
+                      segment_ids=torch.from_numpy(arrays["segment_ids"][a:b].astype(np.int16)))
+        elif blocks:
             kw = dict(positions=torch.arange(n), segment_ids=torch.zeros(n, dtype=torch.int16))
         out.append(Encoded(keys=tuple(f"q{i}" for i in range(len(local))), counts=(3,) * len(local),
                            input_ids=torch.from_numpy(arrays["input_ids"][a:b].copy()), markers=local, **kw))
@@ -192,6 +196,11 @@ CASES = {
                        lengths=("uniform", 6, 8, 96), markers=(1, 1), fp8=False),
     # FP8 projections (serve/qwen_fp8.py and serve/fp8.py).
     "qwen_tiny_fp8": dict(spec=CONFIGS["tiny"], lengths=("uniform", 4, 32, 160), markers=(1, 2), fp8=True),
+    # Branched block layouts (blocks.py:194-214): shared blocks one short of, at and past the window, branches longer
+    # than the window, single-block sequences beside branched ones (the reference's tests/test_gemma_blocks.py PACKS).
+    "gemma_blocks": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
+                         blocks=[(23, []), (21, [5, 7, 3]), (14, [4, 9]), (15, [3]), (16, [6, 2]),
+                                 (17, [10, 1, 4]), (3, [20, 25])], fp8=False),
     "gemma_tiny_fp8": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
                            lengths=("uniform", 4, 8, 96), markers=(1, 1), fp8=True),
 }
@@ -237,10 +246,13 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
 
     spec: Spec = case["spec"]
     weights = numpy_weights(spec, seed)
-    kind, n, low, high = case["lengths"]
-    rng = np.random.default_rng(seed)
-    lengths = [int(x) for x in rng.integers(low, high + 1, size=n)]
-    arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, case["markers"])
+    if "blocks" in case:
+        arrays = synthetic_block_arrays(case["blocks"], spec.vocab, seed + 1)
+    else:
+        kind, n, low, high = case["lengths"]
+        rng = np.random.default_rng(seed)
+        lengths = [int(x) for x in rng.integers(low, high + 1, size=n)]
+        arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, case["markers"])
     seqs = encoded(arrays, blocks=spec.family == "gemma")
     head = Readout.from_rows(to_torch(weights, "readout"), cap=spec.logit_cap)
     captured: dict = {}
@@ -281,8 +293,9 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
     pins = {}
     for proj, (values, scale, out) in captured.items():
         pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
+    extra = {"segment_ids": arrays["segment_ids"]} if "segment_ids" in arrays else {}
     return {
-        **pins,
+        **pins, **extra,
         "input_ids": arrays["input_ids"], "seqpos": arrays["seqpos"], "cu": arrays["cu"],
         "markers": arrays["markers"], "marker_cu": arrays["marker_cu"],
         "hidden": hidden.float().numpy(), "logits": logits.float().numpy(),

@@ -11,7 +11,7 @@ import numpy as np
 from karpo_decision_b200.synthetic import Spec, numpy_weights
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
-CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "qwen_tiny_fp8", "gemma_tiny_fp8"]
+CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_tiny_fp8", "gemma_tiny_fp8"]
 
 
 def load(name: str) -> tuple[Spec, dict, dict, dict]:
@@ -26,6 +26,6 @@ def load(name: str) -> tuple[Spec, dict, dict, dict]:
         h.update(np.ascontiguousarray(weights[key], dtype=np.float32).tobytes())
     if h.hexdigest() != str(z["weights_sha256"]):
         raise AssertionError(f"{name}: regenerated weights differ from the ones the fixture was made with")
-    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu")}
+    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu", "segment_ids") if k in z.files}
     expected = {"hidden": z["hidden"], "logits": z["logits"]}
     return spec, weights, pack, expected

@@ -311,3 +311,10 @@ def test_qkv_projection_equals_gemm_then_norm_rope(family, hd, partial, fp8):
         diff = (a_.float() - b_.float()).abs().max().item()
         assert diff <= 2 ** -7 * max(b_.float().abs().max().item(), 1.0), diff
     ops.check_status(DEV)
+
+
+def test_gather_rows():
+    g = rng(14)
+    src = bf16(g.standard_normal((300, 8, 64)))
+    rows = torch.from_numpy(g.integers(0, 300, 517)).to(DEV)
+    assert torch.equal(ops.gather_rows(src, rows), src[rows])

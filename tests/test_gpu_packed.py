@@ -32,7 +32,7 @@ def run_b200(name):
     return spec, weights, arrays, expected, hidden.float().cpu().numpy(), logits.cpu().numpy()
 
 
-@pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny"])
+@pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks"])
 def test_bf16_forward_matches_reference(name):
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
     assert hidden.shape == expected["hidden"].shape
@@ -49,7 +49,7 @@ def test_bf16_forward_matches_reference(name):
     assert cosine.min() > 0.995, cosine
 
 
-@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny"])
+@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "gemma_blocks"])
 def test_bf16_forward_tracks_bf16_oracle(name):
     """Against the oracle with the reference's bf16 rounding points: closer than to the float32 reference."""
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
@@ -81,3 +81,21 @@ def test_pack_composition_does_not_change_a_sequence():
     }
     one = model(from_arrays(alone, DEV)).float()
     assert torch.allclose(full[mcu[2]:mcu[3]], one, atol=2e-2, rtol=2e-2)
+
+
+def test_a_branch_never_sees_another():
+    """Changing one branch's tokens leaves the shared block's and the other branches' readouts as they were (the
+    reference's tests/test_gemma_blocks.py test_a_branch_never_sees_another)."""
+    from karpo_decision_b200.synthetic import synthetic_block_arrays
+
+    spec, weights, _, _ = load("gemma_blocks")
+    model = Packed(spec, weights, DEV)
+    arrays = synthetic_block_arrays([(30, [12, 20, 9])], spec.vocab, seed=5)
+    base = model(from_arrays(arrays, DEV)).float()
+    changed = dict(arrays)
+    ids = arrays["input_ids"].copy()
+    ids[30 + 12:30 + 12 + 20] = (ids[30 + 12:30 + 12 + 20] + 7) % spec.vocab  # the second branch
+    changed["input_ids"] = ids
+    other = model(from_arrays(changed, DEV)).float()
+    assert torch.equal(base[0], other[0]) and torch.equal(base[2], other[2])
+    assert not torch.equal(base[1], other[1])

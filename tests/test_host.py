@@ -72,3 +72,26 @@ def test_numpy_weights_are_bf16_exact_and_seeded():
         assert np.array_equal(a[key], b[key])
     w = a["layers.0.q_proj"]
     assert np.array_equal(torch.from_numpy(w).bfloat16().float().numpy(), w)
+
+
+def test_block_plan_matches_oracle_and_refuses_bad_segments():
+    import pytest
+
+    import oracle
+    from karpo_decision_b200.plan import block_plan
+    from karpo_decision_b200.synthetic import synthetic_block_arrays
+
+    arrays = synthetic_block_arrays([(5, []), (6, [2, 3]), (2, [4])], 50, seed=0)
+    cu, seg = torch.from_numpy(arrays["cu"]), torch.from_numpy(arrays["segment_ids"])
+    plan = block_plan(cu, seg, window=4, device=torch.device("cpu"))
+    want = oracle.packed.block_plan(arrays["cu"], arrays["segment_ids"], 4)
+    assert plan.q_cu.tolist() == want["q_cu"].tolist() == [0, 5, 11, 13, 16, 18, 22]
+    assert plan.g_rows.tolist() == want["g_rows"].tolist()
+    assert plan.s_rows.tolist() == want["s_rows"].tolist()
+    # the second sequence's first branch sees its whole shared block globally, its last 3 rows in sliding layers
+    assert plan.g_rows[11:19].tolist() == [5, 6, 7, 8, 9, 10, 11, 12]
+    assert plan.s_rows[11:16].tolist() == [8, 9, 10, 11, 12]
+    bad = seg.clone()
+    bad[5:11] = 1  # a sequence starting with branch 1 has no shared block
+    with pytest.raises(ValueError):
+        block_plan(cu, bad, 4, torch.device("cpu"))
