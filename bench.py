@@ -49,6 +49,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--fp8", action="store_true")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="target CPU time of the baseline sample")
+    ap.add_argument("--graphs", action="store_true", help="time the CUDA-graph path (one bucket at the pack size)")
+    ap.add_argument("--requests", type=int, default=16, help="single requests timed for the latency figures")
     ap.add_argument("--tokens", type=int, default=0, help="tokens per pack (default: the configuration's; smaller "
                                                           "packs are for profiling captures)")
     return ap.parse_args()
@@ -140,6 +142,7 @@ def config_block(args: argparse.Namespace, world: int) -> dict:
                         f"{'log-uniform' if log else 'uniform'} [{low},{high}], 1-4 markers/sequence, causal"
                         + (", FP8 projections" if args.fp8 else ""),
             "tokens_per_pack": tokens, "parallelism": f"replicas x{world}",
+            "path": "graphs" if getattr(args, "graphs", False) else "plain",
             "l2": "working set (weights and per-layer activations) larger than L2 between steps"}
 
 
@@ -231,8 +234,14 @@ def run_ours(args: argparse.Namespace) -> None:
     p = from_arrays(arrays, dev)
     torch.cuda.synchronize()
 
+    forward = model
+    if args.graphs:
+        from karpo_decision_b200.graphs import Graphs
+
+        forward = Graphs(model, buckets=(tokens,), max_sequences=len(arrays["cu"]) + 8)
+
     def step():
-        return head(model(p))
+        return head(forward(p))
 
     def barrier():
         if group is not None:
@@ -264,7 +273,7 @@ def run_ours(args: argparse.Namespace) -> None:
 
     def e2e_step():
         q = from_pinned(pinned, dev, arrays)
-        logits = head(model(q))
+        logits = head(forward(q))
         out_host.copy_(logits, non_blocking=True)
 
     for _ in range(2):
@@ -324,11 +333,50 @@ def run_ours(args: argparse.Namespace) -> None:
             "kernel_shares": prof.shares(),
             "clocks": clocks.summary(),
         }
+        if args.requests > 0:
+            line["latency"] = request_latency(model, head, args, dev, args.requests)
         if world == 1 and os.environ.get("KD_BENCH_NO_CPU") != "1":
             line["cpu_baseline"] = cpu_sample_rate(args.config, args.cpu_seconds, args.fp8)
         print(json.dumps(line), flush=True)
     if group is not None:
         group.destroy_process_group()
+
+
+def request_latency(model, head, args, dev, n: int) -> dict:
+    """Per-request latency of single requests (one sequence each, length drawn from the configuration's range,
+    1-4 questions): pinned host pack -> device -> forward -> readout -> host logits, device-synchronized wall time
+    per request (the reference's latency definition, serve/engine.py:53-55, from the packed pass on), on the plain
+    path and on the CUDA-graph path (buckets of powers of two up to the longest request)."""
+    import torch
+
+    from karpo_decision_b200.graphs import Graphs
+    from karpo_decision_b200.synthetic import CONFIGS, synthetic_lengths, synthetic_pack_arrays
+
+    spec = CONFIGS[args.config]
+    _, (low, high), log = WORKLOADS[args.config]
+    rng = np.random.default_rng(7)
+    requests = []
+    for i in range(n):
+        length = synthetic_lengths(high, low, high, seed=int(rng.integers(1 << 30)), log_uniform=log)[0]
+        requests.append(synthetic_pack_arrays([length], spec.vocab, seed=i, markers_per_seq=(1, 4)))
+    longest = max(len(r["input_ids"]) for r in requests)
+    buckets = tuple(1 << k for k in range(7, max(8, int(np.ceil(np.log2(longest)))) + 1))
+    graphs = Graphs(model, buckets=buckets, max_sequences=1)
+    out = {"requests": n, "lengths": f"one sequence each, {'log-uniform' if log else 'uniform'} [{low},{high}]"}
+    for name, fwd in (("plain", model), ("graphs", graphs)):
+        times = []
+        for arrays in requests + requests[:2]:  # the first two again: warm-up excluded below
+            pinned = {k: torch.from_numpy(np.ascontiguousarray(v)).pin_memory() for k, v in arrays.items()}
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            logits = head(fwd(from_pinned(pinned, dev, arrays))).cpu()
+            torch.cuda.synchronize()
+            times.append((time.perf_counter() - t0) * 1000.0)
+            del logits
+        times = times[2:]
+        out[name] = {"p50_ms": round(float(np.median(times)), 3), "mean_ms": round(float(np.mean(times)), 3)}
+    graphs.release()
+    return out
 
 
 def attention_flops(spec, lengths) -> float:

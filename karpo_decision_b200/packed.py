@@ -300,6 +300,17 @@ class Packed(torch.nn.Module):
 
     def forward(self, p: Any) -> torch.Tensor:
         """(M, hidden) final-normalized hidden states at the markers, in pack order."""
+        return self.head(self.body(p), p)
+
+    def head(self, h: torch.Tensor, p: Any) -> torch.Tensor:
+        """(M, hidden): the final norm of the body's output at the markers (families/qwen/packed.py:173-176,
+        families/gemma/packed.py:297-303)."""
+        mode = ops.NORM_ONE_PLUS if self.spec.family == "qwen" else ops.NORM_WEIGHT
+        return ops.marker_norm(h, p.markers, self.norm, mode, self.spec.eps)
+
+    def body(self, p: Any) -> torch.Tensor:
+        """(T, hidden) hidden states after every layer (the workspace's residual buffer): embedding and layers, no
+        host synchronization, so it can be captured in a CUDA graph when ``p``'s tensors are static."""
         s = self.spec
         plan = None
         if p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
@@ -371,7 +382,7 @@ class Packed(torch.nn.Module):
                 m8 = self._quantized(ws, m) if layer.down.fp8 else None
                 d = self._project(layer.down, m, m8, ws.a[:t])
                 ops.norm_add(h, d, layer.post_feedforward_norm, mode, eps, scalar=layer.scalar, out=h)
-        return ops.marker_norm(h, p.markers, self.norm, mode, eps)
+        return h
 
 
 class Readout(torch.nn.Module):
