@@ -287,12 +287,7 @@ def run_ours(args: argparse.Namespace) -> None:
     torch.cuda.synchronize()
     e2e_ms = e0.elapsed_time(e1) / args.steps
 
-    times = torch.tensor([ms, e2e_ms], device=dev)
-    if group is not None:
-        group.all_reduce(times, op=group.ReduceOp.MAX)
-    ms, e2e_ms = times.tolist()
-    value = tokens * world / (ms / 1000.0)
-    e2e_value = tokens * world / (e2e_ms / 1000.0)
+    ms, e2e_ms, value, e2e_value = aggregate([ms, e2e_ms], tokens, world, dev, group)
 
     if rank == 0:
         peaks = peak_numbers()
@@ -340,6 +335,18 @@ def run_ours(args: argparse.Namespace) -> None:
         print(json.dumps(line), flush=True)
     if group is not None:
         group.destroy_process_group()
+
+
+def aggregate(times_ms: list[float], tokens: int, world: int, device, group=None) -> tuple[float, float, float, float]:
+    """The slowest rank's device times (a MAX all-reduce over the ranks; identity on one rank) and the whole-job
+    throughputs: every rank processed ``tokens`` per step, so tokens * world / slowest time."""
+    import torch
+
+    t = torch.tensor(times_ms, dtype=torch.float64, device=device)
+    if group is not None and world > 1:
+        group.all_reduce(t, op=group.ReduceOp.MAX)
+    ms, e2e_ms = t.tolist()
+    return ms, e2e_ms, tokens * world / (ms / 1000.0), tokens * world / (e2e_ms / 1000.0)
 
 
 def request_latency(model, head, args, dev, n: int) -> dict:
