@@ -117,6 +117,21 @@ KD_DEVICE void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int
       : "memory");
 }
 
+// 2-D tiled store of a shared-memory box to (x, y) of the tensor; rows and columns past the tensor are clipped.
+KD_DEVICE void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(smem_u32(src)), "r"(x), "r"(y)
+               : "memory");
+}
+KD_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until this thread's committed bulk stores have finished reading shared memory (the buffer is reusable).
+KD_DEVICE void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until this thread's committed bulk stores have completed.
+KD_DEVICE void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads of them.
+KD_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // ------------------------------------------------------------------------------------------------ tcgen05
 
 // Shared-memory matrix descriptor of a K-major operand tile stored as TMA writes it with 128-byte swizzling: rows of
@@ -284,17 +299,21 @@ KD_DEVICE float2 unpack_bf16x2(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
-// silu(x) = x * sigmoid(x), with the exact exponential of the CUDA math library.
-KD_DEVICE float silu(float x) { return x / (1.0f + expf(-x)); }
+// x * sigmoid(z) with the fast exponential and approximate division (relative error ~1e-6, far below the bf16
+// rounding every caller applies to the product).
+KD_DEVICE float x_sigmoid(float x, float z) { return __fdividef(x, 1.0f + __expf(-z)); }
 
-KD_DEVICE float sigmoid(float x) { return 1.0f / (1.0f + expf(-x)); }
+// silu(x) = x * sigmoid(x).
+KD_DEVICE float silu(float x) { return x_sigmoid(x, x); }
 
-// The tanh approximation of GELU (PyTorch's approximate="tanh"):
-// 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3))).
+KD_DEVICE float sigmoid(float x) { return x_sigmoid(1.0f, x); }
+
+// The tanh approximation of GELU (PyTorch's approximate="tanh"): 0.5 x (1 + tanh(y)), y = sqrt(2/pi) (x + 0.044715
+// x^3), computed as x * sigmoid(2 y) (the same function: 0.5 (1 + tanh(y)) = sigmoid(2 y)).
 KD_DEVICE float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2 / pi)
   const float k1 = 0.044715f;
-  return 0.5f * x * (1.0f + tanhf(k0 * (x + k1 * x * x * x)));
+  return x_sigmoid(x, 2.0f * k0 * (x + k1 * x * x * x));
 }
 
 }  // namespace kd

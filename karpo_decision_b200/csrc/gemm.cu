@@ -11,8 +11,9 @@
 //   warp 0      TMA producer: A and B tiles (128-byte rows, 128-byte swizzle) into a 4-stage shared-memory ring;
 //   warp 1      MMA issuer: one elected thread issues tcgen05.mma (M=128, N=256) into one of two TMEM accumulators
 //               (2 x 256 fp32 columns) and commits each stage back to the producer;
-//   warps 2..5  epilogue: tcgen05.ld of the accumulator (one TMEM lane = one output row per thread), the fused
-//               epilogue, 16-byte stores; the second accumulator lets tile i's epilogue overlap tile i+1's mainloop.
+//   warps 2..9  epilogue, two warpgroups each taking half of a tile's columns: tcgen05.ld of the accumulator (one
+//               TMEM lane = one output row per thread), the fused epilogue, 16-byte stores; the second accumulator
+//               lets tile i's epilogue overlap tile i+1's mainloop.
 // The k-loop is BK = 64 bf16 (or 128 e4m3) elements: one 128-byte swizzle row per operand row.
 #include "common.cuh"
 #include "kd_internal.h"
@@ -28,8 +29,13 @@ constexpr int A_STAGE_BYTES = BM * ROW_BYTES;  // 16 KB
 constexpr int B_STAGE_BYTES = BN * ROW_BYTES;  // 32 KB
 constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 512;  // two 128 x 256 fp32 accumulators
-constexpr int THREADS = 192;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* alignment slack */ + 256 /* barriers */;
+constexpr int EPI_GROUPS = 2;  // epilogue warpgroups, each taking half of a tile's columns
+constexpr int THREADS = 64 + EPI_GROUPS * 128;
+// Output staging: per epilogue warp a 32-row x 64-column bf16 box (128-byte swizzled rows) for its TMA stores.
+constexpr int OUT_BOX_COLS = 64;
+constexpr int OUT_BOX_BYTES = 32 * OUT_BOX_COLS * 2;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_GROUPS * 4 * OUT_BOX_BYTES + 1024 /* alignment slack */ +
+                           256 /* barriers */;
 
 // The fused attention-input epilogue (KD_EPI_QKV): the projection's columns are [q heads][k heads][v heads] (Qwen's
 // gated queries: [q_h | gate_h] per head); each output row's heads are normalized, rotated and scattered to q, k, v
@@ -105,14 +111,16 @@ KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
 // together with its rotation partner rot / 2 further on). The rotary factors come from the per-pack table `cs`
 // ([rot / 2][M]: the lanes of a warp read consecutive rows, one coalesced 128-byte line per pair index).
 template <bool FP8>
-KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, float sa) {
+KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, float sa, int group) {
   const Qkv& g = a.qkv;
   const int hd = g.hd;
   const int q_cols = g.hq * hd * (g.gated ? 2 : 1);
   const int k_end = q_cols + g.hkv * hd;
   const int crow = row < a.M ? row : a.M - 1;  // rows past M compute (warp-collective loads) but store nothing
   const uint32_t* cs = g.cs + crow;
-  for (int h0 = 0; h0 < BN; h0 += hd) {
+  // the epilogue warpgroups share the tile's head slices (one group takes all of a 256-wide head)
+  for (int h0 = (hd < BN ? group * hd : 0); h0 < BN; h0 += (hd < BN ? EPI_GROUPS * hd : BN)) {
+    if (hd >= BN && group != 0) break;
     const int c0 = n0 + h0;  // first column of this head slice
     if (c0 >= a.N) break;
     const uint32_t th = t_row + h0;
@@ -200,52 +208,19 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
   }
 }
 
-template <int EPI>
-KD_DEVICE void store_chunk(const Args& a, int row, int col0, const float (&v)[32]) {
-  // 32 consecutive output columns of one row, rounded to bf16 once (the reference's bf16 Linear output).
-  if (row >= a.M) return;
-  __nv_bfloat16* out = a.C + (int64_t)row * a.ldc + col0;
-  uint32_t packed[16];
-  if constexpr (EPI == KD_EPI_RESIDUAL) {
-    const __nv_bfloat16* res = a.R + (int64_t)row * a.ldr + col0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 rv = *reinterpret_cast<const uint4*>(res + 8 * j);
-      const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-      for (int t = 0; t < 4; ++t) {
-        float2 r2 = unpack_bf16x2(rw[t]);
-        // h + bf16(x): the residual add of two bf16 tensors, rounded once.
-        packed[4 * j + t] = pack_bf16x2(r2.x + bf16_round(v[8 * j + 2 * t]), r2.y + bf16_round(v[8 * j + 2 * t + 1]));
-      }
-    }
-  } else {
-#pragma unroll
-    for (int t = 0; t < 16; ++t) packed[t] = pack_bf16x2(v[2 * t], v[2 * t + 1]);
-  }
-  const int n_out = (EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU) ? a.N / 2 : a.N;
-  if (col0 + 32 <= n_out) {
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      *reinterpret_cast<uint4*>(out + 8 * j) =
-          make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
-  } else {
-    for (int t = 0; t < 16; ++t) {
-      if (col0 + 2 * t < n_out) reinterpret_cast<uint32_t*>(out)[t] = packed[t];
-    }
-  }
-}
-
 template <int EPI, bool FP8>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, Args args) {
+    gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
+                const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r, Args args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* out_stage = smem + STAGES * STAGE_BYTES;  // epilogue warp e's box at e * OUT_BOX_BYTES
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + EPI_GROUPS * 4 * OUT_BOX_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;
   uint64_t* acc_empty = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  uint64_t* res_bar = acc_empty + 2;  // [epilogue warps]: the residual box of that warp has landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + EPI_GROUPS * 4);
 
   const int warp = threadIdx.x / 32;
   const int m_tiles = (args.M + BM - 1) / BM;
@@ -261,8 +236,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], 4 * 32);
+      mbar_init(&acc_empty[b], EPI_GROUPS * 128);
     }
+    for (int e = 0; e < EPI_GROUPS * 4; ++e) mbar_init(&res_bar[e], 1);
     fence_barrier_init();
     tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
@@ -340,7 +316,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   } else {
     // ---------------------------------------------------------------- epilogue (warps 2..5)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int group = (warp - 2) / 4;  // this warp's epilogue warpgroup: its half of each tile's columns
     const int lane = threadIdx.x & 31;
+    uint8_t* box = out_stage + (warp - 2) * OUT_BOX_BYTES;  // this warp's output staging box
+    uint64_t* my_res = &res_bar[warp - 2];
+    uint32_t res_phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -353,48 +333,97 @@ __global__ void __launch_bounds__(THREADS, 1)
       float sa = 1.0f;
       if constexpr (FP8) sa = (row < args.M) ? args.scale_a[row] : 0.0f;
       if constexpr (EPI == KD_EPI_QKV) {
-        qkv_epilogue<FP8>(args, row, n0, t_row, sa);
-      } else if constexpr (EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU) {
-        // Columns [0,128) of the tile are gate rows, [128,256) the matching up rows (weights interleaved at load):
-        // out[:, n0/2 + c] = act(gate) * up, each operand rounded to bf16 first as the reference's Linear outputs are.
-        for (int c = 0; c < BN / 2; c += 32) {
-          uint32_t g[32], u[32];
-          tmem_ld32(t_row + c, g);
-          tmem_ld_wait_regs(g);
-          tmem_ld32(t_row + BN / 2 + c, u);
-          tmem_ld_wait_regs(u);
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float gf = __uint_as_float(g[j]);
-            float uf = __uint_as_float(u[j]);
-            if constexpr (FP8) {
-              gf *= sa * args.scale_b[n0 + c + j];
-              uf *= sa * args.scale_b[n0 + BN / 2 + c + j];
-            }
-            gf = bf16_round(gf);
-            uf = bf16_round(uf);
-            v[j] = (EPI == KD_EPI_SWIGLU ? silu(gf) : gelu_tanh(gf)) * uf;
-          }
-          store_chunk<EPI>(args, row, n0 / 2 + c, v);
-        }
+        qkv_epilogue<FP8>(args, row, n0, t_row, sa, group);
       } else {
-        for (int c = 0; c < BN; c += 32) {
-          if (n0 + c >= args.N) break;
-          uint32_t r[32];
-          tmem_ld32(t_row + c, r);
-          tmem_ld_wait_regs(r);
-          float v[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(r[j]);
-            if constexpr (FP8) {
-              const int col = n0 + c + j;
-              x = x * sa * (col < args.N ? args.scale_b[col] : 0.0f);
+        // Output through this warp's staging box and TMA stores: 64-column chunks of the warp's 32 rows, written
+        // into 128-byte swizzled smem rows (conflict-free: 8 consecutive rows cover all bank groups), then one bulk
+        // tensor store per chunk. The residual (R may alias C) arrives the same way, by a TMA load into the box.
+        constexpr bool gated = EPI == KD_EPI_SWIGLU || EPI == KD_EPI_GEGLU;
+        const int n_out = gated ? args.N / 2 : args.N;
+        const int out0 = (gated ? n0 / 2 : n0) + group * (gated ? BN / 4 : BN / 2);  // this group's first column
+        const int chunks = gated ? 1 : 2;
+        const int ybox = m0 + quarter * 32;
+        for (int k = 0; k < chunks; ++k) {
+          const int oc = out0 + k * OUT_BOX_COLS;
+          if (oc >= n_out) break;
+          if (lane == 0) bulk_wait_read();  // the previous chunk's store has read the box
+          __syncwarp();
+          if constexpr (EPI == KD_EPI_RESIDUAL) {
+            if (lane == 0) {
+              mbar_arrive_expect_tx(my_res, OUT_BOX_BYTES);
+              tma_load_2d(&map_r, my_res, box, oc, ybox);
             }
-            v[j] = x;
+            if (!mbar_wait(my_res, res_phase, args.status)) goto done;
+            res_phase ^= 1;
           }
-          store_chunk<EPI>(args, row, n0 + c, v);
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {  // two 32-column halves of the chunk
+            float v[32];
+            if constexpr (gated) {
+              // tile columns [0,128) are gate rows, [128,256) the matching up rows (weights interleaved at load):
+              // act(gate) * up, each operand rounded to bf16 first as the reference's Linear outputs are
+#pragma unroll
+              for (int s16 = 0; s16 < 2; ++s16) {  // 16 columns at a time keeps gate and up in registers
+                const int cg = group * (BN / 4) + h * 32 + s16 * 16;
+                uint32_t g[16], u[16];
+                tmem_ld16(t_row + cg, g);
+                tmem_ld16(t_row + BN / 2 + cg, u);
+                tmem_ld_wait_regs(g);
+                tmem_ld_wait_regs(u);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                  float gf = __uint_as_float(g[j]);
+                  float uf = __uint_as_float(u[j]);
+                  if constexpr (FP8) {
+                    gf *= sa * args.scale_b[n0 + cg + j];
+                    uf *= sa * args.scale_b[n0 + BN / 2 + cg + j];
+                  }
+                  gf = bf16_round(gf);
+                  uf = bf16_round(uf);
+                  v[s16 * 16 + j] = (EPI == KD_EPI_SWIGLU ? silu(gf) : gelu_tanh(gf)) * uf;
+                }
+              }
+            } else {
+              const int c = group * (BN / 2) + k * OUT_BOX_COLS + h * 32;
+              uint32_t r[32];
+              tmem_ld32(t_row + c, r);
+              tmem_ld_wait_regs(r);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float x = __uint_as_float(r[j]);
+                if constexpr (FP8) {
+                  const int col = n0 + c + j;
+                  x = x * sa * (col < args.N ? args.scale_b[col] : 0.0f);
+                }
+                v[j] = x;
+              }
+            }
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // four 16-byte pieces: chunk index h * 4 + q of the 128-byte row
+              uint8_t* piece = box + lane * 128 + (((h * 4 + q) ^ (lane & 7)) << 4);
+              uint32_t w[4];
+              if constexpr (EPI == KD_EPI_RESIDUAL) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(piece);
+                const uint32_t rw[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int t = 0; t < 4; ++t) {
+                  const float2 r2 = unpack_bf16x2(rw[t]);
+                  // h + bf16(x): the residual add of two bf16 tensors, rounded once
+                  w[t] = pack_bf16x2(r2.x + bf16_round(v[8 * q + 2 * t]), r2.y + bf16_round(v[8 * q + 2 * t + 1]));
+                }
+              } else {
+#pragma unroll
+                for (int t = 0; t < 4; ++t) w[t] = pack_bf16x2(v[8 * q + 2 * t], v[8 * q + 2 * t + 1]);
+              }
+              *reinterpret_cast<uint4*>(piece) = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+          fence_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&map_c, box, oc, ybox);
+            bulk_commit();
+          }
         }
       }
       tc_fence_before();
@@ -406,6 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   }
 done:
+  bulk_wait();  // the epilogue's TMA stores have completed (no-op for threads that issued none) before the CTA exits
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -416,7 +446,8 @@ done:
 }
 
 template <int EPI, bool FP8>
-int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& args, cudaStream_t stream) {
+int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
+           const Args& args, cudaStream_t stream) {
   auto kernel = gemm_kernel<EPI, FP8>;
   static bool configured[64] = {false};
   int dev = 0;
@@ -431,7 +462,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const Args& args, cudaS
   const int n_tiles = (args.N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
   const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, args);
+  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, mc, mr, args);
   return record_cuda_error(cudaGetLastError(), "gemm: launch");
 }
 
@@ -482,10 +513,20 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
   args.status = status;
   args.qkv = qkv ? *qkv : gemm::Qkv{};
 
+  // output (and residual) boxes for the TMA-store epilogue: 64 columns x 32 rows, 128-byte swizzle
+  CUtensorMap mc = ma, mr = ma;
+  if (epilogue != KD_EPI_QKV) {
+    rc = make_tma_2d(&mc, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n_out, M, ldc, gemm::OUT_BOX_COLS, 32,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc && epilogue == KD_EPI_RESIDUAL)
+      rc = make_tma_2d(&mr, R, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, N, M, ldr, gemm::OUT_BOX_COLS, 32,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+  }
 #define KD_GEMM_CASE(E)                                                         \
   case E:                                                                       \
-    return fp8 ? gemm::launch<E, true>(ma, mb, args, stream)                    \
-               : gemm::launch<E, false>(ma, mb, args, stream);
+    return fp8 ? gemm::launch<E, true>(ma, mb, mc, mr, args, stream)            \
+               : gemm::launch<E, false>(ma, mb, mc, mr, args, stream);
   switch (epilogue) {
     KD_GEMM_CASE(KD_EPI_STORE)
     KD_GEMM_CASE(KD_EPI_RESIDUAL)
