@@ -8,7 +8,8 @@ bucket of B tokens serves any pack of at most B tokens, whatever its sequences:
 - the rows past the pack become padding sequences of at most ``PAD_SEQUENCE`` tokens each, computed and never read;
 - the boundary slots past them are empty sequences, so the attention grid of the capture stays valid.
 The reference instead captures one right-padded single-sequence (Gemma) or per-segment (Qwen) layout per bucket. As in
-the reference, the head (final norm at the markers) runs after the replay on the real rows, outside the graph. Packs
+the reference, the head (a bidirectional model's last layer at the markers, then the final norm) runs after the replay
+on the real rows, outside the graph (serve/qwen_graphs.py:160-167, serve/graphs.py:114-118). Packs
 no bucket covers, and branched block layouts (their virtual sequences are planned per pack), run the plain path of
 the same kernels (serve/graphs.py:121-132).
 """
@@ -107,6 +108,7 @@ class Graphs:
         b = self.bucket_for(p)
         if b is None:
             return self.model(p)
+        self.model.plan(p)  # the plain path's refusals of malformed packs (no plan: a covered pack has no branches)
         t = int(p.input_ids.numel())
         n = int(p.cu.numel()) - 1
         b.ids[:t].copy_(p.input_ids, non_blocking=True)

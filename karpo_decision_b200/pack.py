@@ -29,6 +29,7 @@ class Pack:
     segment_ids_cpu: torch.Tensor | None = None
     rope: torch.Tensor | None = None
     plan: Any = None
+    markers_cpu: torch.Tensor | None = None  # the markers on the host (planning checks need no device read)
 
     @property
     def tokens(self) -> int:
@@ -63,6 +64,7 @@ def pack(sequences: Sequence[Any], device: torch.device, blocks: bool = False) -
         max_markers=max(counts),
         segment_ids=None if segment_ids is None else segment_ids.to(device, non_blocking=True),
         segment_ids_cpu=segment_ids,
+        markers_cpu=markers.to(torch.int64),
     )
 
 
@@ -91,4 +93,5 @@ def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: boo
         max_markers=int(counts.max()),
         segment_ids=None if seg_cpu is None else seg_cpu.to(device, non_blocking=True),
         segment_ids_cpu=seg_cpu,
+        markers_cpu=torch.from_numpy(np.asarray(arrays["markers"], dtype=np.int64)),
     )

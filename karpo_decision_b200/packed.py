@@ -32,7 +32,7 @@ import numpy as np
 import torch
 
 from . import ops
-from .plan import block_plan
+from .plan import BlockPlan, block_plan, marker_bounds
 from .synthetic import Spec
 
 #: Qwen's FP8 path keeps projections with fewer outputs in bf16 (serve/qwen_fp8.py:17).
@@ -137,11 +137,11 @@ class Packed(torch.nn.Module):
     ``family.Packed(backbone, attention)`` does (decider.py:35)."""
 
     def __init__(self, spec: Spec, weights: dict[str, Any], device: torch.device | str = "cuda",
-                 attention: str = "causal", fp8: bool = False) -> None:
+                 attention: str | None = None, fp8: bool = False) -> None:
         super().__init__()
-        if attention != "causal":
-            raise NotImplementedError("the B200 path runs causal checkpoints (decision_config attention = causal); "
-                                      "bidirectional attention with the marker-only last layer is not built yet")
+        attention = spec.attention if attention is None else attention
+        if attention not in ("causal", "bidirectional"):
+            raise ValueError(f"attention must be 'causal' or 'bidirectional', not {attention!r}")
         if spec.head_dim not in (64, 128, 256):
             raise ValueError(f"head_dim {spec.head_dim} is not one of the kernels' 64, 128, 256")
         self.spec = spec
@@ -151,6 +151,13 @@ class Packed(torch.nn.Module):
         self.family = spec.family
         self.types = spec.layer_types()
         self.window = spec.window
+        #: Bidirectional checkpoints: full (Qwen) and global (Gemma) layers see their whole (virtual) sequence, and the
+        #: last layer runs for the marker rows only (families/qwen/packed.py:31-32,65-67, families/gemma/packed.py:
+        #: 170-173); Gemma's sliding layers stay causal.
+        self.prune_last = attention == "bidirectional"
+        self.full_window = (-1, -1) if self.prune_last else (-1, 0)
+        if self.prune_last and self.types[-1] != "full_attention":
+            raise ValueError("pruning the last layer needs a full-attention (global) last layer")
         dev = self.device
         s = spec
         self.inter_pad = s.intermediate + (-s.intermediate) % GATE_BLOCK
@@ -300,89 +307,146 @@ class Packed(torch.nn.Module):
 
     def forward(self, p: Any) -> torch.Tensor:
         """(M, hidden) final-normalized hidden states at the markers, in pack order."""
-        return self.head(self.body(p), p)
+        plan = self.plan(p)
+        return self.head(self.body(p, plan), p, plan)
 
-    def head(self, h: torch.Tensor, p: Any) -> torch.Tensor:
-        """(M, hidden): the final norm of the body's output at the markers (families/qwen/packed.py:173-176,
-        families/gemma/packed.py:297-303)."""
-        mode = ops.NORM_ONE_PLUS if self.spec.family == "qwen" else ops.NORM_WEIGHT
-        return ops.marker_norm(h, p.markers, self.norm, mode, self.spec.eps)
-
-    def body(self, p: Any) -> torch.Tensor:
-        """(T, hidden) hidden states after every layer (the workspace's residual buffer): embedding and layers, no
-        host synchronization, so it can be captured in a CUDA graph when ``p``'s tensors are static."""
-        s = self.spec
-        plan = None
-        if p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
-            if s.family != "gemma":  # families/qwen/packed.py:180-181
+    def plan(self, p: Any) -> BlockPlan | None:
+        """Host planning of a pack, done before any kernel is queued: the virtual sequences of branched block layouts
+        (families/gemma/packed.py:103-151; None without branches) and the reference's refusals of malformed packs:
+        Qwen reads joint layouts only (families/qwen/packed.py:180-181); a Gemma block's readout marker is its last
+        token, one per block or branch (families/gemma/packed.py:136-143)."""
+        seg = p.segment_ids_cpu
+        if self.family != "gemma":
+            if p.segment_ids is not None:
                 raise ValueError("the Qwen family reads joint layouts, not block layouts")
-            # branched block layouts: virtual sequences with gathered keys, planned once before any layer is queued
-            plan = block_plan(p.cu_cpu, p.segment_ids_cpu, self.window, self.device)
+            return None
+        if p.cu_cpu is None:
+            raise ValueError("planning a Gemma pack needs its boundaries on the host (cu_cpu)")
+        markers = getattr(p, "markers_cpu", None)
+        if markers is None:
+            markers = p.markers.cpu()  # a device read, as the reference's block_plan makes
+        if seg is not None and bool((seg != 0).any()):
+            return block_plan(p.cu_cpu, seg, self.window, self.device, markers_cpu=markers)
+        marker_bounds([int(x) for x in p.cu_cpu.tolist()], np.asarray(markers))
+        return None
+
+    def head(self, h: torch.Tensor, p: Any, plan: BlockPlan | None = None) -> torch.Tensor:
+        """(M, hidden): the final norm of the body's output at the markers (families/qwen/packed.py:173-176,
+        families/gemma/packed.py:297-303); a bidirectional model first runs its last layer for the marker rows."""
+        mode = ops.NORM_ONE_PLUS if self.spec.family == "qwen" else ops.NORM_WEIGHT
+        if not self.prune_last:
+            return ops.marker_norm(h, p.markers, self.norm, mode, self.spec.eps)
+        if plan is None and p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
+            plan = self.plan(p)
+        hm = self._last_layer_at_markers(h, p, plan)
+        return ops.rmsnorm(hm, self.norm, mode, self.spec.eps)
+
+    def body(self, p: Any, plan: BlockPlan | None = None) -> torch.Tensor:
+        """(T, hidden) hidden states after every layer the whole pack runs (all but the last in a bidirectional
+        model; the workspace's residual buffer): embedding and layers, no host synchronization, so it can be captured
+        in a CUDA graph when ``p``'s tensors are static. Branched block layouts need their ``plan``."""
+        s = self.spec
+        if plan is None and p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
+            plan = self.plan(p)
         t = int(p.input_ids.numel())
         ws = self.workspace(t)
-        n_seqs = int(p.cu.numel()) - 1
-        max_len = int(p.max_length)
         qwen = s.family == "qwen"
-        mode = ops.NORM_ONE_PLUS if qwen else ops.NORM_WEIGHT
-        eps = s.eps
         h = ops.embed(p.input_ids, self.embed_tokens, 0.0 if qwen else math.sqrt(s.hidden), out=ws.h[:t])
-        seqpos = p.seqpos if p.seqpos.dtype == torch.int64 else p.seqpos.long()
-        positions = int(max_len)  # a position (block layouts included) is below its sequence's length
         rope_cs: dict[str, torch.Tensor] = {}  # per rotary kind, gathered once per pack
-        for layer in self.layers:
-            fp8_qkv = any(proj.fp8 for proj, _, _ in layer.qkv)
-            bf16_qkv = any(not proj.fp8 for proj, _, _ in layer.qkv)
-            x, x8 = self._normed(ws, h, layer.input_norm, mode, bf16_qkv, fp8_qkv)
-            cos, sin = self.tables(layer.kind, positions)
-            heads_out = (ws.q[:t], ws.k[:t], ws.v[:t], ws.gate[:t] if qwen else None)
-            v_mode = -1 if qwen else ops.NORM_NONE
-            if self.fused_qkv and len(layer.qkv) == 1:
-                # one GEMM whose epilogue normalizes, rotates and scatters the heads (kd_qkv_projection)
-                if layer.kind not in rope_cs:
-                    rope_cs[layer.kind] = ops.rope_gather(seqpos, cos, sin, out=ws.cs(layer.kind, t))
-                proj = layer.qkv[0][0]
-                a_in, sa = (x8[0], x8[1]) if proj.fp8 else (x, None)
-                q, k, v, gate = ops.qkv_projection(
-                    a_in, proj.weight, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm,
-                    mode, v_mode, eps, rope_cs[layer.kind], cos.shape[1], out=heads_out, scale_a=sa,
-                    scale_w=proj.scale)
-            else:
-                qkv = ws.qkv[:t]
-                for proj, col, width in layer.qkv:
-                    self._project(proj, x, x8, qkv[:, col:col + width] if width != qkv.shape[1] else qkv)
-                q, k, v, gate = ops.qkv_norm_rope(qkv, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm,
-                                                  layer.k_norm, mode, v_mode, eps, cos, sin, out=heads_out)
-            if layer.kind == "sliding_attention":
-                window = (self.window - 1, 0)
-            else:
-                window = (-1, 0)
-            scale = s.head_dim ** -0.5 if qwen else 1.0
+        for layer in self.layers[:-1] if self.prune_last else self.layers:
+            q, k, v, gate = self._attention_inputs(layer, h, p, ws, rope_cs)
+            window = (self.window - 1, 0) if layer.kind == "sliding_attention" else self.full_window
             if plan is None:
-                o = ops.attention_varlen(q, k, v, p.cu, p.cu, max_len, scale, window, gate=gate, out=ws.o[:t])
+                o = ops.attention_varlen(q, k, v, p.cu, p.cu, int(p.max_length), self._scale, window, gate=gate,
+                                         out=ws.o[:t])
             else:  # each virtual sequence's keys: the shared block (or its window tail), then its own rows
                 rows, k_cu = (plan.s_rows, plan.s_cu) if layer.kind == "sliding_attention" else \
                     (plan.g_rows, plan.g_cu)
                 kg, vg = ops.gather_rows(k, rows), ops.gather_rows(v, rows)
-                o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, scale, window, gate=gate,
+                o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, self._scale, window, gate=gate,
                                          out=ws.o[:t])
-            o8 = self._quantized(ws, o) if layer.o.fp8 else None
-            if qwen:
-                self._project(layer.o, o, o8, h, ops.EPI_RESIDUAL, residual=h)  # h += o W_o^T
-                y, y8 = self._normed(ws, h, layer.post_attention_norm, mode, not layer.gate_up.fp8,
-                                     layer.gate_up.fp8)
-                m = self._project(layer.gate_up, y, y8, ws.m[:t], ops.EPI_SWIGLU)
-                m8 = self._quantized(ws, m) if layer.down.fp8 else None
-                self._project(layer.down, m, m8, h, ops.EPI_RESIDUAL, residual=h)  # h += m W_d^T
-            else:
-                a = self._project(layer.o, o, o8, ws.a[:t])
-                ops.norm_add(h, a, layer.post_attention_norm, mode, eps, out=h)  # h = h + norm(a)
-                z, z8 = self._normed(ws, h, layer.pre_feedforward_norm, mode, not layer.gate_up.fp8,
-                                     layer.gate_up.fp8)
-                m = self._project(layer.gate_up, z, z8, ws.m[:t], ops.EPI_GEGLU)
-                m8 = self._quantized(ws, m) if layer.down.fp8 else None
-                d = self._project(layer.down, m, m8, ws.a[:t])
-                ops.norm_add(h, d, layer.post_feedforward_norm, mode, eps, scalar=layer.scalar, out=h)
+            self._after_attention(layer, h, o, ws)
         return h
+
+    @property
+    def _scale(self) -> float:
+        return self.spec.head_dim ** -0.5 if self.spec.family == "qwen" else 1.0
+
+    def _attention_inputs(self, layer: Layer, h: torch.Tensor, p: Any, ws: Workspace,
+                          rope_cs: dict[str, torch.Tensor]) -> tuple:
+        """q, k, v (normed, rotated) and Qwen's gate for every row of ``h`` (the layer's input norm and QKV
+        projection; families/qwen/packed.py:108-121, families/gemma/packed.py:183-193)."""
+        s = self.spec
+        t = h.shape[0]
+        qwen = s.family == "qwen"
+        mode = ops.NORM_ONE_PLUS if qwen else ops.NORM_WEIGHT
+        seqpos = p.seqpos if p.seqpos.dtype == torch.int64 else p.seqpos.long()
+        fp8_qkv = any(proj.fp8 for proj, _, _ in layer.qkv)
+        bf16_qkv = any(not proj.fp8 for proj, _, _ in layer.qkv)
+        x, x8 = self._normed(ws, h, layer.input_norm, mode, bf16_qkv, fp8_qkv)
+        cos, sin = self.tables(layer.kind, int(p.max_length))  # a position is below its sequence's length
+        heads_out = (ws.q[:t], ws.k[:t], ws.v[:t], ws.gate[:t] if qwen else None)
+        v_mode = -1 if qwen else ops.NORM_NONE
+        if self.fused_qkv and len(layer.qkv) == 1:
+            # one GEMM whose epilogue normalizes, rotates and scatters the heads (kd_qkv_projection)
+            if layer.kind not in rope_cs:
+                rope_cs[layer.kind] = ops.rope_gather(seqpos, cos, sin, out=ws.cs(layer.kind, t))
+            proj = layer.qkv[0][0]
+            a_in, sa = (x8[0], x8[1]) if proj.fp8 else (x, None)
+            return ops.qkv_projection(
+                a_in, proj.weight, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm,
+                mode, v_mode, s.eps, rope_cs[layer.kind], cos.shape[1], out=heads_out, scale_a=sa,
+                scale_w=proj.scale)
+        qkv = ws.qkv[:t]
+        for proj, col, width in layer.qkv:
+            self._project(proj, x, x8, qkv[:, col:col + width] if width != qkv.shape[1] else qkv)
+        return ops.qkv_norm_rope(qkv, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm,
+                                 mode, v_mode, s.eps, cos, sin, out=heads_out)
+
+    def _after_attention(self, layer: Layer, h: torch.Tensor, o: torch.Tensor, ws: Workspace) -> None:
+        """The rest of the layer, in place on the rows of ``h`` (``o``: their attention outputs): the output
+        projection and residual, then the MLP (families/qwen/packed.py:153-156, families/gemma/packed.py:262-265)."""
+        s = self.spec
+        t = h.shape[0]
+        mode = ops.NORM_ONE_PLUS if s.family == "qwen" else ops.NORM_WEIGHT
+        o8 = self._quantized(ws, o) if layer.o.fp8 else None
+        if s.family == "qwen":
+            self._project(layer.o, o, o8, h, ops.EPI_RESIDUAL, residual=h)  # h += o W_o^T
+            y, y8 = self._normed(ws, h, layer.post_attention_norm, mode, not layer.gate_up.fp8, layer.gate_up.fp8)
+            m = self._project(layer.gate_up, y, y8, ws.m[:t], ops.EPI_SWIGLU)
+            m8 = self._quantized(ws, m) if layer.down.fp8 else None
+            self._project(layer.down, m, m8, h, ops.EPI_RESIDUAL, residual=h)  # h += m W_d^T
+        else:
+            a = self._project(layer.o, o, o8, ws.a[:t])
+            ops.norm_add(h, a, layer.post_attention_norm, mode, s.eps, out=h)  # h = h + norm(a)
+            z, z8 = self._normed(ws, h, layer.pre_feedforward_norm, mode, not layer.gate_up.fp8, layer.gate_up.fp8)
+            m = self._project(layer.gate_up, z, z8, ws.m[:t], ops.EPI_GEGLU)
+            m8 = self._quantized(ws, m) if layer.down.fp8 else None
+            d = self._project(layer.down, m, m8, ws.a[:t])
+            ops.norm_add(h, d, layer.post_feedforward_norm, mode, s.eps, scalar=layer.scalar, out=h)
+
+    def _last_layer_at_markers(self, h: torch.Tensor, p: Any, plan: BlockPlan | None) -> torch.Tensor:
+        """(M, hidden) before the final norm: the last layer for the marker rows only (families/qwen/packed.py:127-140,
+        families/gemma/packed.py:267-281). Every row's keys and values come from one QKV projection of ``h`` (the
+        queries and gates are then read at the markers); each marker attends to every key of its sequence (Gemma: of
+        its virtual sequence) without a mask; output projection and MLP run on the marker rows."""
+        layer = self.layers[-1]
+        ws = self.workspace(h.shape[0])
+        q, k, v, gate = self._attention_inputs(layer, h, p, ws, {})
+        markers = p.markers
+        n = int(markers.numel())
+        qm = ops.gather_rows(q, markers)
+        gm = None if gate is None else ops.gather_rows(gate, markers)
+        if plan is None:
+            q_cu, k_cu = p.marker_cu, p.cu
+        else:
+            q_cu, k_cu = plan.m_cu, plan.g_cu
+            k, v = ops.gather_rows(k, plan.g_rows), ops.gather_rows(v, plan.g_rows)
+        max_q = int(p.max_markers) if plan is None else 1  # a virtual sequence reads out at most one marker
+        o = ops.attention_varlen(qm, k, v, q_cu, k_cu, max_q, self._scale, (-1, -1), gate=gm, out=ws.o[:n])
+        hm = ops.gather_rows(h, markers)
+        self._after_attention(layer, hm, o, ws)
+        return hm
 
 
 class Readout(torch.nn.Module):

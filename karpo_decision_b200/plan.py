@@ -12,6 +12,7 @@ order; attention aligns each virtual sequence's queries with the end of its keys
 from __future__ import annotations
 
 from dataclasses import dataclass
+from typing import Any
 
 import numpy as np
 import torch
@@ -25,12 +26,25 @@ class BlockPlan:
     s_rows: torch.Tensor  # int64 key rows of sliding layers
     s_cu: torch.Tensor  # (v + 1,) int32 bounds over s_rows
     max_q: int
+    m_cu: torch.Tensor | None = None  # (v + 1,) int32 marker bounds over the virtual sequences (markers in pack order)
 
 
-def block_plan(cu_cpu: torch.Tensor, segment_ids_cpu: torch.Tensor, window: int, device: torch.device
-               ) -> BlockPlan:
+def marker_bounds(q_cu: list[int], markers: np.ndarray) -> list[int]:
+    """The markers' bounds over virtual sequences ``q_cu`` (pack rows), refusing what the reference refuses: a block's
+    readout marker is its last token, at most one per block or branch (families/gemma/packed.py:136-143)."""
+    markers = np.asarray(markers, dtype=np.int64)
+    m_cu = np.searchsorted(markers, np.asarray(q_cu, dtype=np.int64)).tolist()
+    for qb, ma, mb in zip(q_cu[1:], m_cu[:-1], m_cu[1:], strict=True):
+        if mb - ma > 1 or (mb > ma and int(markers[ma]) != qb - 1):
+            raise ValueError("a block's readout marker must be its last token, one per branch")
+    return m_cu
+
+
+def block_plan(cu_cpu: torch.Tensor, segment_ids_cpu: torch.Tensor, window: int, device: torch.device,
+               markers_cpu: Any = None) -> BlockPlan:
     """Raises ValueError on segments that are not a shared block followed by branches 1, 2, ... (the reference's
-    refusal, families/gemma/packed.py:116-118)."""
+    refusal, families/gemma/packed.py:116-118); with ``markers_cpu``, also plans (and checks) the markers per virtual
+    sequence."""
     bounds = cu_cpu.tolist()
     segments = segment_ids_cpu.numpy() if isinstance(segment_ids_cpu, torch.Tensor) else np.asarray(segment_ids_cpu)
     q_cu, g_cu, s_cu = [0], [0], [0]
@@ -62,6 +76,7 @@ def block_plan(cu_cpu: torch.Tensor, segment_ids_cpu: torch.Tensor, window: int,
     def dev(x, dtype):
         return torch.as_tensor(np.asarray(x), dtype=dtype).to(device, non_blocking=False)
 
+    m_cu = None if markers_cpu is None else dev(marker_bounds(q_cu, np.asarray(markers_cpu)), torch.int32)
     return BlockPlan(q_cu=dev(q_cu, torch.int32), g_rows=dev(np.concatenate(g_rows), torch.int64),
                      g_cu=dev(g_cu, torch.int32), s_rows=dev(np.concatenate(s_rows), torch.int64),
-                     s_cu=dev(s_cu, torch.int32), max_q=int(np.diff(q_cu).max()))
+                     s_cu=dev(s_cu, torch.int32), max_q=int(np.diff(q_cu).max()), m_cu=m_cu)

@@ -202,7 +202,10 @@ def qwen_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8:
     """(M, hidden) final-normed hidden states at the markers: families/qwen/packed.py:178-187 over full-attention
     layers (``layer`` :149-156, ``full_attention`` :119-125, ``_qkv`` :108-117, ``head`` :173-176), causal window
     (-1, 0) (:31-32). With ``fp8``, every projection is the rowwise FP8 product of serve/qwen_fp8.py:38-42 (the
-    activation quantized from its bf16 value at each call)."""
+    activation quantized from its bf16 value at each call). ``spec["attention"] == "bidirectional"`` widens the window
+    to (-1, -1) (:31-32); the reference then runs the last layer for the marker rows only (:127-140), whose result is
+    the marker rows of the whole layer, which is what this restatement computes (pinned by the ``qwen_bidir``
+    fixture)."""
     eps, hq, hkv, hd = spec["eps"], spec["heads"], spec["kv_heads"], spec["head_dim"]
     if fp8:
         weights = quantize_weights(weights, QWEN_FP8_MIN_FEATURES)
@@ -283,7 +286,10 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
     ``h + norm(attn)`` (fused.py:29-30), MLP ``norm(down(gelu_tanh(gate z) * up z))`` with z = norm(h) (:258-260),
     ``(h + mlp) * layer_scalar`` (fused.py:33-34). Embeddings scaled by bf16(sqrt(hidden)) (:283-285). With ``fp8``,
     the projections are serve/fp8.py's: one activation quantization per fused producer (norm, gelu-mul), o_proj's
-    input quantized at its call (serve/fp8.py:57-84, :104-117)."""
+    input quantized at its call (serve/fp8.py:57-84, :104-117). ``spec["attention"] == "bidirectional"`` makes the
+    global layers non-causal (:168-170, ``_global`` with causal False); the reference's marker-only last layer
+    (:267-281) equals the marker rows of the whole last layer (a marker is its virtual sequence's last token), which
+    is what this restatement computes (pinned by the ``gemma_bidir`` and ``gemma_blocks_bidir`` fixtures)."""
     eps, hq, hkv, hd, w_len = spec["eps"], spec["heads"], spec["kv_heads"], spec["head_dim"], spec["window"]
     if fp8:
         weights = quantize_weights(weights)

@@ -203,6 +203,17 @@ CASES = {
                                  (17, [10, 1, 4]), (3, [20, 25])], fp8=False),
     "gemma_tiny_fp8": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
                            lengths=("uniform", 4, 8, 96), markers=(1, 1), fp8=True),
+    # Bidirectional checkpoints (config.attention = "bidirectional"): full/global layers see their whole (virtual)
+    # sequence and the last layer runs at the markers only (families/qwen/packed.py:127-140,
+    # families/gemma/packed.py:267-281).
+    "qwen_bidir": dict(spec=small(CONFIGS["tiny"], partial_rotary=0.5, attention="bidirectional"),
+                       lengths=("uniform", 6, 8, 200), markers=(1, 4), fp8=False),
+    "gemma_bidir": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
+                                  attention="bidirectional"),
+                        lengths=("uniform", 6, 8, 96), markers=(1, 1), fp8=False),
+    "gemma_blocks_bidir": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
+                                         attention="bidirectional"),
+                               blocks=[(23, []), (21, [5, 7, 3]), (14, [4, 9]), (3, [20, 25])], fp8=False),
 }
 
 
@@ -264,7 +275,7 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
 
             model = qwen_backbone(spec, weights)
             stack.enter_context(_patched(qp, "_kernels", lambda: (None, varlen_contract, None)))
-            packed = qp.Packed(model, "causal")
+            packed = qp.Packed(model, spec.attention)
             if case["fp8"]:
                 from karpo_decision.serve import qwen_fp8
                 qwen_fp8.quantize(packed)
@@ -278,7 +289,7 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
             lm = gemma_lm(spec, weights)
             stack.enter_context(_patched(sliding_attention, "varlen_attn", varlen_contract))
             stack.enter_context(_patched(gp, "sdpa_kernel", lambda *_: contextlib.nullcontext()))
-            packed = gp.Packed(types.SimpleNamespace(language_model=lm), "causal")
+            packed = gp.Packed(types.SimpleNamespace(language_model=lm), spec.attention)
             if case["fp8"]:
                 from karpo_decision.serve import fp8
                 stack.enter_context(_patched(fp8, "to_e4m3", fp8._rows_e4m3))

@@ -15,13 +15,15 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
 
 
-@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny"])
+@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "qwen_bidir", "gemma_bidir"])
 def test_replay_equals_eager_for_any_covered_pack(name):
     spec, weights, _, _ = load(name)
     model = Packed(spec, weights, DEV)
     graphs = Graphs(model, buckets=(512, 1024, 2048), max_sequences=16)
     for seed, lengths in enumerate([[100], [37, 211, 64, 130], [512], [300, 400, 9, 1, 250], [2000, 48]]):
-        arrays = synthetic_pack_arrays(lengths, spec.vocab, seed=seed, markers_per_seq=(1, 3))
+        # Gemma reads out one marker per block, at its last token (families/gemma/packed.py:136-143)
+        arrays = synthetic_pack_arrays(lengths, spec.vocab, seed=seed,
+                                       markers_per_seq=(1, 3) if spec.family == "qwen" else (1, 1))
         p = from_arrays(arrays, DEV)
         eager = model(p).clone()
         replay = graphs(p)

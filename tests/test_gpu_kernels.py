@@ -273,7 +273,9 @@ def test_marker_norm_and_readout():
 
 @pytest.mark.parametrize("family,hd,partial,fp8", [("qwen", 128, 1.0, False), ("qwen", 64, 0.5, False),
                                                    ("gemma", 256, 1.0, False), ("gemma", 128, 1.0, False),
-                                                   ("qwen", 128, 1.0, True), ("gemma", 128, 1.0, True)])
+                                                   ("qwen", 256, 0.25, False), ("gemma", 64, 1.0, False),
+                                                   ("qwen", 128, 1.0, True), ("gemma", 128, 1.0, True),
+                                                   ("gemma", 256, 1.0, True)])
 def test_qkv_projection_equals_gemm_then_norm_rope(family, hd, partial, fp8):
     """The fused QKV epilogue against the stored projection followed by kd_qkv_norm_rope (one bf16 ulp: the sums of
     squares run in another order)."""

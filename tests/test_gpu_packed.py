@@ -32,7 +32,8 @@ def run_b200(name):
     return spec, weights, arrays, expected, hidden.float().cpu().numpy(), logits.cpu().numpy()
 
 
-@pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks"])
+@pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_bidir",
+                                  "gemma_bidir", "gemma_blocks_bidir"])
 def test_bf16_forward_matches_reference(name):
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
     assert hidden.shape == expected["hidden"].shape
@@ -49,7 +50,7 @@ def test_bf16_forward_matches_reference(name):
     assert cosine.min() > 0.995, cosine
 
 
-@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "gemma_blocks"])
+@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "gemma_blocks", "qwen_bidir", "gemma_blocks_bidir"])
 def test_bf16_forward_tracks_bf16_oracle(name):
     """Against the oracle with the reference's bf16 rounding points: closer than to the float32 reference."""
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
@@ -99,3 +100,16 @@ def test_a_branch_never_sees_another():
     other = model(from_arrays(changed, DEV)).float()
     assert torch.equal(base[0], other[0]) and torch.equal(base[2], other[2])
     assert not torch.equal(base[1], other[1])
+
+
+@pytest.mark.parametrize("name", ["qwen_bidir", "gemma_blocks_bidir"])
+def test_bidirectional_marker_layer_equals_the_whole_last_layer(name):
+    """The marker-only last layer (families/qwen/packed.py:127-140, families/gemma/packed.py:267-281) gives the marker
+    rows of the whole last layer run bidirectionally (a causal model's forward with the full-layer window widened)."""
+    spec, weights, arrays, _ = load(name)
+    pruned = Packed(spec, weights, DEV)
+    whole = Packed(spec, weights, DEV)
+    whole.prune_last = False  # every layer over every row, full/global layers still bidirectional
+    p = from_arrays(arrays, DEV)
+    a, b = pruned(p).float(), whole(from_arrays(arrays, DEV)).float()
+    assert torch.allclose(a, b, atol=2e-2, rtol=2e-2), (a - b).abs().max().item()

@@ -95,3 +95,52 @@ def test_block_plan_matches_oracle_and_refuses_bad_segments():
     bad[5:11] = 1  # a sequence starting with branch 1 has no shared block
     with pytest.raises(ValueError):
         block_plan(cu, bad, 4, torch.device("cpu"))
+
+
+def test_marker_bounds_plan_markers_per_virtual_sequence_and_refuse_bad_ones():
+    """The reference's readout rule for block layouts (families/gemma/packed.py:136-143): per block or branch at most
+    one marker, at its last token; the shared block of a branched sequence reads out none."""
+    import pytest
+
+    from karpo_decision_b200.plan import block_plan, marker_bounds
+    from karpo_decision_b200.synthetic import synthetic_block_arrays
+
+    arrays = synthetic_block_arrays([(5, []), (6, [2, 3]), (2, [4])], 50, seed=0)
+    cu, seg = torch.from_numpy(arrays["cu"]), torch.from_numpy(arrays["segment_ids"])
+    plan = block_plan(cu, seg, window=4, device=torch.device("cpu"), markers_cpu=arrays["markers"])
+    # virtual sequences [0,5) [5,11) [11,13) [13,16) [16,18) [18,22): markers 4, 12, 15, 21
+    assert arrays["markers"].tolist() == [4, 12, 15, 21]
+    assert plan.m_cu.tolist() == [0, 1, 1, 2, 3, 3, 4]
+    assert marker_bounds([0, 5, 9], np.array([4, 8])) == [0, 1, 2]
+    assert marker_bounds([0, 5, 9], np.array([8])) == [0, 0, 1]  # a block may read out nothing
+    with pytest.raises(ValueError):
+        marker_bounds([0, 5, 9], np.array([3, 8]))  # not the block's last token
+    with pytest.raises(ValueError):
+        marker_bounds([0, 5, 9], np.array([4, 7, 8]))  # two markers in one block
+
+
+def test_packed_plan_refuses_what_the_reference_refuses():
+    """``Packed.plan`` on the host (no kernel runs): Qwen refuses block layouts (families/qwen/packed.py:180-181),
+    Gemma refuses a sequence with several markers or one before its last token."""
+    import pytest
+
+    from karpo_decision_b200.packed import Packed
+
+    cpu = torch.device("cpu")
+    qwen = Spec("qwen", 1, 256, 4, 2, 64, 256, 64)
+    model = Packed(qwen, numpy_weights(qwen, 0), cpu)
+    arrays = synthetic_pack_arrays([5, 7], qwen.vocab, seed=0, markers_per_seq=(1, 3))
+    assert model.plan(from_arrays(arrays, cpu)) is None
+    with pytest.raises(ValueError):
+        model.plan(from_arrays({**arrays, "segment_ids": np.zeros(12, dtype=np.int64)}, cpu))
+    gemma = Spec("gemma", 1, 256, 4, 2, 64, 256, 64, window=4, attention="bidirectional")
+    model = Packed(gemma, numpy_weights(gemma, 0), cpu)
+    assert model.prune_last and model.full_window == (-1, -1)
+    good = synthetic_pack_arrays([5, 7], gemma.vocab, seed=0)
+    assert model.plan(from_arrays(good, cpu)) is None
+    two = dict(good, markers=np.array([3, 4, 11]), marker_cu=np.array([0, 2, 3]))
+    with pytest.raises(ValueError):
+        model.plan(from_arrays(two, cpu))
+    early = dict(good, markers=np.array([2, 11]))
+    with pytest.raises(ValueError):
+        model.plan(from_arrays(early, cpu))
