@@ -146,6 +146,7 @@ int kd_rope_table(const float* inv_freq, int rot, int64_t positions, float* cos_
  * Column layout of qkv: gated (Qwen3.5 q_proj) [Hq x (q_hd | gate_hd)] then [Hkv x k_hd] then [Hkv x v_hd];
  * ungated (Gemma 4) [Hq x q_hd][Hkv x k_hd][Hkv x v_hd].
  * q/k norm modes KD_NORM_*; v_norm_mode < 0 leaves v unnormalised (Qwen), KD_NORM_NONE is Gemma's v_norm.
+ * head_dim 64, 128, 256 or 512 (Gemma 4 global layers; attention_k_eq_v: the v columns repeat the k projection).
  * Replaces families/qwen/packed.py:108-121 (_qkv + fused.rope) and families/gemma/packed.py:183-193 (_q, _kv). */
 int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* seqpos, int num_heads_q,
                      int num_heads_kv, int head_dim, int gated, const void* q_norm_w, const void* k_norm_w,
@@ -159,7 +160,8 @@ int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* s
  * q (Tq, Hq, hd), k/v (Tk, Hkv, hd) with row strides in elements; cu_q/cu_k int32 [num_seqs + 1] on the device
  * (read when the kernel runs); q holds total_q rows and k/v total_k rows. max_q bounds every Lq. When gate != NULL,
  * out = bf16(bf16(o) * sigmoid(gate))
- * (Qwen's output gate, families/qwen/fused.py:38-39). head_dim 64, 128 or 256. */
+ * (Qwen's output gate, families/qwen/fused.py:38-39). head_dim 64, 128, 256 or 512 (Gemma 4's global layers,
+ * families/gemma/global_attention.py: two 256-wide value slices per head, each CTA forming the full scores). */
 int kd_attention_varlen(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* out,
                         int64_t ldo, const void* gate, int64_t ldg, const int32_t* cu_q, const int32_t* cu_k,
                         int num_seqs, int max_q, int64_t total_q, int64_t total_k, int num_heads_q,

@@ -10,9 +10,11 @@
 // Sequence boundaries are read from device memory when the kernel runs, so a captured graph serves any pack
 // composition with the same token count.
 //
-// One CTA per (128-query tile of one sequence, query head), two CTAs per SM where memory allows (head dim <= 128);
-// 6 warps:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles through a 2-stage ring;
+// One CTA per (128-query tile of one sequence, query head, value slice), two CTAs per SM where memory allows (head
+// dim <= 128). Head dim 512 (Gemma 4's global layers) exceeds tensor memory for a whole output row block next to the
+// scores, so its output is computed in two 256-wide value slices by separate CTAs, each forming the full scores
+// (K and V single-buffered to fit the 128 KB query tile). 6 warps:
+//   warp 0      TMA producer: the Q tile once, then K and V tiles through a ring (2 stages; 1 for head dim 512);
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers, then O += P_j V_j with
 //               P_j read from TMEM (A operand, written over S_j) and V_j as an MN-major B operand from shared memory;
 //   warps 2..5  softmax, one query row per thread (its TMEM lane): scores -> masked, scaled, exp2 against a running
@@ -25,25 +27,31 @@
 namespace kd {
 namespace fa {
 
-template <int HD>
+template <int HD, int DV>
 struct Cfg {
   static constexpr int BM = 128;                    // query rows per CTA = TMEM lanes
   static constexpr int BN = 64;                     // keys per tile
-  static constexpr int CHUNKS = HD / 64;            // 128-byte swizzle chunks along the head dim
+  static constexpr int CHUNKS = HD / 64;            // 128-byte swizzle chunks along the head dim (Q, K)
+  static constexpr int V_CHUNKS = DV / 64;          // the same along this CTA's value slice (V, O)
+  static constexpr int SLICES = HD / DV;            // value slices per head (CTAs along grid z)
   static constexpr int Q_CHUNK = BM * 128;          // bytes of one Q chunk (BM rows x 128 B)
   static constexpr int KV_CHUNK = BN * 128;         // bytes of one K or V chunk
   static constexpr int Q_BYTES = Q_CHUNK * CHUNKS;
-  static constexpr int KV_BYTES = KV_CHUNK * CHUNKS;
-  static constexpr int STAGES = 2;
-  static constexpr int SMEM = Q_BYTES + STAGES * 2 * KV_BYTES + 1024 + 256;
-  // Tensor-memory columns (fp32): O [0, HD), then two score buffers of BN; the bf16 probabilities P_j overwrite the
+  static constexpr int K_BYTES = KV_CHUNK * CHUNKS;
+  static constexpr int V_BYTES = KV_CHUNK * V_CHUNKS;
+  static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
+  static constexpr int STAGES = HD <= 256 ? 2 : 1;
+  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 256;
+  // Tensor-memory columns (fp32): O [0, DV), then two score buffers of BN; the bf16 probabilities P_j overwrite the
   // first BN / 2 columns of their own score buffer once the softmax has read it.
   static constexpr int O_COL = 0;
-  static constexpr int S_COL = HD;
-  static constexpr int TMEM_COLS = HD + 2 * BN <= 256 ? 256 : 512;
+  static constexpr int S_COL = DV;
+  static constexpr int TMEM_COLS = DV + 2 * BN <= 256 ? 256 : 512;
   // Two CTAs per SM (their softmax and MMA phases interleave) when shared and tensor memory allow it.
   static constexpr int CTAS_PER_SM = (2 * SMEM <= 227 * 1024 && 2 * TMEM_COLS <= 512) ? 2 : 1;
   static_assert(S_COL + 2 * BN <= TMEM_COLS, "tensor memory budget");
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+  static_assert(DV <= 256 && HD % DV == 0, "value slices of at most 256 columns");
 };
 
 struct Args {
@@ -69,22 +77,23 @@ KD_DEVICE float fast_exp2(float x) {
   return y;
 }
 
-template <int HD>
-__global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
+template <int HD, int DV>
+__global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_g, Args a) {
-  using C = Cfg<HD>;
+  using C = Cfg<HD, DV>;
   constexpr int BM = C::BM, BN = C::BN;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_q = smem;
-  uint8_t* s_kv = smem + C::Q_BYTES;  // stage s: K at s * 2 * KV_BYTES, V right after
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::Q_BYTES + C::STAGES * 2 * C::KV_BYTES);
+  uint8_t* s_kv = smem + C::Q_BYTES;  // stage s: K at s * STAGE_BYTES, V right after
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::Q_BYTES + C::STAGES * C::STAGE_BYTES);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;                  // [STAGES]
   uint64_t* v_full = k_full + C::STAGES;        // [STAGES]
-  uint64_t* kv_empty = v_full + C::STAGES;      // [STAGES]
-  uint64_t* s_full = kv_empty + C::STAGES;      // [2]
+  uint64_t* k_empty = v_full + C::STAGES;       // [STAGES]: released by the S = Q K^T that read the stage's K
+  uint64_t* v_empty = k_empty + C::STAGES;      // [STAGES]: released by the O += P V that read its V
+  uint64_t* s_full = v_empty + C::STAGES;       // [2]
   uint64_t* p_full = s_full + 2;                // [2]
   uint64_t* pv_done = p_full + 2;               // [2]
   uint64_t* q_free = pv_done + 2;              // the last S has read Q: its buffer takes the gate tile
@@ -111,6 +120,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
   if (seq < 0) return;  // uniform across the CTA: nothing allocated yet
   const int head = blockIdx.y;
   const int kvh = head / (a.hq / a.hkv);
+  const int vcol = (int)blockIdx.z * DV;  // this CTA's value slice within the head
   const int off = lk - lq;  // end alignment of queries to keys
   const int qe = min(qs + BM, lq);
   int kmin = 0, kmax = lk - 1;
@@ -126,7 +136,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&s_full[b], 1);
@@ -158,36 +169,38 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
       for (int j = 0; j < n_tiles; ++j) {
         const int st = j % C::STAGES;
         const uint32_t ph = (j / C::STAGES) & 1;
-        if (!mbar_wait(&kv_empty[st], ph ^ 1, a.status)) goto done;
         const int row = k0 + (first_tile + j) * BN;
-        uint8_t* sk = s_kv + st * 2 * C::KV_BYTES;
-        uint8_t* sv = sk + C::KV_BYTES;
-        mbar_arrive_expect_tx(&k_full[st], C::KV_BYTES);
+        uint8_t* sk = s_kv + st * C::STAGE_BYTES;
+        uint8_t* sv = sk + C::K_BYTES;
+        if (!mbar_wait(&k_empty[st], ph ^ 1, a.status)) goto done;
+        mbar_arrive_expect_tx(&k_full[st], C::K_BYTES);
         for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(&map_k, &k_full[st], sk + c * C::KV_CHUNK, kvh * HD + c * 64, row);
-        mbar_arrive_expect_tx(&v_full[st], C::KV_BYTES);
-        for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + c * 64, row);
+        if (!mbar_wait(&v_empty[st], ph ^ 1, a.status)) goto done;
+        mbar_arrive_expect_tx(&v_full[st], C::V_BYTES);
+        for (int c = 0; c < C::V_CHUNKS; ++c)
+          tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + vcol + c * 64, row);
       }
       if (a.gate) {
         // Qwen's output gate tile, into the Q buffer once the last S = Q K^T has read it: the epilogue then reads
         // its row from shared memory instead of scattered global loads.
         if (!mbar_wait(q_free, 0, a.status)) goto done;
-        mbar_arrive_expect_tx(g_full, C::Q_BYTES);
-        for (int c = 0; c < C::CHUNKS; ++c)
-          tma_load_2d(&map_g, g_full, s_q + c * C::Q_CHUNK, head * HD + c * 64, q0 + qs);
+        mbar_arrive_expect_tx(g_full, C::V_CHUNKS * C::Q_CHUNK);
+        for (int c = 0; c < C::V_CHUNKS; ++c)
+          tma_load_2d(&map_g, g_full, s_q + c * C::Q_CHUNK, head * HD + vcol + c * 64, q0 + qs);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (n_tiles > 0 && elect_one()) {
       constexpr uint32_t idesc_s = mma_idesc(1, BM, BN);          // bf16, K-major A and B
-      constexpr uint32_t idesc_o = mma_idesc(1, BM, HD, 1);       // bf16, A from TMEM, MN-major B (V)
+      constexpr uint32_t idesc_o = mma_idesc(1, BM, DV, 1);       // bf16, A from TMEM, MN-major B (V)
       const uint32_t sq = smem_u32(s_q);
       if (!mbar_wait(q_full, 0, a.status)) goto done;
       auto issue_s = [&](int j) -> bool {
         const int st = j % C::STAGES;
         if (!mbar_wait(&k_full[st], (j / C::STAGES) & 1, a.status)) return false;
         tc_fence_after();
-        const uint32_t sk = smem_u32(s_kv + st * 2 * C::KV_BYTES);
+        const uint32_t sk = smem_u32(s_kv + st * C::STAGE_BYTES);
         const uint32_t d = tmem + C::S_COL + (j & 1) * BN;
 #pragma unroll
         for (int kk = 0; kk < HD / 16; ++kk) {
@@ -195,6 +208,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
           mma_f16_ss(d, sw128_kmajor_desc(sq + c * C::Q_CHUNK + w), sw128_kmajor_desc(sk + c * C::KV_CHUNK + w),
                      idesc_s, kk > 0);
         }
+        mma_commit(&k_empty[st]);  // the stage's K is free once these MMAs have read it
         mma_commit(&s_full[j & 1]);
         if (j == n_tiles - 1) mma_commit(q_free);  // Q is free once the last S has completed
         return true;
@@ -211,13 +225,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
         if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, a.status)) goto done;
         if (!mbar_wait(&v_full[st], (j / C::STAGES) & 1, a.status)) goto done;
         tc_fence_after();
-        const uint32_t sv = smem_u32(s_kv + st * 2 * C::KV_BYTES + C::KV_BYTES);
+        const uint32_t sv = smem_u32(s_kv + st * C::STAGE_BYTES + C::K_BYTES);
         const uint32_t p = tmem + C::S_COL + (j & 1) * BN;  // P_j over the first BN / 2 columns of S_j
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per instruction: 8 columns of bf16 pairs, 2 KB of V rows
           mma_f16_ts(tmem + C::O_COL, p + kk * 8, sw128_mnmajor_desc(sv + kk * 2048, C::KV_CHUNK), idesc_o,
                      (j | kk) != 0);
-        mma_commit(&kv_empty[st]);
+        mma_commit(&v_empty[st]);
         mma_commit(&pv_done[j & 1]);
       }
     }
@@ -269,7 +283,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
         if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status)) goto done;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < HD; c += 32) {
+        for (int c = 0; c < DV; c += 32) {
           uint32_t t[32];
           tmem_ld32(lane_base + C::O_COL + c, t);
           tmem_ld_wait_regs(t);
@@ -313,9 +327,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD>::CTAS_PER_SM)
     if (gated && !mbar_wait(g_full, 0, a.status)) goto done;
     const int row = qs + r;
     const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-    __nv_bfloat16* orow = a.out + (int64_t)(q0 + row) * a.ldo + (int64_t)head * HD;
+    __nv_bfloat16* orow = a.out + (int64_t)(q0 + row) * a.ldo + (int64_t)head * HD + vcol;
 #pragma unroll 1
-    for (int c = 0; c < HD; c += 32) {
+    for (int c = 0; c < DV; c += 32) {
       uint32_t t[32];
       if (n_tiles > 0) {
         tmem_ld32(lane_base + C::O_COL + c, t);  // warp-collective: every lane loads, valid rows store
@@ -366,10 +380,10 @@ done:
   }
 }
 
-template <int HD>
+template <int HD, int DV>
 int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, int64_t tq, int64_t tk,
            const Args& a, int64_t total_q, cudaStream_t stream) {
-  using C = Cfg<HD>;
+  using C = Cfg<HD, DV>;
   CUtensorMap mq, mk, mv;
   const auto dt = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   int rc = make_tma_2d(&mq, q, dt, 2, (uint64_t)ldq, (uint64_t)tq, (uint64_t)ldq, 64, C::BM,
@@ -383,7 +397,7 @@ int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v
     rc = make_tma_2d(&mg, a.gate, dt, 2, (uint64_t)a.ldg, (uint64_t)tq, (uint64_t)a.ldg, 64, C::BM,
                      CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  auto kernel = attention_kernel<HD>;
+  auto kernel = attention_kernel<HD, DV>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -396,7 +410,7 @@ int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v
   // Upper bound on query tiles over all sequences: sum(ceil(Lq / BM)) <= total_q / BM + num_seqs.
   const int64_t tiles = total_q / C::BM + a.num_seqs;
   if (tiles > 0x7fffffff) return set_error(KD_ERR_ARGUMENT, "attention: too many query tiles");
-  dim3 grid((unsigned)tiles, (unsigned)a.hq);
+  dim3 grid((unsigned)tiles, (unsigned)a.hq, (unsigned)C::SLICES);
   kernel<<<grid, THREADS, C::SMEM, stream>>>(mq, mk, mv, mg, a);
   return record_cuda_error(cudaGetLastError(), "attention: launch");
 }
@@ -441,12 +455,14 @@ extern "C" int kd_attention_varlen(const void* q, int64_t ldq, const void* k, in
   const int64_t tk = total_k;
   switch (head_dim) {
     case 64:
-      return fa::launch<64>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
+      return fa::launch<64, 64>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
     case 128:
-      return fa::launch<128>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
+      return fa::launch<128, 128>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
     case 256:
-      return fa::launch<256>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
+      return fa::launch<256, 256>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
+    case 512:
+      return fa::launch<512, 256>(q, ldq, k, ldk, v, ldv, total_q, tk, a, total_q, stream);
     default:
-      return set_error(KD_ERR_ARGUMENT, "attention: head_dim must be 64, 128 or 256");
+      return set_error(KD_ERR_ARGUMENT, "attention: head_dim must be 64, 128, 256 or 512");
   }
 }

@@ -286,7 +286,7 @@ __global__ void qkv_norm_rope_kernel(const __nv_bfloat16* __restrict__ qkv, int6
                                      const float* __restrict__ sin_tab, int rot, __nv_bfloat16* __restrict__ q,
                                      __nv_bfloat16* __restrict__ k, __nv_bfloat16* __restrict__ v,
                                      __nv_bfloat16* __restrict__ gate) {
-  constexpr int PER = HD / 32;  // elements per lane (2, 4 or 8)
+  constexpr int PER = HD / 32;  // elements per lane (2, 4, 8 or 16)
   __shared__ float stage[WARPS][HD];
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
@@ -521,8 +521,9 @@ extern "C" int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const
     KD_QKV_CASE(64)
     KD_QKV_CASE(128)
     KD_QKV_CASE(256)
+    KD_QKV_CASE(512)
     default:
-      return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: head_dim must be 64, 128 or 256");
+      return set_error(KD_ERR_ARGUMENT, "qkv_norm_rope: head_dim must be 64, 128, 256 or 512");
   }
 #undef KD_QKV_CASE
   return record_cuda_error(cudaGetLastError(), "qkv_norm_rope: launch");

@@ -94,39 +94,68 @@ class Layer:
 
 
 class Workspace:
-    """Activation buffers for packs of up to ``capacity`` tokens (allocated once, reused by every layer and pack)."""
+    """Activation buffers for packs of up to ``capacity`` tokens (allocated once, reused by every layer and pack).
+    Per-head buffers are flat, sized for the widest layer kind (Gemma's global layers may have their own head size),
+    and viewed per layer."""
 
     def __init__(self, spec: Spec, capacity: int, device: torch.device, fp8: bool, inter_pad: int,
                  stored_qkv: bool) -> None:
-        t, h, hd = capacity, spec.hidden, spec.head_dim
+        t, h = capacity, spec.hidden
         bf = dict(dtype=torch.bfloat16, device=device)
+        kinds = set(spec.layer_types())
+        q_cols = max(spec.heads * spec.attn_dims(kind)[0] for kind in kinds)
+        kv_cols = max(spec.attn_dims(kind)[0] * spec.attn_dims(kind)[1] for kind in kinds)
         self.capacity = capacity
         self.h = torch.empty(t, h, **bf)
         self.x = torch.empty(t, h, **bf)
-        # the stored projection, only for the unfused QKV path
-        self.qkv = torch.empty(t, spec.qkv_width, **bf) if stored_qkv else None
-        rot = int(hd * spec.partial_rotary) if spec.family == "qwen" else hd
+        # the stored projection, only for layers that take the unfused QKV path
+        self._qkv = torch.empty(t * max(spec.qkv_width_of(k) for k in kinds), **bf) if stored_qkv else None
         # per rotary kind, the pack's rotary factors: (rot / 2, T) contiguous, viewed from a flat buffer per pack
-        self.rot_half = rot // 2
-        self._cs = {kind: torch.empty(self.rot_half * t, dtype=torch.int32, device=device)
-                    for kind in set(spec.layer_types())}
-        self.q = torch.empty(t, spec.heads, hd, **bf)
-        self.k = torch.empty(t, spec.kv_heads, hd, **bf)
-        self.v = torch.empty(t, spec.kv_heads, hd, **bf)
-        self.gate = torch.empty(t, spec.heads * hd, **bf) if spec.family == "qwen" else None
-        self.o = torch.empty(t, spec.heads * hd, **bf)
+        self._rot_half = {kind: rotary_width(spec, kind) // 2 for kind in kinds}
+        self._cs = {kind: torch.empty(half * t, dtype=torch.int32, device=device)
+                    for kind, half in self._rot_half.items()}
+        self._q = torch.empty(t * q_cols, **bf)
+        self._k = torch.empty(t * kv_cols, **bf)
+        self._v = torch.empty(t * kv_cols, **bf)
+        self._gate = torch.empty(t * q_cols, **bf) if spec.family == "qwen" else None
+        self._o = torch.empty(t * q_cols, **bf)
         self.a = torch.empty(t, h, **bf)
         self.m = torch.empty(t, inter_pad, **bf)
         if fp8:
-            width = max(h, spec.heads * hd, inter_pad)
+            width = max(h, q_cols, inter_pad)
             self.xq = torch.empty(t * width, dtype=torch.float8_e4m3fn, device=device)
             self.xs = torch.empty(t, dtype=torch.float32, device=device)
+
+    @staticmethod
+    def _view(flat: torch.Tensor, *shape: int) -> torch.Tensor:
+        return flat[: math.prod(shape)].view(*shape)
+
+    def heads(self, spec: Spec, kind: str, rows: int) -> tuple:
+        """(q (rows, Hq, hd), k, v (rows, Hkv, hd), gate (rows, Hq * hd) or None) for a layer of ``kind``."""
+        hd, hkv = spec.attn_dims(kind)
+        gate = None if self._gate is None else self._view(self._gate, rows, spec.heads * hd)
+        return (self._view(self._q, rows, spec.heads, hd), self._view(self._k, rows, hkv, hd),
+                self._view(self._v, rows, hkv, hd), gate)
+
+    def o(self, spec: Spec, kind: str, rows: int) -> torch.Tensor:
+        return self._view(self._o, rows, spec.heads * spec.attn_dims(kind)[0])
+
+    def qkv(self, spec: Spec, kind: str, rows: int) -> torch.Tensor:
+        return self._view(self._qkv, rows, spec.qkv_width_of(kind))
 
     def e4m3(self, rows: int, cols: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.xq[: rows * cols].view(rows, cols), self.xs[:rows]
 
     def cs(self, kind: str, tokens: int) -> torch.Tensor:
-        return self._cs[kind][: self.rot_half * tokens].view(self.rot_half, tokens)
+        half = self._rot_half[kind]
+        return self._cs[kind][: half * tokens].view(half, tokens)
+
+
+def rotary_width(spec: Spec, kind: str) -> int:
+    """Rotated dims of a layer of ``kind`` (the rotate-half span): Qwen head_dim * partial_rotary; Gemma the whole head
+    (proportional RoPE spans the head too, its unrotated pairs having frequency 0)."""
+    hd = spec.attn_dims(kind)[0]
+    return int(hd * spec.partial_rotary) if spec.family == "qwen" else hd
 
 
 class Packed(torch.nn.Module):
@@ -142,8 +171,10 @@ class Packed(torch.nn.Module):
         attention = spec.attention if attention is None else attention
         if attention not in ("causal", "bidirectional"):
             raise ValueError(f"attention must be 'causal' or 'bidirectional', not {attention!r}")
-        if spec.head_dim not in (64, 128, 256):
-            raise ValueError(f"head_dim {spec.head_dim} is not one of the kernels' 64, 128, 256")
+        for kind in set(spec.layer_types()):
+            hd = spec.attn_dims(kind)[0]
+            if hd not in (64, 128, 256, 512):
+                raise ValueError(f"head size {hd} ({kind}) is not one of the kernels' 64, 128, 256, 512")
         self.spec = spec
         self.device = torch.device(device)
         self.attention_mode = attention
@@ -167,14 +198,17 @@ class Packed(torch.nn.Module):
         norm_w = (lambda key: _tensor(weights[key], dev))
         for i in range(s.layers):
             p = f"layers.{i}."
-            wq, wk, wv = (_tensor(weights[p + n], dev) for n in ("q_proj", "k_proj", "v_proj"))
+            wq, wk = (_tensor(weights[p + n], dev) for n in ("q_proj", "k_proj"))
+            # attention_k_eq_v: the values are the key projection itself (families/gemma/packed.py:188); the kernels'
+            # layout repeats the key rows in the value columns (the same products, so bit-equal raw values)
+            wv = wk if s.shares_kv(self.types[i]) else _tensor(weights[p + "v_proj"], dev)
             qkv: list[tuple[Projection, int, int]] = []
             if fp8 and s.family == "qwen" and min(wk.shape[0], wv.shape[0]) < QWEN_FP8_MIN_FEATURES:
                 # Qwen keeps narrow projections in bf16: q on its own, k and v together.
                 qkv.append((Projection.of(wq, wq.shape[0] >= QWEN_FP8_MIN_FEATURES), 0, wq.shape[0]))
                 qkv.append((Projection.of(torch.cat([wk, wv]), False), wq.shape[0], wk.shape[0] + wv.shape[0]))
             else:
-                qkv.append((Projection.of(torch.cat([wq, wk, wv]), fp8), 0, s.qkv_width))
+                qkv.append((Projection.of(torch.cat([wq, wk, wv]), fp8), 0, s.qkv_width_of(self.types[i])))
             gate_up = interleave_gate_up(_tensor(weights[p + "gate_proj"], dev), _tensor(weights[p + "up_proj"], dev))
             down = _tensor(weights[p + "down_proj"], dev)
             if self.inter_pad != s.intermediate:
@@ -192,10 +226,12 @@ class Packed(torch.nn.Module):
                                        else weights[p + "layer_scalar"].reshape(1), dev)
             self.layers.append(layer)
         self._inv_freq = {kind: self._inv_freq_of(kind) for kind in set(self.types)}
-        rot = int(s.head_dim * s.partial_rotary) if s.family == "qwen" else s.head_dim
-        #: The QKV projection's epilogue does the norms and RoPE (kd_qkv_projection) when its shape allows:
-        #: width a multiple of 256 and rotary width a multiple of 32; otherwise GEMM + kd_qkv_norm_rope.
-        self.fused_qkv = s.qkv_width % 256 == 0 and rot % 32 == 0
+        #: Per layer kind, whether the QKV projection's epilogue does the norms and RoPE (kd_qkv_projection): width a
+        #: multiple of 256, rotary width a multiple of 32, a head within one 256-wide tile; otherwise GEMM +
+        #: kd_qkv_norm_rope.
+        self.fused_kinds = {kind for kind in set(self.types)
+                            if s.qkv_width_of(kind) % 256 == 0 and rotary_width(s, kind) % 32 == 0
+                            and s.attn_dims(kind)[0] <= 256}
         self._tables: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
         self._workspace: Workspace | None = None
 
@@ -220,7 +256,9 @@ class Packed(torch.nn.Module):
             a = layer.self_attn
             for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
                 if getattr(a, name, None) is None:
-                    raise NotImplementedError("layers whose keys and values share one projection are not built")
+                    if name == "v_proj" and family == "gemma" and getattr(config, "attention_k_eq_v", False):
+                        continue  # attention_k_eq_v: the values are the key projection
+                    raise NotImplementedError(f"layer {i} has no {name}")
                 weights[p + name] = getattr(a, name).weight
             weights[p + "q_norm"] = a.q_norm.weight
             weights[p + "k_norm"] = a.k_norm.weight
@@ -242,11 +280,18 @@ class Packed(torch.nn.Module):
         else:
             rope = config.rope_parameters
             every = 6
+            full = rope["full_attention"]
+            proportional = full.get("rope_type", "default") == "proportional"
             spec = Spec("gemma", len(lm.layers), config.hidden_size, heads, kv_heads, head_dim,
                         config.intermediate_size, config.vocab_size, eps=config.rms_norm_eps,
-                        rope_theta=rope["full_attention"]["rope_theta"],
+                        rope_theta=full["rope_theta"],
                         rope_theta_local=rope["sliding_attention"]["rope_theta"], window=config.sliding_window,
-                        global_every=every, logit_cap=config.final_logit_softcapping)
+                        global_every=every, logit_cap=config.final_logit_softcapping,
+                        global_head_dim=getattr(config, "global_head_dim", None) or head_dim,
+                        global_kv_heads=getattr(config, "num_global_key_value_heads", None),
+                        k_eq_v=bool(getattr(config, "attention_k_eq_v", False)),
+                        global_rope="proportional" if proportional else "default",
+                        global_partial_rotary=full.get("partial_rotary_factor", 1.0) if proportional else 0.25)
             if kinds != spec.layer_types():
                 raise NotImplementedError(f"layer pattern {kinds} is not 5 sliding : 1 global")
         device = next(lm.parameters()).device
@@ -257,14 +302,21 @@ class Packed(torch.nn.Module):
     # ---------------------------------------------------------------- rotary tables
 
     def _inv_freq_of(self, kind: str) -> torch.Tensor:
-        """Transformers' default inv_freq (computed in float32 on the host, as the backbone's rotary module does)."""
+        """Transformers' inv_freq for a layer of ``kind``, computed in float32 on the host as the backbone's rotary
+        module does: default RoPE 1 / theta^(2i / rot); Gemma 4's proportional RoPE (global layers) 1 / theta^(2i / hd)
+        for the first int(partial * hd // 2) pairs and 0 for the rest (modeling_rope_utils proportional)."""
         s = self.spec
+        rot = rotary_width(s, kind)
         if s.family == "qwen":
-            theta, rot = s.rope_theta, int(s.head_dim * s.partial_rotary)
+            theta = s.rope_theta
         else:
             theta = s.rope_theta if kind == "full_attention" else s.rope_theta_local
-            rot = s.head_dim
-        inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
+        if s.family == "gemma" and kind == "full_attention" and s.global_rope == "proportional":
+            angles = int(s.global_partial_rotary * rot // 2)
+            inv = 1.0 / (theta ** (torch.arange(0, 2 * angles, 2, dtype=torch.int64).float() / rot))
+            inv = torch.cat([inv, torch.zeros(rot // 2 - angles, dtype=torch.float32)])
+        else:
+            inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.int64).float() / rot))
         return inv.to(self.device)
 
     def tables(self, kind: str, positions: int) -> tuple[torch.Tensor, torch.Tensor]:
@@ -278,7 +330,7 @@ class Packed(torch.nn.Module):
     def workspace(self, tokens: int) -> Workspace:
         if self._workspace is None or self._workspace.capacity < tokens:
             self._workspace = None
-            stored = not self.fused_qkv or any(len(layer.qkv) > 1 for layer in self.layers)
+            stored = any(not self._fused(layer) for layer in self.layers)
             self._workspace = Workspace(self.spec, tokens, self.device, self.fp8, self.inter_pad, stored)
         return self._workspace
 
@@ -356,21 +408,25 @@ class Packed(torch.nn.Module):
         for layer in self.layers[:-1] if self.prune_last else self.layers:
             q, k, v, gate = self._attention_inputs(layer, h, p, ws, rope_cs)
             window = (self.window - 1, 0) if layer.kind == "sliding_attention" else self.full_window
+            o_buf = ws.o(s, layer.kind, t)
             if plan is None:
                 o = ops.attention_varlen(q, k, v, p.cu, p.cu, int(p.max_length), self._scale, window, gate=gate,
-                                         out=ws.o[:t])
+                                         out=o_buf)
             else:  # each virtual sequence's keys: the shared block (or its window tail), then its own rows
                 rows, k_cu = (plan.s_rows, plan.s_cu) if layer.kind == "sliding_attention" else \
                     (plan.g_rows, plan.g_cu)
                 kg, vg = ops.gather_rows(k, rows), ops.gather_rows(v, rows)
                 o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, self._scale, window, gate=gate,
-                                         out=ws.o[:t])
+                                         out=o_buf)
             self._after_attention(layer, h, o, ws)
         return h
 
     @property
     def _scale(self) -> float:
         return self.spec.head_dim ** -0.5 if self.spec.family == "qwen" else 1.0
+
+    def _fused(self, layer: Layer) -> bool:
+        return layer.kind in self.fused_kinds and len(layer.qkv) == 1
 
     def _attention_inputs(self, layer: Layer, h: torch.Tensor, p: Any, ws: Workspace,
                           rope_cs: dict[str, torch.Tensor]) -> tuple:
@@ -385,22 +441,23 @@ class Packed(torch.nn.Module):
         bf16_qkv = any(not proj.fp8 for proj, _, _ in layer.qkv)
         x, x8 = self._normed(ws, h, layer.input_norm, mode, bf16_qkv, fp8_qkv)
         cos, sin = self.tables(layer.kind, int(p.max_length))  # a position is below its sequence's length
-        heads_out = (ws.q[:t], ws.k[:t], ws.v[:t], ws.gate[:t] if qwen else None)
+        heads_out = ws.heads(s, layer.kind, t)
+        hd, hkv = s.attn_dims(layer.kind)
         v_mode = -1 if qwen else ops.NORM_NONE
-        if self.fused_qkv and len(layer.qkv) == 1:
+        if self._fused(layer):
             # one GEMM whose epilogue normalizes, rotates and scatters the heads (kd_qkv_projection)
             if layer.kind not in rope_cs:
                 rope_cs[layer.kind] = ops.rope_gather(seqpos, cos, sin, out=ws.cs(layer.kind, t))
             proj = layer.qkv[0][0]
             a_in, sa = (x8[0], x8[1]) if proj.fp8 else (x, None)
             return ops.qkv_projection(
-                a_in, proj.weight, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm,
+                a_in, proj.weight, seqpos, s.heads, hkv, hd, qwen, layer.q_norm, layer.k_norm,
                 mode, v_mode, s.eps, rope_cs[layer.kind], cos.shape[1], out=heads_out, scale_a=sa,
                 scale_w=proj.scale)
-        qkv = ws.qkv[:t]
+        qkv = ws.qkv(s, layer.kind, t)
         for proj, col, width in layer.qkv:
             self._project(proj, x, x8, qkv[:, col:col + width] if width != qkv.shape[1] else qkv)
-        return ops.qkv_norm_rope(qkv, seqpos, s.heads, s.kv_heads, s.head_dim, qwen, layer.q_norm, layer.k_norm,
+        return ops.qkv_norm_rope(qkv, seqpos, s.heads, hkv, hd, qwen, layer.q_norm, layer.k_norm,
                                  mode, v_mode, s.eps, cos, sin, out=heads_out)
 
     def _after_attention(self, layer: Layer, h: torch.Tensor, o: torch.Tensor, ws: Workspace) -> None:
@@ -443,7 +500,8 @@ class Packed(torch.nn.Module):
             q_cu, k_cu = plan.m_cu, plan.g_cu
             k, v = ops.gather_rows(k, plan.g_rows), ops.gather_rows(v, plan.g_rows)
         max_q = int(p.max_markers) if plan is None else 1  # a virtual sequence reads out at most one marker
-        o = ops.attention_varlen(qm, k, v, q_cu, k_cu, max_q, self._scale, (-1, -1), gate=gm, out=ws.o[:n])
+        o = ops.attention_varlen(qm, k, v, q_cu, k_cu, max_q, self._scale, (-1, -1), gate=gm,
+                                 out=ws.o(self.spec, layer.kind, n))
         hm = ops.gather_rows(h, markers)
         self._after_attention(layer, hm, o, ws)
         return hm

@@ -40,9 +40,37 @@ class Spec:
     attention: str = "causal"
     logit_cap: float | None = None
     codes: int = 3  # readout rows
+    # Gemma 4 global layers (Gemma4TextAttention): their own head size, and with attention_k_eq_v no v_proj (the
+    # values are the key projection, v-normed) and their own key/value head count; proportional RoPE rotates the
+    # first global_partial_rotary of the head's frequency pairs and leaves the rest unrotated.
+    global_head_dim: int | None = None  # None: head_dim
+    global_kv_heads: int | None = None  # with k_eq_v; None: kv_heads
+    k_eq_v: bool = False
+    global_rope: str = "default"  # or "proportional"
+    global_partial_rotary: float = 0.25
 
     def as_dict(self) -> dict:
         return asdict(self)
+
+    def attn_dims(self, kind: str) -> tuple[int, int]:
+        """(head size, key/value heads) of a layer of ``kind``."""
+        if self.family == "gemma" and kind == "full_attention":
+            hkv = (self.global_kv_heads or self.kv_heads) if self.k_eq_v else self.kv_heads
+            return self.global_head_dim or self.head_dim, hkv
+        return self.head_dim, self.kv_heads
+
+    def shares_kv(self, kind: str) -> bool:
+        """Whether a layer of ``kind`` takes its values from the key projection (attention_k_eq_v)."""
+        return self.family == "gemma" and kind == "full_attention" and self.k_eq_v
+
+    def q_width_of(self, kind: str) -> int:
+        return self.heads * self.attn_dims(kind)[0] * (2 if self.family == "qwen" else 1)
+
+    def qkv_width_of(self, kind: str) -> int:
+        """Columns of a layer's [q | k | v] projection as the kernels lay it out (a shared-key layer's v columns
+        repeat its k projection)."""
+        hd, hkv = self.attn_dims(kind)
+        return self.q_width_of(kind) + 2 * hkv * hd
 
     @property
     def q_width(self) -> int:
@@ -61,10 +89,13 @@ class Spec:
                 for i in range(self.layers)]
 
     def gemm_flops_per_token(self) -> float:
-        """2 * sum(K * N) over one token's projections, all layers."""
-        h, hd = self.hidden, self.head_dim
-        per_layer = h * self.qkv_width + self.heads * hd * h + h * 2 * self.intermediate + self.intermediate * h
-        return 2.0 * per_layer * self.layers
+        """2 * sum(K * N) over one token's projections, all layers (a shared-key layer has no value projection)."""
+        h, total = self.hidden, 0
+        for kind in self.layer_types():
+            hd, hkv = self.attn_dims(kind)
+            kv = (1 if self.shares_kv(kind) else 2) * hkv * hd
+            total += h * (self.q_width_of(kind) + kv) + self.heads * hd * h + 3 * h * self.intermediate
+        return 2.0 * total
 
 
 #: The benchmark configurations (BASELINE.json configs 1-5).
@@ -90,7 +121,7 @@ def numpy_weights(spec: Spec, seed: int = 0, std: float = 0.02) -> dict[str, np.
     norm rule shows: Qwen's ``(1 + w)`` weights ~ N(0, 0.1), Gemma's ``w`` ~ 1 + N(0, 0.1); Gemma layer scalars in
     [0.8, 1.0]; readout rows ~ N(0, std)."""
     rng = np.random.default_rng(seed)
-    h, hd, hq, hkv, inter = spec.hidden, spec.head_dim, spec.heads, spec.kv_heads, spec.intermediate
+    h, hq, inter = spec.hidden, spec.heads, spec.intermediate
 
     def normal(*shape, scale=std):
         return _bf16_exact(rng.standard_normal(shape, dtype=np.float32) * np.float32(scale))
@@ -102,15 +133,16 @@ def numpy_weights(spec: Spec, seed: int = 0, std: float = 0.02) -> dict[str, np.
     # Gemma's attention has scale 1.0 over q/k normalized to unit RMS: with identity-like q/k norm weights a random
     # model's logits have std sqrt(head_dim) and its softmax is one-hot, chaotic under any rounding. Trained
     # checkpoints learn small q/k norm weights; the synthetic ones are scaled to head_dim^-1/4 (logit std ~ 1).
-    qk_base = spec.head_dim ** -0.25 if spec.family == "gemma" else 1.0
-
     w: dict[str, np.ndarray] = {"embed_tokens": normal(spec.vocab, h)}
-    for i in range(spec.layers):
+    for i, kind in enumerate(spec.layer_types()):
         p = f"layers.{i}."
+        hd, hkv = spec.attn_dims(kind)
+        qk_base = hd ** -0.25 if spec.family == "gemma" else 1.0
         w[p + "input_layernorm"] = norm_weight(h)
-        w[p + "q_proj"] = normal(spec.q_width, h)
+        w[p + "q_proj"] = normal(spec.q_width_of(kind), h)
         w[p + "k_proj"] = normal(hkv * hd, h)
-        w[p + "v_proj"] = normal(hkv * hd, h)
+        if not spec.shares_kv(kind):
+            w[p + "v_proj"] = normal(hkv * hd, h)
         w[p + "q_norm"] = norm_weight(hd, qk_base)
         w[p + "k_norm"] = norm_weight(hd, qk_base)
         w[p + "o_proj"] = normal(h, hq * hd)
@@ -131,7 +163,7 @@ def device_weights(spec: Spec, seed: int, device: torch.device, std: float = 0.0
     """The same layout as ``numpy_weights`` drawn directly on ``device`` in bf16 (full-size benchmark models, where a
     host-side draw would take minutes): a torch generator seeded with ``seed`` on that device."""
     gen = torch.Generator(device=device).manual_seed(seed)
-    h, hd, hq, hkv, inter = spec.hidden, spec.head_dim, spec.heads, spec.kv_heads, spec.intermediate
+    h, hq, inter = spec.hidden, spec.heads, spec.intermediate
 
     def normal(*shape, scale=std):
         return (torch.randn(*shape, generator=gen, device=device, dtype=torch.float32) * scale).bfloat16()
@@ -140,15 +172,16 @@ def device_weights(spec: Spec, seed: int, device: torch.device, std: float = 0.0
         w = torch.randn(n, generator=gen, device=device, dtype=torch.float32) * 0.1
         return (w if spec.family == "qwen" else base * (1.0 + w)).bfloat16()
 
-    qk_base = spec.head_dim ** -0.25 if spec.family == "gemma" else 1.0
-
     w: dict[str, torch.Tensor] = {"embed_tokens": normal(spec.vocab, h)}
-    for i in range(spec.layers):
+    for i, kind in enumerate(spec.layer_types()):
         p = f"layers.{i}."
+        hd, hkv = spec.attn_dims(kind)
+        qk_base = hd ** -0.25 if spec.family == "gemma" else 1.0
         w[p + "input_layernorm"] = norm_weight(h)
-        w[p + "q_proj"] = normal(spec.q_width, h)
+        w[p + "q_proj"] = normal(spec.q_width_of(kind), h)
         w[p + "k_proj"] = normal(hkv * hd, h)
-        w[p + "v_proj"] = normal(hkv * hd, h)
+        if not spec.shares_kv(kind):
+            w[p + "v_proj"] = normal(hkv * hd, h)
         w[p + "q_norm"] = norm_weight(hd, qk_base)
         w[p + "k_norm"] = norm_weight(hd, qk_base)
         w[p + "o_proj"] = normal(h, hq * hd)

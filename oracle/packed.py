@@ -103,13 +103,21 @@ def gelu_tanh(x: np.ndarray) -> np.ndarray:
                                                             (x + np.float32(0.044715) * x ** 3)))
 
 
-def rope_tables(positions: np.ndarray, head_dim: int, theta: float, partial: float, mode: str
-                ) -> tuple[np.ndarray, np.ndarray]:
+def rope_tables(positions: np.ndarray, head_dim: int, theta: float, partial: float, mode: str,
+                proportional: bool = False) -> tuple[np.ndarray, np.ndarray]:
     """cos/sin (T, rot) at ``positions``: inv_freq = 1 / theta^(arange(0, rot, 2) / rot), emb = cat(f, f)
     (Transformers' default rotary embedding, as Qwen3_5TextRotaryEmbedding / Gemma4TextRotaryEmbedding compute it, and
-    cast to the activations' dtype)."""
-    rot = int(head_dim * partial)
-    inv_freq = (1.0 / (np.float32(theta) ** (np.arange(0, rot, 2, dtype=np.float32) / np.float32(rot))))
+    cast to the activations' dtype). ``proportional`` (Transformers' "proportional" rope of Gemma 4 global layers):
+    rot = head_dim, the first int(partial * head_dim // 2) frequencies 1 / theta^(2i / head_dim), the rest 0 (those
+    pairs stay unrotated)."""
+    if proportional:
+        rot = head_dim
+        angles = int(partial * head_dim // 2)
+        inv_freq = 1.0 / (np.float32(theta) ** (np.arange(0, 2 * angles, 2, dtype=np.float32) / np.float32(head_dim)))
+        inv_freq = np.concatenate([inv_freq.astype(np.float32), np.zeros(head_dim // 2 - angles, np.float32)])
+    else:
+        rot = int(head_dim * partial)
+        inv_freq = (1.0 / (np.float32(theta) ** (np.arange(0, rot, 2, dtype=np.float32) / np.float32(rot))))
     inv_freq = inv_freq.astype(np.float32)
     freqs = positions.astype(np.float32)[:, None] * inv_freq[None, :]
     emb = np.concatenate([freqs, freqs], axis=-1)
@@ -290,7 +298,15 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
     global layers non-causal (:168-170, ``_global`` with causal False); the reference's marker-only last layer
     (:267-281) equals the marker rows of the whole last layer (a marker is its virtual sequence's last token), which
     is what this restatement computes (pinned by the ``gemma_bidir`` and ``gemma_blocks_bidir`` fixtures)."""
-    eps, hq, hkv, hd, w_len = spec["eps"], spec["heads"], spec["kv_heads"], spec["head_dim"], spec["window"]
+    eps, hq, w_len = spec["eps"], spec["heads"], spec["window"]
+    k_eq_v = bool(spec.get("k_eq_v", False))
+
+    def dims(kind):  # Gemma4TextAttention: global layers' head size and (attention_k_eq_v) key/value heads
+        if kind != "full_attention":
+            return spec["head_dim"], spec["kv_heads"]
+        hkv = (spec.get("global_kv_heads") or spec["kv_heads"]) if k_eq_v else spec["kv_heads"]
+        return spec.get("global_head_dim") or spec["head_dim"], hkv
+
     if fp8:
         weights = quantize_weights(weights)
     ids, seqpos, cu = pack["input_ids"], pack["seqpos"], pack["cu"]
@@ -300,9 +316,12 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
         scale = bf16(np.array([scale]))[0]
     h = _round(weights["embed_tokens"][ids] * scale, mode)
     types = gemma_layer_types(spec)
+    proportional = spec.get("global_rope", "default") == "proportional"
     tables = {
-        "sliding_attention": rope_tables(seqpos, hd, spec["rope_theta_local"], 1.0, mode),
-        "full_attention": rope_tables(seqpos, hd, spec["rope_theta"], 1.0, mode),
+        "sliding_attention": rope_tables(seqpos, dims("sliding_attention")[0], spec["rope_theta_local"], 1.0, mode),
+        "full_attention": rope_tables(seqpos, dims("full_attention")[0], spec["rope_theta"],
+                                      spec.get("global_partial_rotary", 1.0) if proportional else 1.0, mode,
+                                      proportional),
     }
     causal_global = spec.get("attention", "causal") == "causal"
     segs = pack.get("segment_ids")
@@ -315,12 +334,14 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
     for i in range(spec["layers"]):
         p = f"layers.{i}."
         cos, sin = tables[types[i]]
+        hd, hkv = dims(types[i])
         x, xq = normed(h, weights[p + "input_layernorm"])
         q = linear(x, weights[p + "q_proj"], mode, fp8, xq).reshape(t, hq, hd)
         q = _round(apply_rope(rms_norm(q, weights[p + "q_norm"], eps, False), cos, sin), mode)
-        k = linear(x, weights[p + "k_proj"], mode, fp8, xq).reshape(t, hkv, hd)
-        k = _round(apply_rope(rms_norm(k, weights[p + "k_norm"], eps, False), cos, sin), mode)
-        v = linear(x, weights[p + "v_proj"], mode, fp8, xq).reshape(t, hkv, hd)
+        raw = linear(x, weights[p + "k_proj"], mode, fp8, xq).reshape(t, hkv, hd)
+        k = _round(apply_rope(rms_norm(raw, weights[p + "k_norm"], eps, False), cos, sin), mode)
+        # attention_k_eq_v: the values are the key projection itself (families/gemma/packed.py:188)
+        v = raw if p + "v_proj" not in weights else linear(x, weights[p + "v_proj"], mode, fp8, xq).reshape(t, hkv, hd)
         v = _round(rms_norm(v, None, eps, False), mode)
         if types[i] == "sliding_attention":
             window = (w_len - 1, 0)

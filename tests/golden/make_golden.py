@@ -113,7 +113,8 @@ def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
             layer.block_type = layer.layer_type  # harness alias (Transformers 5.5 naming)
             a = layer.self_attn
             for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
-                getattr(a, name).weight.copy_(to_torch(weights, p + name))
+                if getattr(a, name) is not None:  # attention_k_eq_v global layers have no v_proj
+                    getattr(a, name).weight.copy_(to_torch(weights, p + name))
             a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
             a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
             for name in ("gate_proj", "up_proj", "down_proj"):
@@ -127,15 +128,20 @@ def gemma_lm(spec: Spec, weights: dict[str, np.ndarray]):
     from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
     from transformers.models.gemma4.modeling_gemma4 import Gemma4TextModel
 
+    global_rope = {"rope_type": "default", "rope_theta": spec.rope_theta}
+    if spec.global_rope == "proportional":
+        global_rope = {"rope_type": "proportional", "rope_theta": spec.rope_theta,
+                       "partial_rotary_factor": spec.global_partial_rotary}
     config = Gemma4TextConfig(
         vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
         num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
-        head_dim=spec.head_dim, global_head_dim=spec.head_dim, num_global_key_value_heads=spec.kv_heads,
-        attention_k_eq_v=False, sliding_window=spec.window, layer_types=spec.layer_types(),
+        head_dim=spec.head_dim, global_head_dim=spec.global_head_dim or spec.head_dim,
+        num_global_key_value_heads=spec.global_kv_heads or spec.kv_heads, attention_k_eq_v=spec.k_eq_v,
+        sliding_window=spec.window, layer_types=spec.layer_types(),
         hidden_size_per_layer_input=0, final_logit_softcapping=spec.logit_cap, rms_norm_eps=spec.eps,
         hidden_activation="gelu_pytorch_tanh",
         rope_parameters={"sliding_attention": {"rope_type": "default", "rope_theta": spec.rope_theta_local},
-                         "full_attention": {"rope_type": "default", "rope_theta": spec.rope_theta}})
+                         "full_attention": global_rope})
     config._attn_implementation = "sdpa"
     lm = Gemma4TextModel(config).float().eval()
     with torch.no_grad():
@@ -145,7 +151,8 @@ def gemma_lm(spec: Spec, weights: dict[str, np.ndarray]):
             p = f"layers.{i}."
             a = layer.self_attn
             for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
-                getattr(a, name).weight.copy_(to_torch(weights, p + name))
+                if getattr(a, name) is not None:  # attention_k_eq_v global layers have no v_proj
+                    getattr(a, name).weight.copy_(to_torch(weights, p + name))
             a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
             a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
             for name in ("gate_proj", "up_proj", "down_proj"):
@@ -211,6 +218,11 @@ CASES = {
     "gemma_bidir": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
                                   attention="bidirectional"),
                         lengths=("uniform", 6, 8, 96), markers=(1, 1), fp8=False),
+    # Gemma 4's real global layers: head 512, keys = values (attention_k_eq_v, one key/value head), proportional
+    # RoPE over a quarter of the frequency pairs (families/gemma/global_attention.py, packed.py:183-193).
+    "gemma_global512": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
+                                      global_head_dim=512, global_kv_heads=1, k_eq_v=True, global_rope="proportional"),
+                            lengths=("uniform", 5, 8, 160), markers=(1, 1), fp8=False),
     "gemma_blocks_bidir": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
                                          attention="bidirectional"),
                                blocks=[(23, []), (21, [5, 7, 3]), (14, [4, 9]), (3, [20, 25])], fp8=False),

@@ -26,7 +26,31 @@ def test_workspace_views_are_contiguous():
     assert cs.shape == (32, 700) and cs.is_contiguous()
     q, s = ws.e4m3(700, 256)
     assert q.shape == (700, 256) and q.is_contiguous() and s.shape == (700,)
-    assert ws.q.shape == (1000, 4, 64) and ws.gate.shape == (1000, 256) and ws.qkv is None
+    q, k, v, gate = ws.heads(spec, "full_attention", 700)
+    assert q.shape == (700, 4, 64) and k.shape == v.shape == (700, 2, 64) and gate.shape == (700, 256)
+    assert q.is_contiguous() and ws.o(spec, "full_attention", 700).shape == (700, 256) and ws._qkv is None
+
+
+def test_workspace_sizes_for_gemma_global_heads():
+    """Gemma 4 global layers with their own head size and shared key/value heads: buffers sized for the widest kind,
+    viewed per layer kind."""
+    from karpo_decision_b200.packed import rotary_width
+
+    spec = Spec("gemma", 6, 256, 4, 2, 64, 512, 100, global_head_dim=512, global_kv_heads=1, k_eq_v=True,
+                global_rope="proportional")
+    assert spec.attn_dims("full_attention") == (512, 1) and spec.attn_dims("sliding_attention") == (64, 2)
+    assert spec.qkv_width_of("full_attention") == 4 * 512 + 2 * 512 and spec.shares_kv("full_attention")
+    assert rotary_width(spec, "full_attention") == 512 and rotary_width(spec, "sliding_attention") == 64
+    ws = Workspace(spec, 100, torch.device("cpu"), fp8=False, inter_pad=512, stored_qkv=True)
+    q, k, v, gate = ws.heads(spec, "full_attention", 90)
+    assert q.shape == (90, 4, 512) and k.shape == (90, 1, 512) and gate is None
+    q, k, v, _ = ws.heads(spec, "sliding_attention", 90)
+    assert q.shape == (90, 4, 64) and v.shape == (90, 2, 64)
+    assert ws.qkv(spec, "full_attention", 90).shape == (90, 3072) and ws.cs("full_attention", 90).shape == (256, 90)
+    # the weights: no v_proj in the shared-key global layer, per-kind shapes elsewhere
+    w = numpy_weights(spec, 0)
+    assert "layers.5.v_proj" not in w and w["layers.5.q_proj"].shape == (2048, 256)
+    assert w["layers.5.k_proj"].shape == (512, 256) and w["layers.0.v_proj"].shape == (128, 256)
 
 
 def test_synthetic_lengths_fill_exactly():
