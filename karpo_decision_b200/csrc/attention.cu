@@ -70,6 +70,7 @@ struct Args {
 constexpr int THREADS = 192;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: rescale O when the row maximum grows by more than 2^8
 
+
 // 2^x with the hardware exponential (ex2.approx: relative error ~2^-22; the probabilities are rounded to bf16).
 KD_DEVICE float fast_exp2(float x) {
   float y;
@@ -270,9 +271,14 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
           if (!ok) sv[e] = -INFINITY;
         }
       }
-      float mraw = -INFINITY;
+      // row maximum over 8 independent chains (a single chain would serialize BN dependent max operations)
+      float mx[8];
 #pragma unroll
-      for (int e = 0; e < BN; ++e) mraw = fmaxf(mraw, sv[e]);
+      for (int e = 0; e < 8; ++e) mx[e] = sv[e];
+#pragma unroll
+      for (int e = 8; e < BN; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
+      const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       const float mt = mraw * a.scale_log2;  // the scale is positive: max commutes with it
       const float m_new = fmaxf(m_used, mt);
       const bool need = m_new > m_used + RESCALE_THRESHOLD || (m_used == -INFINITY && m_new != -INFINITY);
@@ -298,7 +304,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         m_used = m_new;
       }
       const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
-      float rs = 0.f;
+      float part[4] = {0.f, 0.f, 0.f, 0.f};  // the row sum over independent chains
 #pragma unroll
       for (int c = 0; c < BN; c += 64) {
         uint32_t pk[32];
@@ -306,12 +312,12 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         for (int e = 0; e < 32; ++e) {
           const float p0 = fast_exp2(fmaf(sv[c + 2 * e], a.scale_log2, neg_base));
           const float p1 = fast_exp2(fmaf(sv[c + 2 * e + 1], a.scale_log2, neg_base));
-          rs += p0 + p1;
+          part[e & 3] += p0 + p1;
           pk[e] = pack_bf16x2(p0, p1);
         }
         tmem_st32(s_addr + c / 2, pk);  // P_j over the score columns this thread has already read
       }
-      l_sum += rs;
+      l_sum += (part[0] + part[1]) + (part[2] + part[3]);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);

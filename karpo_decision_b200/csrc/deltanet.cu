@@ -1,0 +1,329 @@
+// Qwen3.5's Gated DeltaNet token mixer (families/qwen/packed.py:74-106), the kernels between its input projection
+// and its output projection:
+//   kd_conv_silu         depthwise causal convolution over the [q | k | v] channels, cut at sequence starts, + silu;
+//   kd_gated_delta_rule  the gated delta rule per (sequence, value head), its decay and write strength computed from
+//                        the projection's a and b columns;
+//   kd_gated_norm        Qwen3_5RMSNormGated: RMSNorm of each head's output times silu of the z gate.
+//
+// The delta rule here is the recurrent form: one CTA per (sequence, value head) holds the head's state S (dk x dv,
+// float32) in registers, two threads per value column each owning half of its dk rows, and walks the sequence token
+// by token. Queries and keys are L2-normalized (the reference's use_qk_l2norm_in_kernel), per chunk of tokens staged
+// in shared memory by the CTA's warps before the sequential walk.
+#include "common.cuh"
+#include "kd_internal.h"
+
+namespace kd {
+namespace dn {
+
+// ------------------------------------------------------------------------------------------------ convolution
+
+// out[t, c] = bf16(silu(sum_s w[c, K-1-s] x[t-s, c])) over taps s with seqpos[t] >= s: 8 channels of one row per
+// thread (16-byte loads), float32 sums in tap order.
+template <int K>
+__global__ void conv_silu_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t T, int C,
+                                 const __nv_bfloat16* __restrict__ w, const int64_t* __restrict__ seqpos,
+                                 __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  const int groups = C / 8;
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * groups) return;
+  const int64_t t = idx / groups;
+  const int c0 = (int)(idx % groups) * 8;
+  const int64_t pos = seqpos[t];
+  float taps[8][K];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+#pragma unroll
+    for (int k = 0; k < K; ++k) taps[e][k] = __bfloat162float(w[(int64_t)(c0 + e) * K + k]);
+  float acc[8];
+#pragma unroll
+  for (int s = 0; s < K; ++s) {
+    if (s > 0 && pos < s) break;
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + (t - s) * ldx + c0);
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(words[e]);
+      if (s == 0) {
+        acc[2 * e] = f.x * taps[2 * e][K - 1];
+        acc[2 * e + 1] = f.y * taps[2 * e + 1][K - 1];
+      } else {
+        acc[2 * e] = fmaf(f.x, taps[2 * e][K - 1 - s], acc[2 * e]);
+        acc[2 * e + 1] = fmaf(f.y, taps[2 * e + 1][K - 1 - s], acc[2 * e + 1]);
+      }
+    }
+  }
+  uint32_t packed[4];
+#pragma unroll
+  for (int e = 0; e < 4; ++e) packed[e] = pack_bf16x2(silu(acc[2 * e]), silu(acc[2 * e + 1]));
+  *reinterpret_cast<uint4*>(out + t * ldo + c0) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+}
+
+// ------------------------------------------------------------------------------------------------ delta rule
+
+constexpr int CHUNK = 16;  // tokens staged in shared memory per step of the walk
+
+template <int DK, int DV>
+struct Cfg {
+  static constexpr int THREADS = 2 * DV;  // two threads per value column
+  static constexpr int ROWS = DK / 2;     // state rows per thread
+  static constexpr int KSTRIDE = DK + 4;  // staged q / k row (the second half 16 bytes further: no bank conflict)
+  // shared memory: q and k rows (float32), v rows (float32), then g and beta
+  static constexpr int SMEM = (2 * CHUNK * KSTRIDE + CHUNK * DV + 2 * CHUNK) * 4;
+};
+
+struct Args {
+  const __nv_bfloat16* qkv;  // rows: [q nk*dk | k nk*dk | v nv*dv]
+  int64_t ldqkv;
+  const __nv_bfloat16* ab;  // rows: [b nv | a nv]
+  int64_t ldab;
+  const __nv_bfloat16* a_log;
+  const __nv_bfloat16* dt_bias;
+  const int32_t* cu;
+  int nk, nv;
+  __nv_bfloat16* out;
+  int64_t ldo;
+};
+
+KD_DEVICE float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+KD_DEVICE float softplus(float x) { return x > 20.f ? x : log1pf(expf(x)); }
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a) {
+  using C = Cfg<DK, DV>;
+  extern __shared__ float sm[];
+  float* q_s = sm;                              // [CHUNK][KSTRIDE]
+  float* k_s = q_s + CHUNK * C::KSTRIDE;        // [CHUNK][KSTRIDE]
+  float* v_s = k_s + CHUNK * C::KSTRIDE;        // [CHUNK][DV]
+  float* g_s = v_s + CHUNK * DV;                // [CHUNK]: decay factor exp(g)
+  float* b_s = g_s + CHUNK;                     // [CHUNK]: beta
+  const int seq = blockIdx.x;
+  const int head = blockIdx.y;                  // value head
+  const int khead = head / (a.nv / a.nk);       // its key head (repeat_interleave)
+  const int64_t t0 = a.cu[seq], t1 = a.cu[seq + 1];
+  const int tid = threadIdx.x;
+  const int col = tid >> 1;                     // value column
+  const int half = tid & 1;                     // rows [half * ROWS, half * ROWS + ROWS)
+  const int warp = tid / 32, lane = tid & 31;
+  constexpr int WARPS = C::THREADS / 32;
+  const float qscale = rsqrtf((float)DK);
+  const float decay_a = -expf(__bfloat162float(a.a_log[head]));
+  const float dt_bias = __bfloat162float(a.dt_bias[head]);
+  const int64_t kd = (int64_t)a.nk * DK;
+
+  float S[C::ROWS];
+#pragma unroll
+  for (int i = 0; i < C::ROWS; ++i) S[i] = 0.f;
+
+  for (int64_t c0 = t0; c0 < t1; c0 += CHUNK) {
+    const int n = t1 - c0 < CHUNK ? (int)(t1 - c0) : CHUNK;
+    __syncthreads();  // the previous chunk's rows have been read
+    // stage: one warp per token row at a time; q and k L2-normalized (eps 1e-6), q scaled by dk^-1/2
+    for (int r = warp; r < n; r += WARPS) {
+      const __nv_bfloat16* row = a.qkv + (c0 + r) * a.ldqkv;
+      const __nv_bfloat16* qr = row + (int64_t)khead * DK;
+      const __nv_bfloat16* kr = row + kd + (int64_t)khead * DK;
+      float qv[DK / 32], kv[DK / 32], sq = 0.f, sk = 0.f;
+#pragma unroll
+      for (int e = 0; e < DK / 32; ++e) {
+        qv[e] = __bfloat162float(qr[lane + 32 * e]);
+        kv[e] = __bfloat162float(kr[lane + 32 * e]);
+        sq += qv[e] * qv[e];
+        sk += kv[e] * kv[e];
+      }
+      const float iq = rsqrtf(warp_sum(sq) + 1e-6f) * qscale;
+      const float ik = rsqrtf(warp_sum(sk) + 1e-6f);
+#pragma unroll
+      for (int e = 0; e < DK / 32; ++e) {
+        const int d = lane + 32 * e;
+        const int at = d < C::ROWS ? d : d + 4;  // the second half of a staged row sits 16 bytes further
+        q_s[r * C::KSTRIDE + at] = qv[e] * iq;
+        k_s[r * C::KSTRIDE + at] = kv[e] * ik;
+      }
+      const __nv_bfloat16* vr = row + 2 * kd + (int64_t)head * DV;
+#pragma unroll
+      for (int e = 0; e < DV / 32; ++e) v_s[r * DV + lane + 32 * e] = __bfloat162float(vr[lane + 32 * e]);
+      if (lane == 0) {
+        const __nv_bfloat16* abr = a.ab + (c0 + r) * a.ldab;
+        const float b = __bfloat162float(abr[head]);
+        const float av = __bfloat162float(abr[a.nv + head]);
+        g_s[r] = expf(decay_a * softplus(av + dt_bias));               // exp(g), g = -exp(A_log) softplus(a + dt)
+        b_s[r] = bf16_round(1.0f / (1.0f + expf(-b)));                 // beta = sigmoid(b), a bf16 tensor op
+      }
+    }
+    __syncthreads();
+    // the walk: S = alpha S + k d^T with d = (v - alpha S^T k) beta, then o = S^T q
+    for (int r = 0; r < n; ++r) {
+      const float* kr = k_s + r * C::KSTRIDE + half * (C::ROWS + 4);
+      const float* qr = q_s + r * C::KSTRIDE + half * (C::ROWS + 4);
+      const float alpha = g_s[r], beta = b_s[r];
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < C::ROWS; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+        acc[0] = fmaf(S[i], k4.x, acc[0]);
+        acc[1] = fmaf(S[i + 1], k4.y, acc[1]);
+        acc[2] = fmaf(S[i + 2], k4.z, acc[2]);
+        acc[3] = fmaf(S[i + 3], k4.w, acc[3]);
+      }
+      float kvm = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+      kvm += __shfl_xor_sync(0xffffffffu, kvm, 1);
+      const float delta = (v_s[r * DV + col] - alpha * kvm) * beta;
+      float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int i = 0; i < C::ROWS; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+        const float4 q4 = *reinterpret_cast<const float4*>(qr + i);
+        S[i] = fmaf(k4.x, delta, S[i] * alpha);
+        S[i + 1] = fmaf(k4.y, delta, S[i + 1] * alpha);
+        S[i + 2] = fmaf(k4.z, delta, S[i + 2] * alpha);
+        S[i + 3] = fmaf(k4.w, delta, S[i + 3] * alpha);
+        o[0] = fmaf(S[i], q4.x, o[0]);
+        o[1] = fmaf(S[i + 1], q4.y, o[1]);
+        o[2] = fmaf(S[i + 2], q4.z, o[2]);
+        o[3] = fmaf(S[i + 3], q4.w, o[3]);
+      }
+      float ov = (o[0] + o[1]) + (o[2] + o[3]);
+      ov += __shfl_xor_sync(0xffffffffu, ov, 1);
+      if (half == 0) a.out[(c0 + r) * a.ldo + (int64_t)head * DV + col] = __float2bfloat16_rn(ov);
+    }
+  }
+}
+
+template <int DK, int DV>
+int launch_delta(const Args& a, int num_seqs, cudaStream_t stream) {
+  using C = Cfg<DK, DV>;
+  auto kernel = delta_rule_kernel<DK, DV>;
+  if (C::SMEM > 48 * 1024) {
+    static bool configured[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) return KD_ERR_ARGUMENT;
+    if (!configured[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+      if (e != cudaSuccess) return record_cuda_error(e, "gated_delta_rule: cudaFuncSetAttribute");
+      configured[dev] = true;
+    }
+  }
+  dim3 grid((unsigned)num_seqs, (unsigned)a.nv);
+  kernel<<<grid, C::THREADS, C::SMEM, stream>>>(a);
+  return record_cuda_error(cudaGetLastError(), "gated_delta_rule: launch");
+}
+
+// ------------------------------------------------------------------------------------------------ gated norm
+
+// One warp per (token, head): out = bf16(bf16(w * bf16(x rsqrt(mean(x^2) + eps))) * silu(float(z))).
+template <int DV>
+__global__ void gated_norm_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                  const __nv_bfloat16* __restrict__ z, int64_t ldz,
+                                  const __nv_bfloat16* __restrict__ w, int64_t T, int heads, float eps,
+                                  __nv_bfloat16* __restrict__ out, int64_t ldo) {
+  constexpr int PER = DV / 32;
+  const int64_t item = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const int lane = threadIdx.x & 31;
+  if (item >= T * heads) return;
+  const int64_t t = item / heads;
+  const int h = (int)(item % heads);
+  const __nv_bfloat16* xr = x + t * ldx + (int64_t)h * DV;
+  const __nv_bfloat16* zr = z + t * ldz + (int64_t)h * DV;
+  float v[PER], ss = 0.f;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    v[e] = __bfloat162float(xr[lane + 32 * e]);
+    ss += v[e] * v[e];
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / (float)DV + eps);
+  __nv_bfloat16* orow = out + t * ldo + (int64_t)h * DV;
+#pragma unroll
+  for (int e = 0; e < PER; ++e) {
+    const int d = lane + 32 * e;
+    const float normed = bf16_round(v[e] * inv);
+    const float weighted = bf16_round(__bfloat162float(w[d]) * normed);
+    orow[d] = __float2bfloat16_rn(weighted * silu(__bfloat162float(zr[d])));
+  }
+}
+
+}  // namespace dn
+}  // namespace kd
+
+using namespace kd;
+
+extern "C" int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const void* weight, int K,
+                            const int64_t* seqpos, void* out, int64_t ldo, cudaStream_t stream) {
+  if (T < 0 || C <= 0 || C % 8 || K < 1 || K > 4) return set_error(KD_ERR_ARGUMENT, "conv_silu: bad sizes");
+  if (T == 0) return KD_OK;
+  if (!x || !weight || !seqpos || !out) return set_error(KD_ERR_ARGUMENT, "conv_silu: null pointer");
+  if (ldx < C || ldo < C || ldx % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(out) & 15))
+    return set_error(KD_ERR_ARGUMENT, "conv_silu: rows must be 16-byte aligned and at least C wide");
+  const auto* xi = static_cast<const __nv_bfloat16*>(x);
+  const auto* wi = static_cast<const __nv_bfloat16*>(weight);
+  auto* oi = static_cast<__nv_bfloat16*>(out);
+  const int64_t n = T * (C / 8);
+  const unsigned blocks = (unsigned)((n + 255) / 256);
+  switch (K) {
+    case 1: dn::conv_silu_kernel<1><<<blocks, 256, 0, stream>>>(xi, ldx, T, C, wi, seqpos, oi, ldo); break;
+    case 2: dn::conv_silu_kernel<2><<<blocks, 256, 0, stream>>>(xi, ldx, T, C, wi, seqpos, oi, ldo); break;
+    case 3: dn::conv_silu_kernel<3><<<blocks, 256, 0, stream>>>(xi, ldx, T, C, wi, seqpos, oi, ldo); break;
+    default: dn::conv_silu_kernel<4><<<blocks, 256, 0, stream>>>(xi, ldx, T, C, wi, seqpos, oi, ldo); break;
+  }
+  return record_cuda_error(cudaGetLastError(), "conv_silu: launch");
+}
+
+extern "C" int kd_gated_delta_rule(const void* qkv, int64_t ldqkv, const void* ab, int64_t ldab, const void* a_log,
+                                   const void* dt_bias, const int32_t* cu, int num_seqs, int64_t T, int num_k_heads,
+                                   int num_v_heads, int head_k_dim, int head_v_dim, void* out, int64_t ldo,
+                                   cudaStream_t stream) {
+  if (num_seqs < 0 || T < 0) return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: negative sizes");
+  if (num_seqs == 0 || T == 0) return KD_OK;
+  if (num_k_heads <= 0 || num_v_heads <= 0 || num_v_heads % num_k_heads)
+    return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: value heads must be a multiple of key heads");
+  if (!qkv || !ab || !a_log || !dt_bias || !cu || !out) return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: null");
+  const int64_t width = 2LL * num_k_heads * head_k_dim + (int64_t)num_v_heads * head_v_dim;
+  if (ldqkv < width || ldab < 2LL * num_v_heads || ldo < (int64_t)num_v_heads * head_v_dim)
+    return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: row strides smaller than the rows");
+  dn::Args a;
+  a.qkv = static_cast<const __nv_bfloat16*>(qkv);
+  a.ldqkv = ldqkv;
+  a.ab = static_cast<const __nv_bfloat16*>(ab);
+  a.ldab = ldab;
+  a.a_log = static_cast<const __nv_bfloat16*>(a_log);
+  a.dt_bias = static_cast<const __nv_bfloat16*>(dt_bias);
+  a.cu = cu;
+  a.nk = num_k_heads;
+  a.nv = num_v_heads;
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.ldo = ldo;
+  if (head_k_dim == 64 && head_v_dim == 64) return dn::launch_delta<64, 64>(a, num_seqs, stream);
+  if (head_k_dim == 128 && head_v_dim == 128) return dn::launch_delta<128, 128>(a, num_seqs, stream);
+  if (head_k_dim == 128 && head_v_dim == 64) return dn::launch_delta<128, 64>(a, num_seqs, stream);
+  if (head_k_dim == 64 && head_v_dim == 128) return dn::launch_delta<64, 128>(a, num_seqs, stream);
+  return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: head dims must be 64 or 128");
+}
+
+extern "C" int kd_gated_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* weight, int64_t T,
+                             int heads, int head_dim, float eps, void* out, int64_t ldo, cudaStream_t stream) {
+  if (T < 0 || heads <= 0) return set_error(KD_ERR_ARGUMENT, "gated_norm: bad sizes");
+  if (T == 0) return KD_OK;
+  if (!x || !z || !weight || !out) return set_error(KD_ERR_ARGUMENT, "gated_norm: null pointer");
+  const int64_t width = (int64_t)heads * head_dim;
+  if (ldx < width || ldz < width || ldo < width) return set_error(KD_ERR_ARGUMENT, "gated_norm: row strides");
+  const auto* xi = static_cast<const __nv_bfloat16*>(x);
+  const auto* zi = static_cast<const __nv_bfloat16*>(z);
+  const auto* wi = static_cast<const __nv_bfloat16*>(weight);
+  auto* oi = static_cast<__nv_bfloat16*>(out);
+  const int64_t threads = T * heads * 32;
+  const unsigned blocks = (unsigned)((threads + 255) / 256);
+  if (head_dim == 64)
+    dn::gated_norm_kernel<64><<<blocks, 256, 0, stream>>>(xi, ldx, zi, ldz, wi, T, heads, eps, oi, ldo);
+  else if (head_dim == 128)
+    dn::gated_norm_kernel<128><<<blocks, 256, 0, stream>>>(xi, ldx, zi, ldz, wi, T, heads, eps, oi, ldo);
+  else
+    return set_error(KD_ERR_ARGUMENT, "gated_norm: head_dim must be 64 or 128");
+  return record_cuda_error(cudaGetLastError(), "gated_norm: launch");
+}

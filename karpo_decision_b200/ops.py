@@ -302,3 +302,51 @@ def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor | None 
         out = torch.empty((n, *src.shape[1:]), dtype=src.dtype, device=src.device)
     call("kd_gather_rows", src.data_ptr(), width, rows.data_ptr(), n, width, out.data_ptr(), width, _stream(src))
     return out
+
+
+# ------------------------------------------------------------------------------------------------ Gated DeltaNet
+
+
+def conv_silu(x: torch.Tensor, weight: torch.Tensor, seqpos: torch.Tensor, channels: int | None = None,
+              out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(causal depthwise convolution) of the first ``channels`` columns of bf16 rows ``x`` with taps ``weight``
+    (C, K), cut at sequence starts (``seqpos``)."""
+    _require(x.dtype == torch.bfloat16 and x.stride(-1) == 1, "conv_silu: bf16 rows")
+    _require(weight.dtype == torch.bfloat16 and weight.is_contiguous(), "conv_silu: contiguous bf16 taps")
+    _require(seqpos.dtype == torch.int64 and seqpos.is_contiguous(), "seqpos must be contiguous int64")
+    t = x.shape[0]
+    c = channels if channels is not None else weight.shape[0]
+    if out is None:
+        out = torch.empty(t, c, dtype=torch.bfloat16, device=x.device)
+    call("kd_conv_silu", x.data_ptr(), x.stride(0), t, c, weight.data_ptr(), weight.shape[1], seqpos.data_ptr(),
+         out.data_ptr(), out.stride(0), _stream(x))
+    return out
+
+
+def gated_delta_rule(qkv: torch.Tensor, ab: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
+                     cu: torch.Tensor, k_heads: int, v_heads: int, k_dim: int, v_dim: int,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """(T, Hv * dv) bf16: the gated delta rule over the packed sequences ``cu`` (int32 on the device)."""
+    _require(qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1, "gated_delta_rule: bf16 qkv rows")
+    _require(ab.dtype == torch.bfloat16 and ab.stride(-1) == 1, "gated_delta_rule: bf16 [b | a] rows")
+    _require(cu.dtype == torch.int32 and cu.is_contiguous(), "cu: contiguous int32")
+    t = qkv.shape[0]
+    if out is None:
+        out = torch.empty(t, v_heads * v_dim, dtype=torch.bfloat16, device=qkv.device)
+    call("kd_gated_delta_rule", qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr(),
+         dt_bias.data_ptr(), cu.data_ptr(), cu.numel() - 1, t, k_heads, v_heads, k_dim, v_dim, out.data_ptr(),
+         out.stride(0), _stream(qkv))
+    return out
+
+
+def gated_norm(x: torch.Tensor, z: torch.Tensor, weight: torch.Tensor, heads: int, head_dim: int, eps: float,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """Qwen3_5RMSNormGated per (row, head): bf16(bf16(w * bf16(norm(x))) * silu(z))."""
+    _require(x.dtype == torch.bfloat16 and z.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16,
+             "gated_norm: bf16 operands")
+    t = x.shape[0]
+    if out is None:
+        out = torch.empty(t, heads * head_dim, dtype=torch.bfloat16, device=x.device)
+    call("kd_gated_norm", x.data_ptr(), x.stride(0), z.data_ptr(), z.stride(0), weight.data_ptr(), t, heads,
+         head_dim, float(eps), out.data_ptr(), out.stride(0), _stream(x))
+    return out

@@ -78,19 +78,39 @@ class Projection:
 
 
 @dataclass
+class Mixer:
+    """A Gated DeltaNet layer's token mixer (Qwen3_5GatedDeltaNet): its input projections write one buffer of
+    ``width`` columns, [q k v (conv_dim) | z (value_dim) | b (Hv) | a (Hv) | zero padding to a multiple of 32]."""
+
+    proj: list[tuple[Projection, int, int]]  # (projection, first column, width) into the mixer buffer
+    width: int
+    conv: torch.Tensor  # (conv_dim, K) bf16 taps
+    a_log: torch.Tensor
+    dt_bias: torch.Tensor
+    norm: torch.Tensor  # the gated RMSNorm's weight (head_v_dim)
+
+
+@dataclass
 class Layer:
-    kind: str  # "full_attention" or "sliding_attention"
+    kind: str  # "full_attention", "sliding_attention" or "linear_attention"
     input_norm: torch.Tensor
-    qkv: list[tuple[Projection, int, int]]  # (projection, first output column, width) into the qkv buffer
-    q_norm: torch.Tensor
-    k_norm: torch.Tensor
-    o: Projection
+    o: Projection  # attention's o_proj, or the Gated DeltaNet's out_proj
     post_attention_norm: torch.Tensor
     gate_up: Projection
     down: Projection
+    qkv: list[tuple[Projection, int, int]] | None = None  # (projection, first output column, width) into qkv
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+    mixer: Mixer | None = None
     pre_feedforward_norm: torch.Tensor | None = None
     post_feedforward_norm: torch.Tensor | None = None
     scalar: torch.Tensor | None = None
+
+
+def mixer_width(spec: Spec) -> int:
+    """Columns of a Gated DeltaNet layer's projection buffer (padded to a multiple of 32, the GEMM's N granule)."""
+    width = spec.conv_dim + spec.lin_value_dim + 2 * spec.lin_v_heads
+    return width + (-width) % 32
 
 
 class Workspace:
@@ -102,14 +122,15 @@ class Workspace:
                  stored_qkv: bool) -> None:
         t, h = capacity, spec.hidden
         bf = dict(dtype=torch.bfloat16, device=device)
-        kinds = set(spec.layer_types())
-        q_cols = max(spec.heads * spec.attn_dims(kind)[0] for kind in kinds)
-        kv_cols = max(spec.attn_dims(kind)[0] * spec.attn_dims(kind)[1] for kind in kinds)
+        all_kinds = set(spec.layer_types())
+        kinds = all_kinds - {"linear_attention"}  # attention kinds
+        q_cols = max((spec.heads * spec.attn_dims(kind)[0] for kind in kinds), default=0)
+        kv_cols = max((spec.attn_dims(kind)[0] * spec.attn_dims(kind)[1] for kind in kinds), default=0)
         self.capacity = capacity
         self.h = torch.empty(t, h, **bf)
         self.x = torch.empty(t, h, **bf)
         # the stored projection, only for layers that take the unfused QKV path
-        self._qkv = torch.empty(t * max(spec.qkv_width_of(k) for k in kinds), **bf) if stored_qkv else None
+        self._qkv = torch.empty(t * max(spec.qkv_width_of(k) for k in kinds), **bf) if stored_qkv and kinds else None
         # per rotary kind, the pack's rotary factors: (rot / 2, T) contiguous, viewed from a flat buffer per pack
         self._rot_half = {kind: rotary_width(spec, kind) // 2 for kind in kinds}
         self._cs = {kind: torch.empty(half * t, dtype=torch.int32, device=device)
@@ -121,8 +142,14 @@ class Workspace:
         self._o = torch.empty(t * q_cols, **bf)
         self.a = torch.empty(t, h, **bf)
         self.m = torch.empty(t, inter_pad, **bf)
+        vd = spec.lin_value_dim if "linear_attention" in all_kinds else 0
+        if vd:  # Gated DeltaNet layers: projection buffer, convolution output, delta-rule output, gated norm
+            self.lin = torch.empty(t, mixer_width(spec), **bf)
+            self.conv = torch.empty(t, spec.conv_dim, **bf)
+            self.core = torch.empty(t, vd, **bf)
+            self.gn = torch.empty(t, vd, **bf)
         if fp8:
-            width = max(h, q_cols, inter_pad)
+            width = max(h, q_cols, inter_pad, vd)
             self.xq = torch.empty(t * width, dtype=torch.float8_e4m3fn, device=device)
             self.xs = torch.empty(t, dtype=torch.float32, device=device)
 
@@ -171,7 +198,7 @@ class Packed(torch.nn.Module):
         attention = spec.attention if attention is None else attention
         if attention not in ("causal", "bidirectional"):
             raise ValueError(f"attention must be 'causal' or 'bidirectional', not {attention!r}")
-        for kind in set(spec.layer_types()):
+        for kind in set(spec.layer_types()) - {"linear_attention"}:
             hd = spec.attn_dims(kind)[0]
             if hd not in (64, 128, 256, 512):
                 raise ValueError(f"head size {hd} ({kind}) is not one of the kernels' 64, 128, 256, 512")
@@ -198,6 +225,9 @@ class Packed(torch.nn.Module):
         norm_w = (lambda key: _tensor(weights[key], dev))
         for i in range(s.layers):
             p = f"layers.{i}."
+            if self.types[i] == "linear_attention":
+                self.layers.append(self._linear_layer(weights, p, fp8))
+                continue
             wq, wk = (_tensor(weights[p + n], dev) for n in ("q_proj", "k_proj"))
             # attention_k_eq_v: the values are the key projection itself (families/gemma/packed.py:188); the kernels'
             # layout repeats the key rows in the value columns (the same products, so bit-equal raw values)
@@ -209,15 +239,12 @@ class Packed(torch.nn.Module):
                 qkv.append((Projection.of(torch.cat([wk, wv]), False), wq.shape[0], wk.shape[0] + wv.shape[0]))
             else:
                 qkv.append((Projection.of(torch.cat([wq, wk, wv]), fp8), 0, s.qkv_width_of(self.types[i])))
-            gate_up = interleave_gate_up(_tensor(weights[p + "gate_proj"], dev), _tensor(weights[p + "up_proj"], dev))
-            down = _tensor(weights[p + "down_proj"], dev)
-            if self.inter_pad != s.intermediate:
-                down = torch.cat([down, down.new_zeros(down.shape[0], self.inter_pad - s.intermediate)], 1)
+            gate_up, down = self._mlp_weights(weights, p)
             layer = Layer(kind=self.types[i], input_norm=norm_w(p + "input_layernorm"), qkv=qkv,
                           q_norm=norm_w(p + "q_norm"), k_norm=norm_w(p + "k_norm"),
                           o=Projection.of(_tensor(weights[p + "o_proj"], dev), fp8),
                           post_attention_norm=norm_w(p + "post_attention_layernorm"),
-                          gate_up=Projection.of(gate_up.contiguous(), fp8), down=Projection.of(down.contiguous(), fp8))
+                          gate_up=Projection.of(gate_up, fp8), down=Projection.of(down, fp8))
             if s.family == "gemma":
                 layer.pre_feedforward_norm = norm_w(p + "pre_feedforward_layernorm")
                 layer.post_feedforward_norm = norm_w(p + "post_feedforward_layernorm")
@@ -225,22 +252,60 @@ class Packed(torch.nn.Module):
                                        if not isinstance(weights[p + "layer_scalar"], torch.Tensor)
                                        else weights[p + "layer_scalar"].reshape(1), dev)
             self.layers.append(layer)
-        self._inv_freq = {kind: self._inv_freq_of(kind) for kind in set(self.types)}
+        attention_kinds = set(self.types) - {"linear_attention"}
+        self._inv_freq = {kind: self._inv_freq_of(kind) for kind in attention_kinds}
         #: Per layer kind, whether the QKV projection's epilogue does the norms and RoPE (kd_qkv_projection): width a
         #: multiple of 256, rotary width a multiple of 32, a head within one 256-wide tile; otherwise GEMM +
         #: kd_qkv_norm_rope.
-        self.fused_kinds = {kind for kind in set(self.types)
+        self.fused_kinds = {kind for kind in attention_kinds
                             if s.qkv_width_of(kind) % 256 == 0 and rotary_width(s, kind) % 32 == 0
                             and s.attn_dims(kind)[0] <= 256}
         self._tables: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
         self._workspace: Workspace | None = None
 
+    def _linear_layer(self, weights: dict[str, Any], p: str, fp8: bool) -> Layer:
+        """A Gated DeltaNet layer: its input projections into one buffer (Qwen's FP8 path keeps the per-head b and a
+        projections, fewer than 256 outputs, in bf16: serve/qwen_fp8.py:17), the convolution taps, decay parameters,
+        gated-norm weight and output projection, then the MLP as in every layer."""
+        s, dev = self.spec, self.device
+        la = p + "linear_attn."
+        w = {n: _tensor(weights[la + n], dev) for n in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a")}
+        width = mixer_width(s)
+        wide = torch.cat([w["in_proj_qkv"], w["in_proj_z"]])
+        narrow = torch.cat([w["in_proj_b"], w["in_proj_a"]])
+        pad = width - wide.shape[0] - narrow.shape[0]
+        if pad:
+            narrow = torch.cat([narrow, narrow.new_zeros(pad, narrow.shape[1])])
+        if fp8:
+            proj = [(Projection.of(wide, wide.shape[0] >= QWEN_FP8_MIN_FEATURES), 0, wide.shape[0]),
+                    (Projection.of(narrow, False), wide.shape[0], narrow.shape[0])]
+        else:
+            proj = [(Projection.of(torch.cat([wide, narrow]), False), 0, width)]
+        out = _tensor(weights[la + "out_proj"], dev)
+        mixer = Mixer(proj=proj, width=width, conv=_tensor(weights[la + "conv1d"], dev).reshape(s.conv_dim, -1),
+                      a_log=_tensor(weights[la + "A_log"], dev), dt_bias=_tensor(weights[la + "dt_bias"], dev),
+                      norm=_tensor(weights[la + "norm"], dev))
+        gate_up, down = self._mlp_weights(weights, p)
+        return Layer(kind="linear_attention", input_norm=_tensor(weights[p + "input_layernorm"], dev),
+                     o=Projection.of(out, fp8 and out.shape[0] >= QWEN_FP8_MIN_FEATURES),
+                     post_attention_norm=_tensor(weights[p + "post_attention_layernorm"], dev),
+                     gate_up=Projection.of(gate_up, fp8), down=Projection.of(down, fp8), mixer=mixer)
+
+    def _mlp_weights(self, weights: dict[str, Any], p: str) -> tuple[torch.Tensor, torch.Tensor]:
+        """The MLP's interleaved gate/up weight and its down weight (padded to the interleave's width)."""
+        dev, s = self.device, self.spec
+        gate_up = interleave_gate_up(_tensor(weights[p + "gate_proj"], dev), _tensor(weights[p + "up_proj"], dev))
+        down = _tensor(weights[p + "down_proj"], dev)
+        if self.inter_pad != s.intermediate:
+            down = torch.cat([down, down.new_zeros(down.shape[0], self.inter_pad - s.intermediate)], 1)
+        return gate_up.contiguous(), down.contiguous()
+
     # ---------------------------------------------------------------- construction from a Transformers backbone
 
     @classmethod
     def from_backbone(cls, backbone: Any, attention: str = "causal", fp8: bool = False) -> Packed:
-        """From a Transformers ``Qwen3_5Model`` (full-attention layers) or a Gemma 4 text model, as the reference's
-        ``family.Packed(backbone, attention)``; the weights are copied into the kernels' layouts."""
+        """From a Transformers ``Qwen3_5Model`` (full-attention and Gated DeltaNet layers) or a Gemma 4 text model, as
+        the reference's ``family.Packed(backbone, attention)``; the weights are copied into the kernels' layouts."""
         lm = getattr(backbone, "language_model", backbone)
         config = lm.config
         model_type = getattr(config, "model_type", "")
@@ -250,9 +315,22 @@ class Packed(torch.nn.Module):
         for i, layer in enumerate(lm.layers):
             p = f"layers.{i}."
             kind = getattr(layer, "layer_type", getattr(layer, "block_type", "full_attention"))
-            if family == "qwen" and kind != "full_attention":
-                raise NotImplementedError("Gated DeltaNet (linear-attention) layers are not built on the B200 path")
             kinds.append(kind)
+            for name in ("gate_proj", "up_proj", "down_proj"):
+                weights[p + name] = getattr(layer.mlp, name).weight
+            weights[p + "input_layernorm"] = layer.input_layernorm.weight
+            weights[p + "post_attention_layernorm"] = layer.post_attention_layernorm.weight
+            if kind == "linear_attention":
+                la = layer.linear_attn
+                if la.conv1d.bias is not None:  # families/qwen/packed.py:77-78
+                    raise ValueError("unexpected convolution bias")
+                for name in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+                    weights[p + "linear_attn." + name] = getattr(la, name).weight
+                weights[p + "linear_attn.conv1d"] = la.conv1d.weight.squeeze(1)
+                weights[p + "linear_attn.A_log"] = la.A_log
+                weights[p + "linear_attn.dt_bias"] = la.dt_bias
+                weights[p + "linear_attn.norm"] = la.norm.weight
+                continue
             a = layer.self_attn
             for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
                 if getattr(a, name, None) is None:
@@ -262,10 +340,6 @@ class Packed(torch.nn.Module):
                 weights[p + name] = getattr(a, name).weight
             weights[p + "q_norm"] = a.q_norm.weight
             weights[p + "k_norm"] = a.k_norm.weight
-            for name in ("gate_proj", "up_proj", "down_proj"):
-                weights[p + name] = getattr(layer.mlp, name).weight
-            weights[p + "input_layernorm"] = layer.input_layernorm.weight
-            weights[p + "post_attention_layernorm"] = layer.post_attention_layernorm.weight
             if family == "gemma":
                 weights[p + "pre_feedforward_layernorm"] = layer.pre_feedforward_layernorm.weight
                 weights[p + "post_feedforward_layernorm"] = layer.post_feedforward_layernorm.weight
@@ -274,9 +348,19 @@ class Packed(torch.nn.Module):
         head_dim = getattr(config, "head_dim", None) or config.hidden_size // heads
         if family == "qwen":
             rope = config.rope_parameters
+            every = 0
+            if "linear_attention" in kinds:  # the hybrid pattern: every n-th layer full attention
+                every = kinds.index("full_attention") + 1 if "full_attention" in kinds else 0
             spec = Spec("qwen", len(lm.layers), config.hidden_size, heads, kv_heads, head_dim,
                         config.intermediate_size, config.vocab_size, eps=config.rms_norm_eps,
-                        rope_theta=rope["rope_theta"], partial_rotary=rope.get("partial_rotary_factor", 1.0))
+                        rope_theta=rope["rope_theta"], partial_rotary=rope.get("partial_rotary_factor", 1.0),
+                        full_every=every, lin_k_heads=getattr(config, "linear_num_key_heads", 16),
+                        lin_v_heads=getattr(config, "linear_num_value_heads", 32),
+                        lin_k_dim=getattr(config, "linear_key_head_dim", 128),
+                        lin_v_dim=getattr(config, "linear_value_head_dim", 128),
+                        conv_kernel=getattr(config, "linear_conv_kernel_dim", 4))
+            if kinds != spec.layer_types():
+                raise NotImplementedError(f"layer pattern {kinds} is not a full-attention layer every n-th")
         else:
             rope = config.rope_parameters
             every = 6
@@ -330,7 +414,7 @@ class Packed(torch.nn.Module):
     def workspace(self, tokens: int) -> Workspace:
         if self._workspace is None or self._workspace.capacity < tokens:
             self._workspace = None
-            stored = any(not self._fused(layer) for layer in self.layers)
+            stored = any(layer.qkv is not None and not self._fused(layer) for layer in self.layers)
             self._workspace = Workspace(self.spec, tokens, self.device, self.fp8, self.inter_pad, stored)
         return self._workspace
 
@@ -406,6 +490,9 @@ class Packed(torch.nn.Module):
         h = ops.embed(p.input_ids, self.embed_tokens, 0.0 if qwen else math.sqrt(s.hidden), out=ws.h[:t])
         rope_cs: dict[str, torch.Tensor] = {}  # per rotary kind, gathered once per pack
         for layer in self.layers[:-1] if self.prune_last else self.layers:
+            if layer.kind == "linear_attention":
+                self._after_attention(layer, h, self._linear_mixer(layer, h, p, ws), ws)
+                continue
             q, k, v, gate = self._attention_inputs(layer, h, p, ws, rope_cs)
             window = (self.window - 1, 0) if layer.kind == "sliding_attention" else self.full_window
             o_buf = ws.o(s, layer.kind, t)
@@ -427,6 +514,26 @@ class Packed(torch.nn.Module):
 
     def _fused(self, layer: Layer) -> bool:
         return layer.kind in self.fused_kinds and len(layer.qkv) == 1
+
+    def _linear_mixer(self, layer: Layer, h: torch.Tensor, p: Any, ws: Workspace) -> torch.Tensor:
+        """A Gated DeltaNet layer's token mixer before its output projection (families/qwen/packed.py:74-106): the
+        input norm and projections, causal convolution + silu, the gated delta rule over the pack's sequences and the
+        gated RMSNorm; returns the (T, value_dim) rows the output projection reads."""
+        s = self.spec
+        t = h.shape[0]
+        mix = layer.mixer
+        x, x8 = self._normed(ws, h, layer.input_norm, ops.NORM_ONE_PLUS, any(not pr.fp8 for pr, _, _ in mix.proj),
+                             any(pr.fp8 for pr, _, _ in mix.proj))
+        buf = ws.lin[:t]
+        for proj, col, width in mix.proj:
+            self._project(proj, x, x8, buf if width == mix.width else buf[:, col:col + width])
+        seqpos = p.seqpos if p.seqpos.dtype == torch.int64 else p.seqpos.long()
+        conv = ops.conv_silu(buf, mix.conv, seqpos, channels=s.conv_dim, out=ws.conv[:t])
+        vd = s.lin_value_dim
+        core = ops.gated_delta_rule(conv, buf[:, s.conv_dim + vd:], mix.a_log, mix.dt_bias, p.cu, s.lin_k_heads,
+                                    s.lin_v_heads, s.lin_k_dim, s.lin_v_dim, out=ws.core[:t])
+        return ops.gated_norm(core, buf[:, s.conv_dim:s.conv_dim + vd], mix.norm, s.lin_v_heads, s.lin_v_dim, s.eps,
+                              out=ws.gn[:t])
 
     def _attention_inputs(self, layer: Layer, h: torch.Tensor, p: Any, ws: Workspace,
                           rope_cs: dict[str, torch.Tensor]) -> tuple:

@@ -48,6 +48,14 @@ class Spec:
     k_eq_v: bool = False
     global_rope: str = "default"  # or "proportional"
     global_partial_rotary: float = 0.25
+    # Qwen3.5 hybrid stacks: every full_every-th layer is full attention and the others Gated DeltaNet layers
+    # (Transformers' full_attention_interval; 0: every layer full attention), with their own head shapes.
+    full_every: int = 0
+    lin_k_heads: int = 16
+    lin_v_heads: int = 32
+    lin_k_dim: int = 128
+    lin_v_dim: int = 128
+    conv_kernel: int = 4
 
     def as_dict(self) -> dict:
         return asdict(self)
@@ -81,8 +89,24 @@ class Spec:
     def qkv_width(self) -> int:
         return self.q_width + 2 * self.kv_heads * self.head_dim
 
+    @property
+    def lin_key_dim(self) -> int:
+        return self.lin_k_heads * self.lin_k_dim
+
+    @property
+    def lin_value_dim(self) -> int:
+        return self.lin_v_heads * self.lin_v_dim
+
+    @property
+    def conv_dim(self) -> int:
+        """Channels of a Gated DeltaNet layer's causal convolution: [q | k | v]."""
+        return 2 * self.lin_key_dim + self.lin_value_dim
+
     def layer_types(self) -> list[str]:
         if self.family == "qwen":
+            if self.full_every:
+                return ["linear_attention" if (i + 1) % self.full_every else "full_attention"
+                        for i in range(self.layers)]
             return ["full_attention"] * self.layers
         # Every global_every-th layer is global, and so is the last (Gemma4TextConfig forces a global last layer).
         return ["full_attention" if (i + 1) % self.global_every == 0 or i == self.layers - 1 else "sliding_attention"
@@ -92,6 +116,10 @@ class Spec:
         """2 * sum(K * N) over one token's projections, all layers (a shared-key layer has no value projection)."""
         h, total = self.hidden, 0
         for kind in self.layer_types():
+            if kind == "linear_attention":
+                total += h * (self.conv_dim + self.lin_value_dim + 2 * self.lin_v_heads) + self.lin_value_dim * h
+                total += 3 * h * self.intermediate
+                continue
             hd, hkv = self.attn_dims(kind)
             kv = (1 if self.shares_kv(kind) else 2) * hkv * hd
             total += h * (self.q_width_of(kind) + kv) + self.heads * hd * h + 3 * h * self.intermediate
@@ -136,6 +164,26 @@ def numpy_weights(spec: Spec, seed: int = 0, std: float = 0.02) -> dict[str, np.
     w: dict[str, np.ndarray] = {"embed_tokens": normal(spec.vocab, h)}
     for i, kind in enumerate(spec.layer_types()):
         p = f"layers.{i}."
+        if kind == "linear_attention":
+            w[p + "input_layernorm"] = norm_weight(h)
+            la = p + "linear_attn."
+            w[la + "in_proj_qkv"] = normal(spec.conv_dim, h)
+            w[la + "in_proj_z"] = normal(spec.lin_value_dim, h)
+            w[la + "in_proj_b"] = normal(spec.lin_v_heads, h)
+            w[la + "in_proj_a"] = normal(spec.lin_v_heads, h)
+            w[la + "conv1d"] = normal(spec.conv_dim, spec.conv_kernel, scale=0.3)
+            # A = exp(A_log) uniform in [1, 16]; dt_bias the inverse softplus of dt log-uniform in [1e-3, 1e-1] (the
+            # usual Mamba-style initialization, so the state keeps a memory over many tokens)
+            w[la + "A_log"] = _bf16_exact(np.log(rng.uniform(1.0, 16.0, spec.lin_v_heads)).astype(np.float32))
+            dt = np.exp(rng.uniform(np.log(1e-3), np.log(1e-1), spec.lin_v_heads))
+            w[la + "dt_bias"] = _bf16_exact((dt + np.log(-np.expm1(-dt))).astype(np.float32))
+            w[la + "norm"] = _bf16_exact((1.0 + 0.1 * rng.standard_normal(spec.lin_v_dim)).astype(np.float32))
+            w[la + "out_proj"] = normal(h, spec.lin_value_dim)
+            w[p + "post_attention_layernorm"] = norm_weight(h)
+            w[p + "gate_proj"] = normal(inter, h)
+            w[p + "up_proj"] = normal(inter, h)
+            w[p + "down_proj"] = normal(h, inter)
+            continue
         hd, hkv = spec.attn_dims(kind)
         qk_base = hd ** -0.25 if spec.family == "gemma" else 1.0
         w[p + "input_layernorm"] = norm_weight(h)
@@ -175,6 +223,27 @@ def device_weights(spec: Spec, seed: int, device: torch.device, std: float = 0.0
     w: dict[str, torch.Tensor] = {"embed_tokens": normal(spec.vocab, h)}
     for i, kind in enumerate(spec.layer_types()):
         p = f"layers.{i}."
+        if kind == "linear_attention":
+            nv = spec.lin_v_heads
+            w[p + "input_layernorm"] = norm_weight(h)
+            la = p + "linear_attn."
+            w[la + "in_proj_qkv"] = normal(spec.conv_dim, h)
+            w[la + "in_proj_z"] = normal(spec.lin_value_dim, h)
+            w[la + "in_proj_b"] = normal(nv, h)
+            w[la + "in_proj_a"] = normal(nv, h)
+            w[la + "conv1d"] = normal(spec.conv_dim, spec.conv_kernel, scale=0.3)
+            uniform = torch.rand(nv, generator=gen, device=device)
+            w[la + "A_log"] = torch.log(1.0 + 15.0 * uniform).bfloat16()
+            dt = torch.exp(math.log(1e-3) + (math.log(1e-1) - math.log(1e-3)) *
+                           torch.rand(nv, generator=gen, device=device))
+            w[la + "dt_bias"] = (dt + torch.log(-torch.expm1(-dt))).bfloat16()
+            w[la + "norm"] = (1.0 + 0.1 * torch.randn(spec.lin_v_dim, generator=gen, device=device)).bfloat16()
+            w[la + "out_proj"] = normal(h, spec.lin_value_dim)
+            w[p + "post_attention_layernorm"] = norm_weight(h)
+            w[p + "gate_proj"] = normal(inter, h)
+            w[p + "up_proj"] = normal(inter, h)
+            w[p + "down_proj"] = normal(h, inter)
+            continue
         hd, hkv = spec.attn_dims(kind)
         qk_base = hd ** -0.25 if spec.family == "gemma" else 1.0
         w[p + "input_layernorm"] = norm_weight(h)

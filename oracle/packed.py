@@ -196,11 +196,90 @@ def quantize_weights(weights: dict, min_features: int = 0) -> dict:
     does at load (serve/fp8.py:86-90, serve/qwen_fp8.py:27-33)."""
     out = dict(weights)
     for key, w in weights.items():
-        if key.endswith(("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")) and \
+        if key.endswith(("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj", "in_proj_qkv",
+                         "in_proj_z", "in_proj_b", "in_proj_a", "out_proj")) and \
                 w.shape[0] >= min_features:
             q, s = e4m3_rows(w)
             out[key] = (q, s.reshape(1, -1))
     return out
+
+
+# ------------------------------------------------------------------------------------------------ Gated DeltaNet
+
+
+def causal_conv_silu(x: np.ndarray, weight: np.ndarray, seqpos: np.ndarray) -> np.ndarray:
+    """Depthwise causal convolution over rows (T, C) with taps (C, K), cut at every sequence start (a tap reaches
+    back ``shift`` rows only where seqpos >= shift: families/qwen/packed.py:45-53), float32 sums, then silu: the
+    convolution and activation of the Gated DeltaNet (families/qwen/packed.py:81-86, flash-linear-attention's
+    causal_conv1d with cu_seqlens)."""
+    taps = weight.shape[1]
+    xf = x.astype(np.float32)
+    out = xf * weight[:, taps - 1].astype(np.float32)[None, :]
+    for shift in range(1, taps):
+        shifted = np.zeros_like(xf)
+        shifted[shift:] = xf[:-shift]
+        out = out + shifted * (seqpos >= shift).astype(np.float32)[:, None] * \
+            weight[:, taps - 1 - shift].astype(np.float32)[None, :]
+    return silu(out)
+
+
+def gated_delta_rule(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray, beta: np.ndarray,
+                     cu: np.ndarray) -> np.ndarray:
+    """The gated delta rule per sequence and head, in its recurrent form (Transformers'
+    torch_recurrent_gated_delta_rule, the contract of flash-linear-attention's chunk_gated_delta_rule that
+    families/qwen/packed.py:96-98 calls with use_qk_l2norm_in_kernel): q, k L2-normalized (eps 1e-6), q scaled by
+    dk^-0.5, state S (dk, dv) from zero at each sequence start; per token S = S exp(g) ; d = (v - S^T k) beta ;
+    S = S + k d^T ; o = S^T q. q, k (T, H, dk), v (T, H, dv), g, beta (T, H) -> (T, H, dv) float32."""
+    def l2(x):
+        x = x.astype(np.float32)
+        return x / np.sqrt((x * x).sum(-1, keepdims=True) + np.float32(1e-6))
+
+    q, k = l2(q) * np.float32(q.shape[-1] ** -0.5), l2(k)
+    v, g, beta = v.astype(np.float32), g.astype(np.float32), beta.astype(np.float32)
+    heads, dk, dv = q.shape[1], q.shape[2], v.shape[2]
+    out = np.zeros((q.shape[0], heads, dv), dtype=np.float32)
+    for a, b in zip(cu[:-1].tolist(), cu[1:].tolist(), strict=True):
+        state = np.zeros((heads, dk, dv), dtype=np.float32)
+        for t in range(a, b):
+            state = state * np.exp(g[t])[:, None, None]
+            kv = np.einsum("hkv,hk->hv", state, k[t])
+            delta = (v[t] - kv) * beta[t][:, None]
+            state = state + k[t][:, :, None] * delta[:, None, :]
+            out[t] = np.einsum("hkv,hk->hv", state, q[t])
+    return out
+
+
+def softplus(x: np.ndarray) -> np.ndarray:
+    return np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0)))).astype(np.float32)
+
+
+def linear_attention(weights: dict, spec: dict, p: str, x: np.ndarray, pack: dict, mode: str,
+                     fp8: bool = False) -> np.ndarray:
+    """Qwen3.5's Gated DeltaNet token mixer over the pack (families/qwen/packed.py:74-106): projections, causal
+    convolution + silu, decay g = -exp(A_log) softplus(a + dt_bias) and write strength beta = sigmoid(b)
+    (fused.py:45-47), query/key heads repeated to the value heads, the gated delta rule, the gated RMSNorm
+    weight * bf16(norm(core)) * silu(z) (fused.py:29-32, Qwen3_5RMSNormGated) and the output projection."""
+    la = p + "linear_attn."
+    t = x.shape[0]
+    nk, nv, dk, dv = spec["lin_k_heads"], spec["lin_v_heads"], spec["lin_k_dim"], spec["lin_v_dim"]
+    kd = nk * dk
+    mixed = linear(x, weights[la + "in_proj_qkv"], mode, fp8)
+    z = linear(x, weights[la + "in_proj_z"], mode, fp8).reshape(t, nv, dv)
+    b = linear(x, weights[la + "in_proj_b"], mode, fp8)
+    a = linear(x, weights[la + "in_proj_a"], mode, fp8)
+    mixed = _round(causal_conv_silu(mixed, weights[la + "conv1d"], pack["seqpos"]), mode)
+    q = mixed[:, :kd].reshape(t, nk, dk)
+    k = mixed[:, kd:2 * kd].reshape(t, nk, dk)
+    v = mixed[:, 2 * kd:].reshape(t, nv, dv)
+    g = -np.exp(weights[la + "A_log"].astype(np.float32)) * softplus(a + weights[la + "dt_bias"].astype(np.float32))
+    beta = _round(np.float32(1.0) / (np.float32(1.0) + np.exp(-b)), mode)
+    if nv > nk:
+        q, k = np.repeat(q, nv // nk, axis=1), np.repeat(k, nv // nk, axis=1)
+    core = _round(gated_delta_rule(q, k, v, g, beta, pack["cu"]), mode)
+    normed = _round(core / np.sqrt((core * core).mean(-1, keepdims=True) + np.float32(spec["eps"])), mode)
+    normed = _round(weights[la + "norm"].astype(np.float32) * normed, mode)
+    out = _round(normed * silu(z), mode).reshape(t, nv * dv)
+    return linear(out, weights[la + "out_proj"], mode, fp8)
 
 
 # ------------------------------------------------------------------------------------------------ Qwen-shaped
@@ -222,9 +301,19 @@ def qwen_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8:
     h = _round(weights["embed_tokens"][ids], mode)  # :158-159
     cos, sin = rope_tables(seqpos, hd, spec["rope_theta"], spec.get("partial_rotary", 1.0), mode)  # :186
     window = (-1, 0) if spec.get("attention", "causal") == "causal" else (-1, -1)
+    every = spec.get("full_every", 0)
     for i in range(spec["layers"]):
         p = f"layers.{i}."
         x = _round(rms_norm(h, weights[p + "input_layernorm"], eps, True), mode)  # :150
+        if every and (i + 1) % every:  # a Gated DeltaNet layer (:152-153)
+            a = linear_attention(weights, spec, p, x, pack, mode, fp8)
+            h = _round(h + a, mode)
+            y = _round(rms_norm(h, weights[p + "post_attention_layernorm"], eps, True), mode)
+            g = linear(y, weights[p + "gate_proj"], mode, fp8)
+            u = linear(y, weights[p + "up_proj"], mode, fp8)
+            m = _round(silu(g) * u, mode)
+            h = _round(h + linear(m, weights[p + "down_proj"], mode, fp8), mode)
+            continue
         qg = linear(x, weights[p + "q_proj"], mode, fp8).reshape(t, hq, 2 * hd)  # :113
         q, gate = qg[..., :hd], qg[..., hd:].reshape(t, hq * hd)
         q = _round(rms_norm(q, weights[p + "q_norm"], eps, True), mode)  # :114

@@ -17,7 +17,9 @@ reference's own tests use:
 - ``torch._scaled_mm`` (rowwise scales are not implemented on CPU): ``(a.float() @ b.float()) * scale_a * scale_b``
   rounded to the output dtype, the documented semantics of rowwise scaling;
 - Transformers 5.5 names a layer's kind ``layer_type``; the reference reads ``block_type``: aliased per layer;
-- ``transformers.models.gemma4_unified`` (newer Transformers) is absent: stubbed, it is only imported for a type.
+- ``transformers.models.gemma4_unified`` (newer Transformers) is absent: stubbed, it is only imported for a type;
+- flash-linear-attention's GPU kernels for the Gated DeltaNet: ``delta_rule_contract`` (Transformers' recurrent
+  torch implementation per packed sequence) and ``conv_contract`` (the causal convolution cut at sequence starts).
 """
 
 from __future__ import annotations
@@ -61,6 +63,37 @@ def varlen_contract(q, k, v, cu_q, cu_k, max_q, max_k, scale=None, window_size=(
     return torch.cat(outs)
 
 
+def delta_rule_contract(q, k, v, g, beta, initial_state=None, output_final_state=False,
+                        use_qk_l2norm_in_kernel=False, cu_seqlens=None, cu_seqlens_cpu=None, **_):
+    """flash-linear-attention's chunk_gated_delta_rule over packed sequences (its cu_seqlens contract: the state
+    restarts from zero at every boundary), by Transformers' own recurrent torch implementation per sequence."""
+    from transformers.models.qwen3_5.modeling_qwen3_5 import torch_recurrent_gated_delta_rule
+
+    bounds = cu_seqlens_cpu.tolist() if cu_seqlens_cpu is not None else [0, q.shape[1]]
+    outs = []
+    for a, b in zip(bounds[:-1], bounds[1:], strict=True):
+        o, _ = torch_recurrent_gated_delta_rule(q[:, a:b], k[:, a:b], v[:, a:b], g[:, a:b], beta[:, a:b], None, False,
+                                                use_qk_l2norm_in_kernel)
+        outs.append(o)
+    return torch.cat(outs, 1), None
+
+
+def conv_contract(x, weight, activation=None, cu_seqlens=None, cu_seqlens_cpu=None, **_):
+    """flash-linear-attention's causal_conv1d over packed sequences: x (1, T, C), depthwise taps (C, K), no tap
+    reaching before its sequence's start, float32 sums, the activation in float32, cast back to x's dtype."""
+    bounds = cu_seqlens_cpu.tolist() if cu_seqlens_cpu is not None else [0, x.shape[1]]
+    taps = weight.shape[1]
+    xf, wf = x[0].float(), weight.float()
+    out = torch.zeros_like(xf)
+    for a, b in zip(bounds[:-1], bounds[1:], strict=True):
+        for shift in range(taps):
+            if b - a > shift:
+                out[a + shift:b] += xf[a:b - shift] * wf[:, taps - 1 - shift]
+    if activation in ("silu", "swish"):
+        out = F.silu(out)
+    return out.to(x.dtype)[None], None
+
+
 def scaled_mm_contract(a, b, scale_a, scale_b, out_dtype=torch.bfloat16, **_):
     return ((a.float() @ b.float()) * scale_a * scale_b).to(out_dtype)
 
@@ -96,10 +129,12 @@ def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
     section = [half - 2 * (half // 3), half // 3, half // 3]
     text = dict(vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
                 num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
-                head_dim=spec.head_dim, rms_norm_eps=spec.eps, layer_types=["full_attention"] * spec.layers,
+                head_dim=spec.head_dim, rms_norm_eps=spec.eps, layer_types=spec.layer_types(),
                 rope_parameters={"rope_type": "default", "rope_theta": spec.rope_theta,
                                  "partial_rotary_factor": spec.partial_rotary, "mrope_section": section},
-                attention_bias=False, hidden_act="silu")
+                attention_bias=False, hidden_act="silu", linear_num_key_heads=spec.lin_k_heads,
+                linear_num_value_heads=spec.lin_v_heads, linear_key_head_dim=spec.lin_k_dim,
+                linear_value_head_dim=spec.lin_v_dim, linear_conv_kernel_dim=spec.conv_kernel)
     config = Qwen3_5Config(text_config=text, vision_config={"depth": 1, "hidden_size": 32, "intermediate_size": 64,
                                                            "num_heads": 2, "out_hidden_size": spec.hidden})
     config._attn_implementation = "sdpa"
@@ -111,12 +146,20 @@ def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
         for i, layer in enumerate(lm.layers):
             p = f"layers.{i}."
             layer.block_type = layer.layer_type  # harness alias (Transformers 5.5 naming)
-            a = layer.self_attn
-            for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
-                if getattr(a, name) is not None:  # attention_k_eq_v global layers have no v_proj
+            if layer.layer_type == "linear_attention":
+                la = layer.linear_attn
+                for name in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
+                    getattr(la, name).weight.copy_(to_torch(weights, p + "linear_attn." + name))
+                la.conv1d.weight.copy_(to_torch(weights, p + "linear_attn.conv1d")[:, None, :])
+                la.A_log.copy_(to_torch(weights, p + "linear_attn.A_log"))
+                la.dt_bias.copy_(to_torch(weights, p + "linear_attn.dt_bias"))
+                la.norm.weight.copy_(to_torch(weights, p + "linear_attn.norm"))
+            else:
+                a = layer.self_attn
+                for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
                     getattr(a, name).weight.copy_(to_torch(weights, p + name))
-            a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
-            a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
+                a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
+                a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
             for name in ("gate_proj", "up_proj", "down_proj"):
                 getattr(layer.mlp, name).weight.copy_(to_torch(weights, p + name))
             layer.input_layernorm.weight.copy_(to_torch(weights, p + "input_layernorm"))
@@ -223,6 +266,11 @@ CASES = {
     "gemma_global512": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
                                       global_head_dim=512, global_kv_heads=1, k_eq_v=True, global_rope="proportional"),
                             lengths=("uniform", 5, 8, 160), markers=(1, 1), fp8=False),
+    # Qwen3.5's hybrid stack: Gated DeltaNet layers with a full-attention layer every 2nd (the real 3:1 is
+    # full_attention_interval 4), value heads twice the key heads.
+    "qwen_hybrid": dict(spec=small(CONFIGS["tiny"], layers=4, full_every=2, partial_rotary=0.5, lin_k_heads=2,
+                                   lin_v_heads=4, lin_k_dim=64, lin_v_dim=64),
+                        lengths=("uniform", 6, 8, 200), markers=(1, 3), fp8=False),
     "gemma_blocks_bidir": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
                                          attention="bidirectional"),
                                blocks=[(23, []), (21, [5, 7, 3]), (14, [4, 9]), (3, [20, 25])], fp8=False),
@@ -286,7 +334,8 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
             from karpo_decision.families.qwen import packed as qp
 
             model = qwen_backbone(spec, weights)
-            stack.enter_context(_patched(qp, "_kernels", lambda: (None, varlen_contract, None)))
+            stack.enter_context(_patched(qp, "_kernels", lambda: (delta_rule_contract, varlen_contract,
+                                                                   conv_contract)))
             packed = qp.Packed(model, spec.attention)
             if case["fp8"]:
                 from karpo_decision.serve import qwen_fp8

@@ -12,7 +12,7 @@ from karpo_decision_b200.synthetic import Spec, numpy_weights
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
 CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_tiny_fp8", "gemma_tiny_fp8", "qwen_bidir",
-         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512"]
+         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid"]
 
 
 def load(name: str) -> tuple[Spec, dict, dict, dict]:

@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda")
 
 
-@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "qwen_bidir", "gemma_bidir"])
+@pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "qwen_bidir", "gemma_bidir", "qwen_hybrid"])
 def test_replay_equals_eager_for_any_covered_pack(name):
     spec, weights, _, _ = load(name)
     model = Packed(spec, weights, DEV)

@@ -341,3 +341,59 @@ def test_gather_rows():
     src = bf16(g.standard_normal((300, 8, 64)))
     rows = torch.from_numpy(g.integers(0, 300, 517)).to(DEV)
     assert torch.equal(ops.gather_rows(src, rows), src[rows])
+
+
+# ------------------------------------------------------------------------------------------------ Gated DeltaNet
+
+
+def test_conv_silu_matches_oracle_and_restarts_at_sequence_starts():
+    g = rng(21)
+    lengths = [1, 2, 37, 300, 5]
+    t, c = sum(lengths), 384
+    x = bf16(g.standard_normal((t, c + 64)))  # a wider buffer: the convolution reads its first c columns
+    w = bf16(g.standard_normal((c, 4)) * 0.3)
+    seqpos = np.concatenate([np.arange(n) for n in lengths])
+    got = ops.conv_silu(x, w, torch.from_numpy(seqpos).to(DEV), channels=c)
+    want = oracle.packed.causal_conv_silu(x[:, :c].float().cpu().numpy(), w.float().cpu().numpy(), seqpos)
+    assert np.abs(got.float().cpu().numpy() - oracle.bf16(want)).max() <= 2 ** -7 * max(np.abs(want).max(), 1.0)
+
+
+@pytest.mark.parametrize("nk,nv,dk,dv", [(2, 4, 64, 64), (1, 2, 128, 128), (2, 2, 128, 64)])
+def test_gated_delta_rule_matches_oracle(nk, nv, dk, dv):
+    """The recurrent gated delta rule against the oracle's (Transformers' torch_recurrent_gated_delta_rule), over
+    packed sequences of ragged lengths (the state restarts at each)."""
+    g = rng(22)
+    lengths = [1, 17, 200, 33]
+    t = sum(lengths)
+    width = 2 * nk * dk + nv * dv
+    qkv = bf16(g.standard_normal((t, width)))
+    ab = bf16(g.standard_normal((t, 2 * nv)))
+    a_log = bf16(np.log(g.uniform(1, 16, nv)))
+    dt = np.exp(g.uniform(np.log(1e-3), np.log(1e-1), nv))
+    dt_bias = bf16(dt + np.log(-np.expm1(-dt)))
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int32)
+    got = ops.gated_delta_rule(qkv, ab, a_log, dt_bias, torch.from_numpy(cu).to(DEV), nk, nv, dk, dv)
+    x = qkv.float().cpu().numpy()
+    q = x[:, :nk * dk].reshape(t, nk, dk).repeat(nv // nk, axis=1)
+    k = x[:, nk * dk:2 * nk * dk].reshape(t, nk, dk).repeat(nv // nk, axis=1)
+    v = x[:, 2 * nk * dk:].reshape(t, nv, dv)
+    abn = ab.float().cpu().numpy()
+    b, a = abn[:, :nv], abn[:, nv:]
+    gg = -np.exp(a_log.float().cpu().numpy()) * oracle.packed.softplus(a + dt_bias.float().cpu().numpy())
+    beta = oracle.bf16(1.0 / (1.0 + np.exp(-b)))
+    want = oracle.packed.gated_delta_rule(q, k, v, gg, beta, cu).reshape(t, nv * dv)
+    assert np.abs(got.float().cpu().numpy() - want).max() <= 2 ** -7 * max(np.abs(want).max(), 1.0)
+
+
+def test_gated_norm_matches_oracle():
+    g = rng(23)
+    t, heads, dv = 77, 4, 128
+    x = bf16(g.standard_normal((t, heads * dv)))
+    z = bf16(g.standard_normal((t, heads * dv)))
+    w = bf16(1 + 0.1 * g.standard_normal(dv))
+    got = ops.gated_norm(x, z, w, heads, dv, 1e-6).float().cpu().numpy()
+    xn = x.float().cpu().numpy().reshape(t, heads, dv)
+    normed = oracle.bf16(xn / np.sqrt((xn * xn).mean(-1, keepdims=True) + 1e-6))
+    normed = oracle.bf16(w.float().cpu().numpy() * normed)
+    want = oracle.bf16(normed * oracle.packed.silu(z.float().cpu().numpy().reshape(t, heads, dv)))
+    assert np.abs(got - want.reshape(t, -1)).max() <= 2 ** -7 * max(np.abs(want).max(), 1.0)
