@@ -17,45 +17,90 @@ namespace dn {
 
 // ------------------------------------------------------------------------------------------------ convolution
 
-// out[t, c] = bf16(silu(sum_s w[c, K-1-s] x[t-s, c])) over taps s with seqpos[t] >= s: 8 channels of one row per
-// thread (16-byte loads), float32 sums in tap order.
+// out[t, c] = bf16(silu(sum_s w[c, K-1-s] x[t-s, c])) over taps s with seqpos[t] >= s, float32 sums in tap order.
+// A thread takes 8 channels (16-byte loads) of ROWS_PER_THREAD consecutive rows: its taps are loaded once and the
+// K - 1 rows before each row come from registers, so every input row is read from memory about once.
+constexpr int ROWS_PER_THREAD = 16;
+
 template <int K>
 __global__ void conv_silu_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int64_t T, int C,
                                  const __nv_bfloat16* __restrict__ w, const int64_t* __restrict__ seqpos,
                                  __nv_bfloat16* __restrict__ out, int64_t ldo) {
   const int groups = C / 8;
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (idx >= T * groups) return;
-  const int64_t t = idx / groups;
-  const int c0 = (int)(idx % groups) * 8;
-  const int64_t pos = seqpos[t];
+  const int64_t blocks = (T + ROWS_PER_THREAD - 1) / ROWS_PER_THREAD;
+  if (idx >= blocks * groups) return;
+  const int c0 = (int)(idx % groups) * 8;  // consecutive threads: consecutive channel groups of the same rows
+  const int64_t r0 = (idx / groups) * ROWS_PER_THREAD;
+  const int64_t r1 = r0 + ROWS_PER_THREAD < T ? r0 + ROWS_PER_THREAD : T;
+  // taps of channels c0..c0+7: 8 x K contiguous bf16
   float taps[8][K];
+  {
+    const __nv_bfloat16* wp = w + (int64_t)c0 * K;
 #pragma unroll
-  for (int e = 0; e < 8; ++e)
+    for (int q = 0; q < K; ++q) {  // 8 * K elements = K 16-byte pieces
+      const uint4 raw = *reinterpret_cast<const uint4*>(wp + 8 * q);
+      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-    for (int k = 0; k < K; ++k) taps[e][k] = __bfloat162float(w[(int64_t)(c0 + e) * K + k]);
-  float acc[8];
-#pragma unroll
-  for (int s = 0; s < K; ++s) {
-    if (s > 0 && pos < s) break;
-    const uint4 raw = *reinterpret_cast<const uint4*>(x + (t - s) * ldx + c0);
-    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 f = unpack_bf16x2(words[e]);
-      if (s == 0) {
-        acc[2 * e] = f.x * taps[2 * e][K - 1];
-        acc[2 * e + 1] = f.y * taps[2 * e + 1][K - 1];
-      } else {
-        acc[2 * e] = fmaf(f.x, taps[2 * e][K - 1 - s], acc[2 * e]);
-        acc[2 * e + 1] = fmaf(f.y, taps[2 * e + 1][K - 1 - s], acc[2 * e + 1]);
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(words[e]);
+        const int i0 = 8 * q + 2 * e;  // flat index channel * K + tap
+        taps[i0 / K][i0 % K] = f.x;
+        taps[(i0 + 1) / K][(i0 + 1) % K] = f.y;
       }
     }
   }
-  uint32_t packed[4];
+  // hist[s]: the row s back from the current one (s = 1 .. K - 1), zero before the pack's first row
+  float hist[K][8];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) packed[e] = pack_bf16x2(silu(acc[2 * e]), silu(acc[2 * e + 1]));
-  *reinterpret_cast<uint4*>(out + t * ldo + c0) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  for (int s = 1; s < K; ++s) {
+#pragma unroll
+    for (int e = 0; e < 8; ++e) hist[s][e] = 0.f;
+    if (r0 - s >= 0) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(x + (r0 - s) * ldx + c0);
+      const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = unpack_bf16x2(words[e]);
+        hist[s][2 * e] = f.x;
+        hist[s][2 * e + 1] = f.y;
+      }
+    }
+  }
+  for (int64_t t = r0; t < r1; ++t) {
+    const int64_t pos = seqpos[t];
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + t * ldx + c0);
+    const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
+    float cur[8];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(words[e]);
+      cur[2 * e] = f.x;
+      cur[2 * e + 1] = f.y;
+    }
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = cur[e] * taps[e][K - 1];
+#pragma unroll
+    for (int s = 1; s < K; ++s) {
+      if (pos >= s) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(hist[s][e], taps[e][K - 1 - s], acc[e]);
+      }
+    }
+#pragma unroll
+    for (int s = K - 1; s > 1; --s)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hist[s][e] = hist[s - 1][e];
+    if constexpr (K > 1) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) hist[1][e] = cur[e];
+    }
+    uint32_t packed[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) packed[e] = pack_bf16x2(silu(acc[2 * e]), silu(acc[2 * e + 1]));
+    *reinterpret_cast<uint4*>(out + t * ldo + c0) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------ delta rule
@@ -256,6 +301,7 @@ using namespace kd;
 extern "C" int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const void* weight, int K,
                             const int64_t* seqpos, void* out, int64_t ldo, cudaStream_t stream) {
   if (T < 0 || C <= 0 || C % 8 || K < 1 || K > 4) return set_error(KD_ERR_ARGUMENT, "conv_silu: bad sizes");
+  if (reinterpret_cast<uintptr_t>(weight) & 15) return set_error(KD_ERR_ARGUMENT, "conv_silu: 16-byte aligned taps");
   if (T == 0) return KD_OK;
   if (!x || !weight || !seqpos || !out) return set_error(KD_ERR_ARGUMENT, "conv_silu: null pointer");
   if (ldx < C || ldo < C || ldx % 8 || ldo % 8 || (reinterpret_cast<uintptr_t>(x) & 15) ||
@@ -264,7 +310,7 @@ extern "C" int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const 
   const auto* xi = static_cast<const __nv_bfloat16*>(x);
   const auto* wi = static_cast<const __nv_bfloat16*>(weight);
   auto* oi = static_cast<__nv_bfloat16*>(out);
-  const int64_t n = T * (C / 8);
+  const int64_t n = (T + dn::ROWS_PER_THREAD - 1) / dn::ROWS_PER_THREAD * (C / 8);
   const unsigned blocks = (unsigned)((n + 255) / 256);
   switch (K) {
     case 1: dn::conv_silu_kernel<1><<<blocks, 256, 0, stream>>>(xi, ldx, T, C, wi, seqpos, oi, ldo); break;

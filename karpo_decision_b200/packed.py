@@ -451,6 +451,8 @@ class Packed(torch.nn.Module):
         (families/gemma/packed.py:103-151; None without branches) and the reference's refusals of malformed packs:
         Qwen reads joint layouts only (families/qwen/packed.py:180-181); a Gemma block's readout marker is its last
         token, one per block or branch (families/gemma/packed.py:136-143)."""
+        if getattr(p, "pixel_values", None) is not None:
+            raise NotImplementedError("packs with images are not run by the B200 path")
         seg = p.segment_ids_cpu
         if self.family != "gemma":
             if p.segment_ids is not None:
