@@ -174,6 +174,12 @@ int kd_attention_varlen(const void* q, int64_t ldq, const void* k, int64_t ldk, 
 int kd_gather_rows(const void* src, int64_t ld_src, const int64_t* rows, int64_t n, int width, void* dst,
                    int64_t ld_dst, cudaStream_t stream);
 
+/* dst[rows[i], :] = src[i, :] for n bf16 rows of `width` elements (rows distinct, width % 8 == 0): image features
+ * written at their soft-token rows, and the image rows' attention written back over a sliding layer's output.
+ * Replaces index_copy in families/gemma/packed.py:318-320 and families/gemma/vision.py:210. */
+int kd_scatter_rows(const void* src, int64_t ld_src, const int64_t* rows, int64_t n, int width, void* dst,
+                    int64_t ld_dst, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- Gated DeltaNet
  * Qwen3.5's linear-attention token mixer (families/qwen/packed.py:74-106) between its input projection
  * [q | k | v | z | b | a] and its output projection. */

@@ -265,6 +265,18 @@ __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_
   for (int c = lane; c < width / 8; c += 32) d[c] = s[c];
 }
 
+// dst[rows[i], :] = src[i, :] (rows distinct): one warp per row, 16-byte copies.
+__global__ void scatter_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t ld_src,
+                                    const int64_t* __restrict__ rows, int64_t n, int width,
+                                    __nv_bfloat16* __restrict__ dst, int64_t ld_dst) {
+  const int64_t i = (int64_t)blockIdx.x * WARPS + threadIdx.x / 32;
+  if (i >= n) return;
+  const int lane = threadIdx.x & 31;
+  const uint4* s = reinterpret_cast<const uint4*>(src + i * ld_src);
+  uint4* d = reinterpret_cast<uint4*>(dst + rows[i] * ld_dst);
+  for (int c = lane; c < width / 8; c += 32) d[c] = s[c];
+}
+
 // cs[i * T + t] = bf16 cos | bf16 sin << 16 of rotary pair i at seqpos[t] (t fastest: coalesced writes).
 __global__ void rope_gather_kernel(const int64_t* __restrict__ seqpos, int64_t T, const float* __restrict__ cos_tab,
                                    const float* __restrict__ sin_tab, int rot, uint32_t* __restrict__ cs) {
@@ -574,4 +586,17 @@ extern "C" int kd_gather_rows(const void* src, int64_t ld_src, const int64_t* ro
                                                                   rows, n, width, static_cast<__nv_bfloat16*>(dst),
                                                                   ld_dst);
   return record_cuda_error(cudaGetLastError(), "gather_rows: launch");
+}
+
+extern "C" int kd_scatter_rows(const void* src, int64_t ld_src, const int64_t* rows, int64_t n, int width, void* dst,
+                               int64_t ld_dst, cudaStream_t stream) {
+  if (n < 0 || width <= 0 || width % 8 || ld_src < width || ld_dst < width || ld_src % 8 || ld_dst % 8)
+    return set_error(KD_ERR_ARGUMENT, "scatter_rows: bad sizes or strides (width % 8 == 0, 16-byte rows)");
+  if (n == 0) return KD_OK;
+  if (!src || !rows || !dst || !aligned16(src) || !aligned16(dst))
+    return set_error(KD_ERR_ARGUMENT, "scatter_rows: null or unaligned pointer");
+  ew::scatter_rows_kernel<<<blocks_for(n), 32 * WARPS, 0, stream>>>(static_cast<const __nv_bfloat16*>(src), ld_src,
+                                                                   rows, n, width, static_cast<__nv_bfloat16*>(dst),
+                                                                   ld_dst);
+  return record_cuda_error(cudaGetLastError(), "scatter_rows: launch");
 }

@@ -95,6 +95,8 @@ class Graphs:
         """The smallest bucket holding pack ``p``, or None when it runs the plain path."""
         if p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
             return None  # branched layouts plan their virtual sequences per pack
+        if getattr(p, "pixel_values", None) is not None:
+            return None  # images plan their rows per pack
         t = int(p.input_ids.numel())
         n = int(p.cu.numel()) - 1
         if n > self.max_sequences:

@@ -292,6 +292,18 @@ def qkv_projection(a: torch.Tensor, w: torch.Tensor, seqpos: torch.Tensor, heads
     return q, k, v, gate
 
 
+def scatter_rows(src: torch.Tensor, rows: torch.Tensor, dst: torch.Tensor) -> torch.Tensor:
+    """``dst[rows] = src`` for bf16 rows (distinct ``rows``, int64 on the device); returns ``dst``."""
+    _require(src.dtype == torch.bfloat16 and dst.dtype == torch.bfloat16, "scatter_rows: bf16 rows")
+    _require(src.stride(-1) == 1 and dst.stride(-1) == 1, "scatter_rows: rows with unit inner stride")
+    _require(rows.dtype == torch.int64 and rows.is_contiguous(), "scatter_rows: contiguous int64 rows")
+    width = int(np.prod(src.shape[1:])) if src.dim() > 1 else 1
+    _require(width == int(np.prod(dst.shape[1:])), "scatter_rows: row widths differ")
+    call("kd_scatter_rows", src.data_ptr(), src.stride(0), rows.data_ptr(), rows.numel(), width, dst.data_ptr(),
+         dst.stride(0), _stream(src))
+    return dst
+
+
 def gather_rows(src: torch.Tensor, rows: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """``src[rows]`` for bf16 rows (src (T, ...) with contiguous rows; rows int64 on the device)."""
     _require(src.dtype == torch.bfloat16 and src.is_contiguous(), "gather_rows: contiguous bf16 source")

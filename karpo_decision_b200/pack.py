@@ -30,6 +30,8 @@ class Pack:
     rope: torch.Tensor | None = None
     plan: Any = None
     markers_cpu: torch.Tensor | None = None  # the markers on the host (planning checks need no device read)
+    pixel_values: torch.Tensor | None = None  # images: what the model's image_features reads (model/packed.py:43-48)
+    image_position_ids: torch.Tensor | None = None
 
     @property
     def tokens(self) -> int:
@@ -94,4 +96,6 @@ def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: boo
         segment_ids=None if seg_cpu is None else seg_cpu.to(device, non_blocking=True),
         segment_ids_cpu=seg_cpu,
         markers_cpu=torch.from_numpy(np.asarray(arrays["markers"], dtype=np.int64)),
+        pixel_values=(torch.from_numpy(np.ascontiguousarray(arrays["pixel_values"])).to(device)
+                      if arrays.get("pixel_values") is not None else None),
     )

@@ -26,13 +26,13 @@ from __future__ import annotations
 
 import math
 from dataclasses import dataclass
-from typing import Any
+from typing import Any, Callable
 
 import numpy as np
 import torch
 
 from . import ops
-from .plan import BlockPlan, block_plan, marker_bounds
+from .plan import BlockPlan, ImagePlan, block_plan, image_plan, marker_bounds
 from .synthetic import Spec
 
 #: Qwen's FP8 path keeps projections with fewer outputs in bf16 (serve/qwen_fp8.py:17).
@@ -193,8 +193,13 @@ class Packed(torch.nn.Module):
     ``family.Packed(backbone, attention)`` does (decider.py:35)."""
 
     def __init__(self, spec: Spec, weights: dict[str, Any], device: torch.device | str = "cuda",
-                 attention: str | None = None, fp8: bool = False) -> None:
+                 attention: str | None = None, fp8: bool = False, image_token_id: int | None = None,
+                 image_features: Callable[[Any], torch.Tensor] | None = None) -> None:
         super().__init__()
+        #: Gemma 4 images: the soft-token id and the pack's image features ((soft tokens, hidden), images in pack
+        #: order), made by the backbone's vision encoder outside this path (families/gemma/vision.py:136-144).
+        self.image_token_id = image_token_id
+        self.image_features = image_features
         attention = spec.attention if attention is None else attention
         if attention not in ("causal", "bidirectional"):
             raise ValueError(f"attention must be 'causal' or 'bidirectional', not {attention!r}")
@@ -381,7 +386,19 @@ class Packed(torch.nn.Module):
         device = next(lm.parameters()).device
         if device.type != "cuda":
             device = torch.device("cuda")
-        return cls(spec, weights, device, attention, fp8)
+        image_token = getattr(getattr(backbone, "config", None), "image_token_id", None)
+        features = None
+        if family == "gemma" and (getattr(backbone, "vision_tower", None) is not None or
+                                  getattr(backbone, "embed_vision", None) is not None):
+            def features(p: Any) -> torch.Tensor:
+                """Every image's soft-token embeddings in order, from the backbone's own vision tower and embedder
+                (or its encoder-free embedder), as families/gemma/vision.py:136-144 makes them."""
+                reader = getattr(backbone, "vision_tower", None) or backbone.embed_vision
+                param = next(reader.parameters())
+                out = backbone.get_image_features(p.pixel_values.to(param.device, param.dtype),
+                                                  p.image_position_ids.to(param.device), return_dict=True)
+                return torch.cat(list(out.pooler_output))
+        return cls(spec, weights, device, attention, fp8, image_token_id=image_token, image_features=features)
 
     # ---------------------------------------------------------------- rotary tables
 
@@ -444,7 +461,17 @@ class Packed(torch.nn.Module):
     def forward(self, p: Any) -> torch.Tensor:
         """(M, hidden) final-normalized hidden states at the markers, in pack order."""
         plan = self.plan(p)
-        return self.head(self.body(p, plan), p, plan)
+        images = self.images(p)
+        return self.head(self.body(p, plan, images), p, plan)
+
+    def images(self, p: Any) -> ImagePlan | None:
+        """The pack's image plan (None without images): each image's soft-token rows and the keys they see in the
+        sliding layers (families/gemma/packed.py:310-315)."""
+        if getattr(p, "pixel_values", None) is None:
+            return None
+        seg = None if p.segment_ids_cpu is None else p.segment_ids_cpu.numpy()
+        return image_plan(p.input_ids.cpu().numpy(), [int(x) for x in p.cu_cpu.tolist()], seg,
+                          p.seqpos.cpu().numpy(), self.image_token_id, self.window, self.device)
 
     def plan(self, p: Any) -> BlockPlan | None:
         """Host planning of a pack, done before any kernel is queued: the virtual sequences of branched block layouts
@@ -452,7 +479,13 @@ class Packed(torch.nn.Module):
         Qwen reads joint layouts only (families/qwen/packed.py:180-181); a Gemma block's readout marker is its last
         token, one per block or branch (families/gemma/packed.py:136-143)."""
         if getattr(p, "pixel_values", None) is not None:
-            raise NotImplementedError("packs with images are not run by the B200 path")
+            if self.family != "gemma":
+                raise NotImplementedError("Qwen packs with images (M-RoPE positions) are not run by the B200 path")
+            if not self.prune_last:  # families/gemma/packed.py:311-313
+                raise ValueError("images are supported on bidirectional checkpoints only, the ones the image path was "
+                                 "validated on")
+            if self.image_token_id is None or self.image_features is None:
+                raise ValueError("a pack with images needs the model's image_token_id and image_features")
         seg = p.segment_ids_cpu
         if self.family != "gemma":
             if p.segment_ids is not None:
@@ -479,10 +512,12 @@ class Packed(torch.nn.Module):
         hm = self._last_layer_at_markers(h, p, plan)
         return ops.rmsnorm(hm, self.norm, mode, self.spec.eps)
 
-    def body(self, p: Any, plan: BlockPlan | None = None) -> torch.Tensor:
+    def body(self, p: Any, plan: BlockPlan | None = None, images: ImagePlan | None = None) -> torch.Tensor:
         """(T, hidden) hidden states after every layer the whole pack runs (all but the last in a bidirectional
         model; the workspace's residual buffer): embedding and layers, no host synchronization, so it can be captured
-        in a CUDA graph when ``p``'s tensors are static. Branched block layouts need their ``plan``."""
+        in a CUDA graph when ``p``'s tensors are static. Branched block layouts need their ``plan``; packs with
+        images their ``images`` (the features written at the soft-token rows, which see their whole image in the
+        sliding layers)."""
         s = self.spec
         if plan is None and p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
             plan = self.plan(p)
@@ -490,6 +525,11 @@ class Packed(torch.nn.Module):
         ws = self.workspace(t)
         qwen = s.family == "qwen"
         h = ops.embed(p.input_ids, self.embed_tokens, 0.0 if qwen else math.sqrt(s.hidden), out=ws.h[:t])
+        if images is not None:  # the features over the scaled token embeddings, unscaled (families/gemma/packed.py:316)
+            features = self.image_features(p)
+            if features.shape[0] != images.rows.numel():
+                raise ValueError(f"{images.rows.numel()} soft tokens for {features.shape[0]} image features")
+            ops.scatter_rows(features.to(device=self.device, dtype=torch.bfloat16).contiguous(), images.rows, h)
         rope_cs: dict[str, torch.Tensor] = {}  # per rotary kind, gathered once per pack
         for layer in self.layers[:-1] if self.prune_last else self.layers:
             if layer.kind == "linear_attention":
@@ -507,6 +547,13 @@ class Packed(torch.nn.Module):
                 kg, vg = ops.gather_rows(k, rows), ops.gather_rows(v, rows)
                 o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, self._scale, window, gate=gate,
                                          out=o_buf)
+            if images is not None and layer.kind == "sliding_attention":
+                # each image's rows again, over the window before the image and the whole image
+                # (families/gemma/vision.py:199-210)
+                oi = ops.attention_varlen(ops.gather_rows(q, images.rows), ops.gather_rows(k, images.keys),
+                                          ops.gather_rows(v, images.keys), images.q_cu, images.k_cu, images.max_q,
+                                          self._scale, (self.window - 1, -1))
+                ops.scatter_rows(oi, images.rows, o)
             self._after_attention(layer, h, o, ws)
         return h
 

@@ -80,3 +80,57 @@ def block_plan(cu_cpu: torch.Tensor, segment_ids_cpu: torch.Tensor, window: int,
     return BlockPlan(q_cu=dev(q_cu, torch.int32), g_rows=dev(np.concatenate(g_rows), torch.int64),
                      g_cu=dev(g_cu, torch.int32), s_rows=dev(np.concatenate(s_rows), torch.int64),
                      s_cu=dev(s_cu, torch.int32), max_q=int(np.diff(q_cu).max()), m_cu=m_cu)
+
+
+@dataclass
+class ImagePlan:
+    """Each image's soft-token rows in a pack of block layouts, for the sliding layers (families/gemma/vision.py:
+    146-210): every soft token's row (images in pack order, each a run of rows), and per image the key rows it sees,
+    whose positions run contiguously up to the image's end (the window before the image inside what its block reads,
+    then the image itself), so the end-aligned window (W - 1, unbounded right) of the varlen contract over those keys
+    is the reference's mask: a key at or after the query's position - (W - 1), the whole image included."""
+
+    rows: torch.Tensor  # int64 soft-token rows, image by image
+    q_cu: torch.Tensor  # (images + 1,) int32 bounds over ``rows``
+    keys: torch.Tensor  # int64 key rows, image by image
+    k_cu: torch.Tensor  # (images + 1,) int32 bounds over ``keys``
+    max_q: int
+
+
+def image_plan(input_ids: np.ndarray, bounds: list[int], segments: np.ndarray | None, positions: np.ndarray,
+               soft: int, window: int, device: torch.device) -> ImagePlan:
+    """The plan of a pack's images from host arrays (``soft``: the soft-token id), with the reference's refusals:
+    no soft token in a pack with images, an image longer than the sliding window (families/gemma/vision.py:174-196).
+    An image in a shared block (or a sequence's only block) sees the rows before it within the window; one in a branch
+    sees the shared block's rows within the window by position and its branch's rows before it."""
+    input_ids = np.asarray(input_ids)
+    positions = np.asarray(positions, dtype=np.int64)
+    segments = np.zeros(len(input_ids), dtype=np.int64) if segments is None else np.asarray(segments)
+    rows = np.flatnonzero(input_ids == soft)
+    if rows.size == 0:
+        raise ValueError("a pack with images has no image soft tokens")
+    breaks = (np.flatnonzero(rows[1:] != rows[:-1] + 1) + 1).tolist()
+    q_cu, k_cu, keys = [0], [0], []
+    max_q = 0
+    for a, b in zip([0, *breaks], [*breaks, len(rows)], strict=True):
+        s, e = int(rows[a]), int(rows[b - 1]) + 1
+        if e - s > window:
+            raise ValueError(f"an image of {e - s} soft tokens is longer than the sliding window ({window})")
+        start = bounds[int(np.searchsorted(bounds, s, side="right")) - 1]
+        if int(segments[s]) == 0:
+            seen = np.arange(max(start, s - (window - 1)), e)
+        else:
+            shared = int((segments[start:s] == 0).sum())  # the shared block's length: branch positions follow it
+            branch = s - (int(positions[s]) - shared)  # the branch's first row
+            first = min(max(0, int(positions[s]) - (window - 1)), shared)  # the first shared position it sees
+            seen = np.concatenate([np.arange(start + first, start + shared), np.arange(branch, e)])
+        keys.append(seen)
+        q_cu.append(q_cu[-1] + e - s)
+        k_cu.append(k_cu[-1] + len(seen))
+        max_q = max(max_q, e - s)
+
+    def dev(x, dtype):
+        return torch.as_tensor(np.asarray(x), dtype=dtype).to(device)
+
+    return ImagePlan(rows=dev(rows, torch.int64), q_cu=dev(q_cu, torch.int32),
+                     keys=dev(np.concatenate(keys), torch.int64), k_cu=dev(k_cu, torch.int32), max_q=max_q)

@@ -375,6 +375,48 @@ def block_plan(cu: np.ndarray, segment_ids: np.ndarray, window: int) -> dict:
             "s_rows": np.concatenate(s_rows), "s_cu": np.array(s_cu)}
 
 
+def image_spans(pack: dict, window: int) -> list[tuple[int, int, np.ndarray]]:
+    """Per image (a run of soft-token rows ``pack["image_token"]``): (s, e, the rows its queries may see) as
+    families/gemma/vision.py:174-196 plans them: in a shared (or only) block the rows before it within the window,
+    in a branch the shared block's rows within the window by position and the branch's rows before it; then the
+    image itself."""
+    ids, cu, pos = pack["input_ids"], pack["cu"].tolist(), pack["seqpos"]
+    seg = pack.get("segment_ids")
+    seg = np.zeros(len(ids), dtype=np.int64) if seg is None else seg
+    rows = np.flatnonzero(ids == pack["image_token"])
+    breaks = (np.flatnonzero(rows[1:] != rows[:-1] + 1) + 1).tolist()
+    out = []
+    for a, b in zip([0, *breaks], [*breaks, len(rows)], strict=True):
+        s, e = int(rows[a]), int(rows[b - 1]) + 1
+        start = max(c for c in cu if c <= s)
+        if int(seg[s]) == 0:
+            seen = np.arange(max(start, s - (window - 1)), e)
+        else:
+            shared = int((seg[start:s] == 0).sum())
+            branch = s - (int(pos[s]) - shared)
+            first = min(max(0, int(pos[s]) - (window - 1)), shared)
+            seen = np.concatenate([np.arange(start + first, start + shared), np.arange(branch, e)])
+        out.append((s, e, seen))
+    return out
+
+
+def see_whole(o: np.ndarray, q: np.ndarray, k: np.ndarray, v: np.ndarray, pack: dict, window: int,
+              scale: float) -> np.ndarray:
+    """A sliding layer's output with each image's rows recomputed (families/gemma/vision.py:199-210): query row r
+    sees key row c of its ``seen`` rows when position(c) >= position(r) - (window - 1), its whole image included."""
+    pos = pack["seqpos"]
+    out = o.copy()
+    group = q.shape[1] // k.shape[1]
+    for s, e, seen in image_spans(pack, window):
+        mask = pos[seen][None, :] >= pos[s:e][:, None] - (window - 1)
+        for h in range(q.shape[1]):
+            scores = (q[s:e, h].astype(np.float32) @ k[seen, h // group].astype(np.float32).T) * np.float32(scale)
+            scores = np.where(mask, scores, -np.inf)
+            p = np.exp(scores - scores.max(-1, keepdims=True))
+            out[s:e, h] = (p @ v[seen, h // group].astype(np.float32)) / p.sum(-1, keepdims=True)
+    return out
+
+
 def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8: bool = False) -> np.ndarray:
     """(M, hidden) at the markers: families/gemma/packed.py:305-323 over single-block sequences (each virtual sequence
     is a whole sequence) or over block layouts with branches (``block_plan`` :103-151, virtual sequences whose keys
@@ -404,6 +446,9 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
     if mode == "bf16":
         scale = bf16(np.array([scale]))[0]
     h = _round(weights["embed_tokens"][ids] * scale, mode)
+    images = pack.get("image_features")
+    if images is not None:  # the vision features over the soft-token rows, unscaled (families/gemma/packed.py:316-320)
+        h[ids == pack["image_token"]] = _round(images.astype(np.float32), mode)
     types = gemma_layer_types(spec)
     proportional = spec.get("global_rope", "default") == "proportional"
     tables = {
@@ -442,6 +487,8 @@ def gemma_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8
             rows, k_cu = (plan["s_rows"], plan["s_cu"]) if types[i] == "sliding_attention" else \
                 (plan["g_rows"], plan["g_cu"])
             o = attention_varlen(q, k[rows], v[rows], plan["q_cu"], k_cu, 1.0, window)
+        if images is not None and types[i] == "sliding_attention":
+            o = see_whole(o, q, k, v, pack, w_len, 1.0)
         o = _round(o, mode).reshape(t, hq * hd)
         a = linear(o, weights[p + "o_proj"], mode, fp8)
         h = _round(h + rms_norm(a, weights[p + "post_attention_layernorm"], eps, False), mode)

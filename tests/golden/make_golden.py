@@ -26,6 +26,7 @@ from __future__ import annotations
 
 import argparse
 import contextlib
+import dataclasses
 import hashlib
 import sys
 import types
@@ -40,6 +41,15 @@ sys.path.insert(0, str(HERE.parents[1]))
 
 from karpo_decision_b200.synthetic import (  # noqa: E402
     CONFIGS, Spec, numpy_weights, small, synthetic_block_arrays, synthetic_pack_arrays)
+
+
+#: The image soft-token id of the image cases (the last vocabulary id; other tokens never take it).
+IMAGE_TOKEN = 4095
+
+
+def oracle_bf16(x: np.ndarray) -> np.ndarray:
+    """float32 values rounded to bf16 (round to nearest even), kept as float32."""
+    return torch.from_numpy(x).bfloat16().float().numpy()
 
 
 def varlen_contract(q, k, v, cu_q, cu_k, max_q, max_k, scale=None, window_size=(-1, -1), enable_gqa=False):
@@ -271,6 +281,12 @@ CASES = {
     "qwen_hybrid": dict(spec=small(CONFIGS["tiny"], layers=4, full_every=2, partial_rotary=0.5, lin_k_heads=2,
                                    lin_v_heads=4, lin_k_dim=64, lin_v_dim=64),
                         lengths=("uniform", 6, 8, 200), markers=(1, 3), fp8=False),
+    # Gemma 4 images (bidirectional checkpoints): soft-token runs in a single block, a shared block, a branch and at a
+    # sequence's start; features stand in for the vision encoder's output (families/gemma/vision.py:136-144).
+    "gemma_images": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
+                                   attention="bidirectional"),
+                         blocks=[(40, []), (30, [12, 20]), (25, [])], fp8=False,
+                         images=[(10, 13), (45, 10), (85, 12), (102, 9)]),
     "gemma_blocks_bidir": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,
                                          attention="bidirectional"),
                                blocks=[(23, []), (21, [5, 7, 3]), (14, [4, 9]), (3, [20, 25])], fp8=False),
@@ -324,7 +340,19 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
         rng = np.random.default_rng(seed)
         lengths = [int(x) for x in rng.integers(low, high + 1, size=n)]
         arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, case["markers"])
+    features = None
+    if "images" in case:  # soft tokens (id vocab - 1) over the given (row, length) runs, and their features
+        arrays = dict(arrays, input_ids=arrays["input_ids"].copy())
+        arrays["input_ids"][arrays["input_ids"] == IMAGE_TOKEN] = 0
+        for row, length in case["images"]:
+            arrays["input_ids"][row:row + length] = IMAGE_TOKEN
+        n_soft = sum(length for _, length in case["images"])
+        features = np.random.default_rng(seed + 2).standard_normal((n_soft, spec.hidden)).astype(np.float32) * 0.3
+        arrays["image_features"] = oracle_bf16(features)
     seqs = encoded(arrays, blocks=spec.family == "gemma")
+    if features is not None:  # the sequences with soft tokens carry (placeholder) pixels, so the pack has images
+        seqs = [dataclasses.replace(q, pixel_values=torch.zeros(1, 1), image_position_ids=torch.zeros(1, 1, 2))
+                if bool((q.input_ids == IMAGE_TOKEN).any()) else q for q in seqs]
     head = Readout.from_rows(to_torch(weights, "readout"), cap=spec.logit_cap)
     captured: dict = {}
     with torch.inference_mode(), contextlib.ExitStack() as stack:
@@ -350,7 +378,11 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
             lm = gemma_lm(spec, weights)
             stack.enter_context(_patched(sliding_attention, "varlen_attn", varlen_contract))
             stack.enter_context(_patched(gp, "sdpa_kernel", lambda *_: contextlib.nullcontext()))
-            packed = gp.Packed(types.SimpleNamespace(language_model=lm), spec.attention)
+            backbone = types.SimpleNamespace(language_model=lm, config=types.SimpleNamespace(image_token_id=IMAGE_TOKEN))
+            if features is not None:  # the vision encoder's output, given
+                given = torch.from_numpy(arrays["image_features"])
+                stack.enter_context(_patched(gp.vision, "embed", lambda *_: given))
+            packed = gp.Packed(backbone, spec.attention)
             if case["fp8"]:
                 from karpo_decision.serve import fp8
                 stack.enter_context(_patched(fp8, "to_e4m3", fp8._rows_e4m3))
@@ -365,7 +397,7 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
     pins = {}
     for proj, (values, scale, out) in captured.items():
         pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
-    extra = {"segment_ids": arrays["segment_ids"]} if "segment_ids" in arrays else {}
+    extra = {k: arrays[k] for k in ("segment_ids", "image_features") if k in arrays}
     return {
         **pins, **extra,
         "input_ids": arrays["input_ids"], "seqpos": arrays["seqpos"], "cu": arrays["cu"],

@@ -11,8 +11,9 @@ import numpy as np
 from karpo_decision_b200.synthetic import Spec, numpy_weights
 
 GOLDEN = Path(__file__).resolve().parent / "golden"
+IMAGE_TOKEN = 4095  # the image cases' soft-token id
 CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_tiny_fp8", "gemma_tiny_fp8", "qwen_bidir",
-         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid"]
+         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid", "gemma_images"]
 
 
 def load(name: str) -> tuple[Spec, dict, dict, dict]:
@@ -27,6 +28,9 @@ def load(name: str) -> tuple[Spec, dict, dict, dict]:
         h.update(np.ascontiguousarray(weights[key], dtype=np.float32).tobytes())
     if h.hexdigest() != str(z["weights_sha256"]):
         raise AssertionError(f"{name}: regenerated weights differ from the ones the fixture was made with")
-    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu", "segment_ids") if k in z.files}
+    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu", "segment_ids", "image_features")
+            if k in z.files}
+    if "image_features" in pack:  # the image cases' soft-token id (tests/golden/make_golden.py IMAGE_TOKEN)
+        pack["image_token"] = IMAGE_TOKEN
     expected = {"hidden": z["hidden"], "logits": z["logits"]}
     return spec, weights, pack, expected

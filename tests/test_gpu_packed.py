@@ -114,3 +114,26 @@ def test_bidirectional_marker_layer_equals_the_whole_last_layer(name):
     p = from_arrays(arrays, DEV)
     a, b = pruned(p).float(), whole(from_arrays(arrays, DEV)).float()
     assert torch.allclose(a, b, atol=2e-2, rtol=2e-2), (a - b).abs().max().item()
+
+
+def test_gemma_images_match_reference():
+    """Gemma 4 images on a bidirectional checkpoint (families/gemma/vision.py:146-210): the features written at the
+    soft-token rows, each image's rows seeing their whole image in the sliding layers; the vision encoder's output is
+    given (the fixture's features), as the reference's was."""
+    from golden_cases import IMAGE_TOKEN
+
+    spec, weights, arrays, expected = load("gemma_images")
+    model = Packed(spec, weights, DEV, image_token_id=IMAGE_TOKEN, image_features=lambda p: p.pixel_values)
+    head = Readout(weights["readout"], spec.logit_cap, DEV)
+    p = from_arrays(dict(arrays, pixel_values=arrays["image_features"]), DEV)
+    hidden = model(p)
+    logits = head(hidden).cpu().numpy()
+    err = np.abs(logits - expected["logits"]).max()
+    assert err <= 2e-2, err
+    h = hidden.float().cpu().numpy()
+    cosine = (h * expected["hidden"]).sum(-1) / (np.linalg.norm(h, axis=-1) * np.linalg.norm(expected["hidden"],
+                                                                                               axis=-1))
+    assert cosine.min() > 0.995, cosine
+    # without the image path (features dropped) the answer moves: the test sees the images
+    plain = model(from_arrays(arrays, DEV)).float().cpu().numpy()
+    assert np.abs(plain - expected["hidden"]).max() > 10 * np.abs(h - expected["hidden"]).max()

@@ -168,3 +168,33 @@ def test_packed_plan_refuses_what_the_reference_refuses():
     early = dict(good, markers=np.array([2, 11]))
     with pytest.raises(ValueError):
         model.plan(from_arrays(early, cpu))
+
+
+def test_image_plan_matches_oracle_and_refuses_what_the_reference_refuses():
+    """Image rows and key rows (families/gemma/vision.py:160-196) against the oracle's plan, and the refusals: a pack
+    with images but no soft token, an image longer than the sliding window."""
+    import pytest
+
+    import oracle
+    from karpo_decision_b200.plan import image_plan
+    from karpo_decision_b200.synthetic import synthetic_block_arrays
+
+    arrays = synthetic_block_arrays([(40, []), (30, [12, 20]), (25, [])], 100, seed=0)
+    ids = arrays["input_ids"].copy()
+    ids[ids == 99] = 0
+    for row, length in [(10, 13), (45, 10), (85, 12), (102, 9)]:
+        ids[row:row + length] = 99
+    plan = image_plan(ids, arrays["cu"].tolist(), arrays["segment_ids"], arrays["seqpos"], 99, 16,
+                      torch.device("cpu"))
+    spans = oracle.packed.image_spans(dict(arrays, input_ids=ids, image_token=99), 16)
+    assert plan.q_cu.tolist() == [0, 13, 23, 35, 44] and plan.max_q == 13
+    assert plan.keys.tolist() == np.concatenate([seen for _, _, seen in spans]).tolist()
+    # the branch image (rows 85..96, positions 33..44) sees shared positions 18..29 and its branch rows 82..96
+    assert plan.keys[plan.k_cu[2]:plan.k_cu[3]].tolist() == [*range(58, 70), *range(82, 97)]
+    with pytest.raises(ValueError):
+        image_plan(arrays["input_ids"] % 50, arrays["cu"].tolist(), arrays["segment_ids"], arrays["seqpos"], 99, 16,
+                   torch.device("cpu"))
+    long = ids.copy()
+    long[0:17] = 99
+    with pytest.raises(ValueError):
+        image_plan(long, arrays["cu"].tolist(), arrays["segment_ids"], arrays["seqpos"], 99, 16, torch.device("cpu"))
