@@ -308,7 +308,7 @@ def run_ours(args: argparse.Namespace) -> None:
                           "ms_per_step": a_ms / args.steps, "traffic": traffic("attention", args, tokens)},
             "gemm": {"kernel": "kd_gemm_bf16 + kd_qkv_projection" if not args.fp8 else
                      "kd_gemm_fp8 + kd_qkv_projection_fp8", "bound": "tensor", "achieved": gemm_tf,
-                     "ms_per_step": g_ms / args.steps, "traffic": None},
+                     "ms_per_step": g_ms / args.steps, "traffic": traffic("gemm", args, tokens)},
         }
         dominant = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
         top = kernels[dominant]
@@ -401,7 +401,12 @@ def attention_flops(spec, lengths) -> float:
 
 #: DRAM bytes per launch from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) on a smaller pack of the
 #: same configuration, scaled by the tokens a launch processes (Q, K, V and O each move once per launch).
-TRAFFIC_CAPTURES = {("qwen-0.8b", "attention"): (8192, 100.748032e6 + 13.882112e6)}
+# DRAM bytes (read + write) per launch from ncu captures of the same kernels on an 8,192-token pack, scaled to the
+# bench's pack by tokens: attention (one layer's launch), and the GEMM family as the mean of one layer's four launches
+# (QKV + norm + RoPE, o_proj + residual, gate/up + SwiGLU, down + residual). Source: the profiles/ summaries.
+TRAFFIC_CAPTURES = {("qwen-0.8b", "attention"): (8192, 100.771584e6 + 14.428672e6),
+                    ("qwen-0.8b", "gemm"): (8192, (31.583744e6 + 47.450624e6 + 54.546432e6 + 0.334848e6 + 29.390336e6 +
+                                                   5.088512e6 + 73.422592e6 + 1.999104e6) / 4)}
 
 
 def traffic(kernel: str, args, tokens: int) -> float | None:
