@@ -34,8 +34,9 @@ constexpr int THREADS = 64 + EPI_GROUPS * 128;
 // Output staging: per epilogue warp a 32-row x 64-column bf16 box (128-byte swizzled rows) for its TMA stores.
 constexpr int OUT_BOX_COLS = 64;
 constexpr int OUT_BOX_BYTES = 32 * OUT_BOX_COLS * 2;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_GROUPS * 4 * OUT_BOX_BYTES + 1024 /* alignment slack */ +
-                           256 /* barriers */;
+constexpr int NORM_BYTES = 2 * 256 * 2;  // the QKV epilogue's q and k norm weights (bf16, head_dim <= 256)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_GROUPS * 4 * OUT_BOX_BYTES + NORM_BYTES +
+                           1024 /* alignment slack */ + 256 /* barriers */;
 
 // The fused attention-input epilogue (KD_EPI_QKV): the projection's columns are [q heads][k heads][v heads] (Qwen's
 // gated queries: [q_h | gate_h] per head); each output row's heads are normalized, rotated and scattered to q, k, v
@@ -79,6 +80,17 @@ KD_DEVICE void load16(const Args& a, uint32_t taddr, int col, float sa, float (&
   }
 }
 
+// 16 accumulator columns of one row (raw tcgen05.ld registers) as the projection's bf16 outputs (FP8: scaled first).
+template <bool FP8>
+KD_DEVICE void to_bf16_16(const Args& a, const uint32_t (&r)[16], int col, float sa, float (&x)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float v = __uint_as_float(r[j]);
+    if constexpr (FP8) v = v * sa * a.scale_b[col + j];
+    x[j] = bf16_round(v);
+  }
+}
+
 KD_DEVICE void store16(__nv_bfloat16* dst, const float (&x)[16]) {
   uint32_t p[8];
 #pragma unroll
@@ -87,7 +99,7 @@ KD_DEVICE void store16(__nv_bfloat16* dst, const float (&x)[16]) {
   reinterpret_cast<uint4*>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
 }
 
-// The norm multipliers of 16 consecutive head dims (none, w or 1 + w), from two 16-byte loads.
+// The norm multipliers of 16 consecutive head dims (none, w or 1 + w), from two 16-byte loads (shared memory).
 KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
   if (mode != KD_NORM_WEIGHT && mode != KD_NORM_ONE_PLUS) {
 #pragma unroll
@@ -108,17 +120,20 @@ KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
 // One row's heads inside the 256 columns [n0, n0 + 256) of the QKV projection: per-head RMSNorm over head_dim, then
 // rotate-half RoPE on the first `rot` dims (q, k); Gemma's weightless v norm; gate and plain v copied. Two passes
 // over tensor memory: the sum of squares, then the normalized, rotated head in 16-column pieces (a piece below rot / 2
-// together with its rotation partner rot / 2 further on). The rotary factors come from the per-pack table `cs`
-// ([rot / 2][M]: the lanes of a warp read consecutive rows, one coalesced 128-byte line per pair index).
+// together with its rotation partner rot / 2 further on). The epilogue warpgroups take alternate head slices (one
+// group takes all of a 256-wide head). Each step issues its tensor-memory loads, its rotary factors (the per-pack
+// table `cs`, [rot / 2][M]: a warp's lanes read consecutive rows, one coalesced line per pair index) and its norm
+// weights (a shared-memory copy: q_norm then k_norm) before waiting on any of them, so their latencies overlap.
 template <bool FP8>
-KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, float sa, int group) {
+KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, float sa, int group,
+                            const __nv_bfloat16* norm_s) {
   const Qkv& g = a.qkv;
   const int hd = g.hd;
   const int q_cols = g.hq * hd * (g.gated ? 2 : 1);
   const int k_end = q_cols + g.hkv * hd;
   const int crow = row < a.M ? row : a.M - 1;  // rows past M compute (warp-collective loads) but store nothing
   const uint32_t* cs = g.cs + crow;
-  // the epilogue warpgroups share the tile's head slices (one group takes all of a 256-wide head)
+  const int half = g.rot / 2;
   for (int h0 = (hd < BN ? group * hd : 0); h0 < BN; h0 += (hd < BN ? EPI_GROUPS * hd : BN)) {
     if (hd >= BN && group != 0) break;
     const int c0 = n0 + h0;  // first column of this head slice
@@ -146,64 +161,100 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
                          : kind == 2 ? g.k + ((int64_t)row * g.hkv + head) * hd
                                      : g.v + ((int64_t)row * g.hkv + head) * hd;
     const bool normed = kind == 0 || kind == 2 || (kind == 3 && g.v_mode >= 0);
+    const bool rotated = kind == 0 || kind == 2;
     float inv = 1.0f;
     if (normed) {
-      float ss = 0.f;
-      for (int d = 0; d < hd; d += 16) {
-        float x[16];
-        load16<FP8>(a, th + d, c0 + d, sa, x);
+      float ss0 = 0.f, ss1 = 0.f;
+      for (int d = 0; d < hd; d += 32) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(th + d, r0);
+        tmem_ld16(th + d + 16, r1);
+        tmem_ld_wait_regs(r0);
+        tmem_ld_wait_regs(r1);
+        float x[16], y[16];
+        to_bf16_16<FP8>(a, r0, c0 + d, sa, x);
+        to_bf16_16<FP8>(a, r1, c0 + d + 16, sa, y);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) ss += x[j] * x[j];
+        for (int j = 0; j < 16; ++j) {
+          ss0 = fmaf(x[j], x[j], ss0);
+          ss1 = fmaf(y[j], y[j], ss1);
+        }
       }
-      inv = 1.0f / sqrtf(ss / (float)hd + g.eps);
+      inv = 1.0f / sqrtf((ss0 + ss1) / (float)hd + g.eps);
     }
-    if (kind == 1 || kind == 3) {  // gate, v: no rotation
-      for (int d = 0; d < hd; d += 16) {
-        float x[16];
-        load16<FP8>(a, th + d, c0 + d, sa, x);
+    if (!rotated) {  // gate, v: pieces of 32 columns, normalized for Gemma's v
+      for (int d = 0; d < hd; d += 32) {
+        uint32_t r0[16], r1[16];
+        tmem_ld16(th + d, r0);
+        tmem_ld16(th + d + 16, r1);
+        tmem_ld_wait_regs(r0);
+        tmem_ld_wait_regs(r1);
+        float x[16], y[16];
+        to_bf16_16<FP8>(a, r0, c0 + d, sa, x);
+        to_bf16_16<FP8>(a, r1, c0 + d + 16, sa, y);
         if (normed) {
 #pragma unroll
-          for (int j = 0; j < 16; ++j) x[j] *= inv;
+          for (int j = 0; j < 16; ++j) {
+            x[j] *= inv;
+            y[j] *= inv;
+          }
         }
-        if (row < a.M) store16(dst + d, x);
+        if (row < a.M) {
+          store16(dst + d, x);
+          store16(dst + d + 16, y);
+        }
       }
       continue;
     }
-    const __nv_bfloat16* w = kind == 0 ? g.q_norm : g.k_norm;
-    const int half = g.rot / 2;
-    for (int d = 0; d < hd; d += 16) {
-      if (d >= half && d < g.rot) continue;  // written with its partner
-      float x[16], m[16];
-      load16<FP8>(a, th + d, c0 + d, sa, x);
+    const __nv_bfloat16* w = norm_s + (kind == 0 ? 0 : hd);
+    // rotation pairs: the piece at d < rot / 2 with its partner at d + rot / 2
+    for (int d = 0; d < half; d += 16) {
+      uint32_t rx[16], ry[16], f[16];
+      tmem_ld16(th + d, rx);
+      tmem_ld16(th + d + half, ry);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) f[j] = cs[(int64_t)(d + j) * a.M];
+      float mx[16], my[16];
+      norm16(w, g.qk_mode, d, mx);
+      norm16(w, g.qk_mode, d + half, my);
+      tmem_ld_wait_regs(rx);
+      tmem_ld_wait_regs(ry);
+      float x[16], y[16];
+      to_bf16_16<FP8>(a, rx, c0 + d, sa, x);
+      to_bf16_16<FP8>(a, ry, c0 + d + half, sa, y);
+      float ox[16], oy[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float xn = (x[j] * inv) * mx[j];
+        float yn = (y[j] * inv) * my[j];
+        if (g.gated) {  // Qwen: the norm is its own op (rounded), RoPE another
+          xn = bf16_round(xn);
+          yn = bf16_round(yn);
+        }
+        const float2 c_s = unpack_bf16x2(f[j]);  // cos and sin of pair d + j (the same for d + j + half)
+        ox[j] = xn * c_s.x - yn * c_s.y;
+        oy[j] = yn * c_s.x + xn * c_s.y;
+      }
+      if (row < a.M) {
+        store16(dst + d, ox);
+        store16(dst + d + half, oy);
+      }
+    }
+    // the unrotated rest, pieces of 16 columns
+    for (int d = g.rot; d < hd; d += 16) {
+      uint32_t r[16];
+      tmem_ld16(th + d, r);
+      float m[16];
       norm16(w, g.qk_mode, d, m);
+      tmem_ld_wait_regs(r);
+      float x[16];
+      to_bf16_16<FP8>(a, r, c0 + d, sa, x);
 #pragma unroll
       for (int j = 0; j < 16; ++j) {
         x[j] = (x[j] * inv) * m[j];
-        if (g.gated) x[j] = bf16_round(x[j]);  // Qwen: the norm is its own op (rounded), RoPE another
+        if (g.gated) x[j] = bf16_round(x[j]);
       }
-      if (d < half) {
-        uint32_t f[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) f[j] = cs[(int64_t)(d + j) * a.M];
-        float y[16];
-        load16<FP8>(a, th + d + half, c0 + d + half, sa, y);
-        norm16(w, g.qk_mode, d + half, m);
-        float ox[16], oy[16];
-#pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          y[j] = (y[j] * inv) * m[j];
-          if (g.gated) y[j] = bf16_round(y[j]);
-          const float2 c_s = unpack_bf16x2(f[j]);  // cos and sin of pair d + j (the same for d + j + half)
-          ox[j] = x[j] * c_s.x - y[j] * c_s.y;
-          oy[j] = y[j] * c_s.x + x[j] * c_s.y;
-        }
-        if (row < a.M) {
-          store16(dst + d, ox);
-          store16(dst + d + half, oy);
-        }
-      } else if (row < a.M) {
-        store16(dst + d, x);
-      }
+      if (row < a.M) store16(dst + d, x);
     }
   }
 }
@@ -215,12 +266,21 @@ __global__ void __launch_bounds__(THREADS, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* out_stage = smem + STAGES * STAGE_BYTES;  // epilogue warp e's box at e * OUT_BOX_BYTES
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + EPI_GROUPS * 4 * OUT_BOX_BYTES);
+  __nv_bfloat16* norm_s = reinterpret_cast<__nv_bfloat16*>(out_stage + EPI_GROUPS * 4 * OUT_BOX_BYTES);
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + EPI_GROUPS * 4 * OUT_BOX_BYTES + NORM_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* res_bar = acc_empty + 2;  // [epilogue warps]: the residual box of that warp has landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(res_bar + EPI_GROUPS * 4);
+  if constexpr (EPI == KD_EPI_QKV) {  // q / k norm weights into shared memory: the epilogue reads them per head piece
+    const int hd = args.qkv.hd;
+    const bool weighted = args.qkv.qk_mode == KD_NORM_WEIGHT || args.qkv.qk_mode == KD_NORM_ONE_PLUS;
+    for (int i = threadIdx.x; weighted && i < 2 * hd / 8; i += THREADS) {
+      const __nv_bfloat16* src = i < hd / 8 ? args.qkv.q_norm + 8 * i : args.qkv.k_norm + 8 * (i - hd / 8);
+      reinterpret_cast<uint4*>(norm_s)[i] = *reinterpret_cast<const uint4*>(src);
+    }
+  }
 
   const int warp = threadIdx.x / 32;
   const int m_tiles = (args.M + BM - 1) / BM;
@@ -333,7 +393,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       float sa = 1.0f;
       if constexpr (FP8) sa = (row < args.M) ? args.scale_a[row] : 0.0f;
       if constexpr (EPI == KD_EPI_QKV) {
-        qkv_epilogue<FP8>(args, row, n0, t_row, sa, group);
+        qkv_epilogue<FP8>(args, row, n0, t_row, sa, group, norm_s);
       } else {
         // Output through this warp's staging box and TMA stores: 64-column chunks of the warp's 32 rows, written
         // into 128-byte swizzled smem rows (conflict-free: 8 consecutive rows cover all bank groups), then one bulk
