@@ -132,6 +132,35 @@ KD_DEVICE void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "mem
 // Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads of them.
 KD_DEVICE void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 
+// ------------------------------------------------------------------------------------------------ CTA pairs
+// A cluster of two CTAs sharing one tcgen05.mma (cta_group::2): rank 0 (the leader) issues the MMA over both CTAs'
+// shared-memory operands and tensor memory. A shared::cta address with bit 24 cleared names rank 0's copy of it.
+
+KD_DEVICE uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of both CTAs: every earlier shared-memory write and barrier init is visible to the peer after it.
+KD_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+KD_DEVICE uint32_t leader_addr(const void* p) { return smem_u32(p) & 0xFEFFFFFFu; }
+
+// 2-D tiled TMA load into this CTA's shared memory whose completion (bytes) is counted on the leader's barrier
+// at the same offset as `bar`.
+KD_DEVICE void tma_load_2d_pair(const CUtensorMap* map, uint64_t* bar, void* dst, int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(leader_addr(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+// One arrival on the leader's barrier at the same offset as `bar` (from either CTA of the pair).
+KD_DEVICE void mbar_arrive_leader(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(leader_addr(bar)) : "memory");
+}
+
 // ------------------------------------------------------------------------------------------------ tcgen05
 
 // Shared-memory matrix descriptor of a K-major operand tile stored as TMA writes it with 128-byte swizzling: rows of
@@ -167,6 +196,16 @@ KD_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
   asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
 }
 
+KD_DEVICE void tmem_alloc_pair(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols));
+}
+KD_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;");
+}
+KD_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols));
+}
 KD_DEVICE void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 KD_DEVICE void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -198,6 +237,33 @@ KD_DEVICE void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uin
 }
 
 // Arrives once on `bar` when every tcgen05 operation this thread issued before has completed.
+// The pair forms: D (256 rows over both CTAs' tensor memory) (+)= A (128 rows in each CTA) * B^T (N / 2 rows of B
+// in each CTA), issued by the leader.
+KD_DEVICE void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+KD_DEVICE void mma_f8_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+}
+// Arrives on the barrier at `bar`'s offset in both CTAs of the pair once the leader's earlier MMAs have completed.
+KD_DEVICE void mma_commit_pair(uint64_t* bar) {
+  const uint16_t both = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+      ::"r"(smem_u32(bar)), "h"(both)
+      : "memory");
+}
+
 KD_DEVICE void mma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
                : "memory");

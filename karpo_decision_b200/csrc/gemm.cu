@@ -24,10 +24,7 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int ROW_BYTES = 128;  // one swizzle row per operand row per stage
-constexpr int STAGES = 4;
 constexpr int A_STAGE_BYTES = BM * ROW_BYTES;  // 16 KB
-constexpr int B_STAGE_BYTES = BN * ROW_BYTES;  // 32 KB
-constexpr int STAGE_BYTES = A_STAGE_BYTES + B_STAGE_BYTES;
 constexpr int TMEM_COLS = 512;  // two 128 x 256 fp32 accumulators
 constexpr int EPI_GROUPS = 2;  // epilogue warpgroups, each taking half of a tile's columns
 constexpr int THREADS = 64 + EPI_GROUPS * 128;
@@ -35,8 +32,22 @@ constexpr int THREADS = 64 + EPI_GROUPS * 128;
 constexpr int OUT_BOX_COLS = 64;
 constexpr int OUT_BOX_BYTES = 32 * OUT_BOX_COLS * 2;
 constexpr int NORM_BYTES = 2 * 256 * 2;  // the QKV epilogue's q and k norm weights (bf16, head_dim <= 256)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_GROUPS * 4 * OUT_BOX_BYTES + NORM_BYTES +
-                           1024 /* alignment slack */ + 256 /* barriers */;
+
+// The pipeline of one CTA. Single: a 128 x 256 tile per CTA, A (128 rows) and B (256 rows) per stage. Pair (a
+// cluster of two CTAs, one cta_group::2 MMA over 256 x 256): each CTA stages its 128 rows of A and its 128 rows of B,
+// so a stage is a third smaller and the ring one deeper per byte; the leader issues the MMA over both CTAs' stages.
+template <bool PAIR>
+struct Pipe {
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;
+  static constexpr int STAGE_BYTES = A_STAGE_BYTES + B_ROWS * ROW_BYTES;
+  static constexpr int STAGES = PAIR ? 6 : 4;
+  static constexpr int TILE_M = PAIR ? 2 * BM : BM;  // output rows of one (cluster) tile
+  static constexpr int SMEM = STAGES * STAGE_BYTES + EPI_GROUPS * 4 * OUT_BOX_BYTES + NORM_BYTES +
+                              1024 /* alignment slack */ + 256 /* barriers */;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+// Pack sizes from which the CTA-pair kernel runs (below, the single-CTA one: the pair's second half would idle).
+constexpr int PAIR_MIN_ROWS = 256;
 
 // The fused attention-input epilogue (KD_EPI_QKV): the projection's columns are [q heads][k heads][v heads] (Qwen's
 // gated queries: [q_h | gate_h] per head); each output row's heads are normalized, rotated and scattered to q, k, v
@@ -259,12 +270,15 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
   }
 }
 
-template <int EPI, bool FP8>
+template <int EPI, bool FP8, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
                 const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r, Args args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  using P = Pipe<PAIR>;
+  constexpr int STAGES = P::STAGES;
+  constexpr int STAGE_BYTES = P::STAGE_BYTES;
   uint8_t* out_stage = smem + STAGES * STAGE_BYTES;  // epilogue warp e's box at e * OUT_BOX_BYTES
   __nv_bfloat16* norm_s = reinterpret_cast<__nv_bfloat16*>(out_stage + EPI_GROUPS * 4 * OUT_BOX_BYTES);
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(out_stage + EPI_GROUPS * 4 * OUT_BOX_BYTES + NORM_BYTES);
@@ -283,7 +297,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 
   const int warp = threadIdx.x / 32;
-  const int m_tiles = (args.M + BM - 1) / BM;
+  const uint32_t rank = PAIR ? cluster_rank() : 0;  // this CTA's half of a pair tile: rows rank * 128 ..
+  const bool leader = rank == 0;
+  const int first_tile = PAIR ? (int)blockIdx.x / 2 : (int)blockIdx.x;
+  const int tile_step = PAIR ? (int)gridDim.x / 2 : (int)gridDim.x;
+  const int m_tiles = (args.M + P::TILE_M - 1) / P::TILE_M;
   const int n_tiles = (args.N + BN - 1) / BN;
   const int num_tiles = m_tiles * n_tiles;
   const int elems_per_row = FP8 ? ROW_BYTES : ROW_BYTES / 2;  // BK in elements
@@ -296,7 +314,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
-      mbar_init(&acc_empty[b], EPI_GROUPS * 128);
+      // single: every epilogue thread arrives; pair: one arrival per epilogue warp of both CTAs, on the leader's
+      mbar_init(&acc_empty[b], PAIR ? 2 * EPI_GROUPS * 4 : EPI_GROUPS * 128);
     }
     for (int e = 0; e < EPI_GROUPS * 4; ++e) mbar_init(&res_bar[e], 1);
     fence_barrier_init();
@@ -304,11 +323,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&map_b);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(tmem_slot, TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // both CTAs' barriers initialized before either signals the other's
+  else
+    __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -317,16 +344,23 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (elect_one()) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-        const int m0 = (tile / n_tiles) * BM;
+      for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+        const int m0 = (tile / n_tiles) * P::TILE_M;
         const int n0 = (tile % n_tiles) * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status)) goto done;
           uint8_t* sa = smem + stage * STAGE_BYTES;
           uint8_t* sb = sa + A_STAGE_BYTES;
-          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
-          tma_load_2d(&map_a, &full_bar[stage], sa, kb * elems_per_row, m0);
-          tma_load_2d(&map_b, &full_bar[stage], sb, kb * elems_per_row, n0);
+          if constexpr (PAIR) {
+            // both CTAs' halves land on the leader's full barrier, which expects the bytes of both
+            if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
+            tma_load_2d_pair(&map_a, &full_bar[stage], sa, kb * elems_per_row, m0 + (int)rank * BM);
+            tma_load_2d_pair(&map_b, &full_bar[stage], sb, kb * elems_per_row, n0 + (int)rank * P::B_ROWS);
+          } else {
+            mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+            tma_load_2d(&map_a, &full_bar[stage], sa, kb * elems_per_row, m0);
+            tma_load_2d(&map_b, &full_bar[stage], sb, kb * elems_per_row, n0);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -336,13 +370,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    constexpr uint32_t idesc = mma_idesc(FP8 ? 0u : 1u, BM, BN);
-    if (elect_one()) {
+    constexpr uint32_t idesc = mma_idesc(FP8 ? 0u : 1u, P::TILE_M, BN);
+    if (leader && elect_one()) {  // pair: the leader issues the MMA for both CTAs
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
         if (!mbar_wait(&acc_empty[acc], acc_phase ^ 1, args.status)) goto done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
@@ -355,18 +389,33 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int k = 0; k < ROW_BYTES / 32; ++k) {  // 32 bytes of K per instruction (16 bf16 or 32 e4m3)
             const uint64_t da = sw128_kmajor_desc(sa + 32 * k);
             const uint64_t db = sw128_kmajor_desc(sb + 32 * k);
-            if constexpr (FP8)
-              mma_f8_ss(d_tmem, da, db, idesc, (kb | k) != 0);
-            else
-              mma_f16_ss(d_tmem, da, db, idesc, (kb | k) != 0);
+            if constexpr (PAIR) {
+              if constexpr (FP8)
+                mma_f8_ss_pair(d_tmem, da, db, idesc, (kb | k) != 0);
+              else
+                mma_f16_ss_pair(d_tmem, da, db, idesc, (kb | k) != 0);
+            } else {
+              if constexpr (FP8)
+                mma_f8_ss(d_tmem, da, db, idesc, (kb | k) != 0);
+              else
+                mma_f16_ss(d_tmem, da, db, idesc, (kb | k) != 0);
+            }
           }
-          mma_commit(&empty_bar[stage]);  // the stage is free once these MMAs have read it
+          // the stage is free once these MMAs have read it (pair: in both CTAs)
+          if constexpr (PAIR)
+            mma_commit_pair(&empty_bar[stage]);
+          else
+            mma_commit(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
           }
         }
-        mma_commit(&acc_full[acc]);  // the accumulator is complete once every MMA above has finished
+        // the accumulator is complete once every MMA above has finished (pair: both CTAs' halves)
+        if constexpr (PAIR)
+          mma_commit_pair(&acc_full[acc]);
+        else
+          mma_commit(&acc_full[acc]);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -383,8 +432,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t res_phase = 0;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      const int m0 = (tile / n_tiles) * BM;
+    for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
+      const int m0 = (tile / n_tiles) * P::TILE_M + (int)rank * BM;  // this CTA's 128 rows of the tile
       const int n0 = (tile % n_tiles) * BN;
       if (!mbar_wait(&acc_full[acc], acc_phase, args.status)) goto done;
       tc_fence_after();
@@ -487,7 +536,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
       }
       tc_fence_before();
-      mbar_arrive(&acc_empty[acc]);
+      if constexpr (PAIR) {  // one arrival per warp, on the leader's barrier
+        __syncwarp();
+        if (lane == 0) mbar_arrive_leader(&acc_empty[acc]);
+      } else {
+        mbar_arrive(&acc_empty[acc]);
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
@@ -497,32 +551,58 @@ __global__ void __launch_bounds__(THREADS, 1)
 done:
   bulk_wait();  // the epilogue's TMA stores have completed (no-op for threads that issued none) before the CTA exits
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // neither CTA leaves while the other may still signal its barriers or use the pair's TMEM
+  else
+    __syncthreads();
   tc_fence_after();
   if (warp == 1) {
     __syncwarp();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else
+      tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
-template <int EPI, bool FP8>
+template <int EPI, bool FP8, bool PAIR>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
            const Args& args, cudaStream_t stream) {
-  auto kernel = gemm_kernel<EPI, FP8>;
+  using P = Pipe<PAIR>;
+  auto kernel = gemm_kernel<EPI, FP8, PAIR>;
   static bool configured[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) return KD_ERR_ARGUMENT;
   if (!configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P::SMEM);
     if (e != cudaSuccess) return record_cuda_error(e, "gemm: cudaFuncSetAttribute");
     configured[dev] = true;
   }
-  const int m_tiles = (args.M + BM - 1) / BM;
+  const int m_tiles = (args.M + P::TILE_M - 1) / P::TILE_M;
   const int n_tiles = (args.N + BN - 1) / BN;
   const int tiles = m_tiles * n_tiles;
-  const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-  kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(ma, mb, mc, mr, args);
+  if constexpr (!PAIR) {
+    const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
+    kernel<<<grid, THREADS, P::SMEM, stream>>>(ma, mb, mc, mr, args);
+  } else {
+    const int pairs = num_sms(dev) / 2;
+    const int grid = 2 * (tiles < pairs ? tiles : pairs);
+    cudaLaunchConfig_t config = {};
+    config.gridDim = dim3((unsigned)grid);
+    config.blockDim = dim3(THREADS);
+    config.dynamicSmemBytes = P::SMEM;
+    config.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    config.attrs = attr;
+    config.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&config, kernel, ma, mb, mc, mr, args);
+    if (e != cudaSuccess) return record_cuda_error(e, "gemm: cluster launch");
+  }
   return record_cuda_error(cudaGetLastError(), "gemm: launch");
 }
 
@@ -557,7 +637,8 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
   const uint32_t box_k = gemm::ROW_BYTES / esize;
   int rc = make_tma_2d(&ma, A, dt, esize, K, M, lda, box_k, gemm::BM, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_tma_2d(&mb, B, dt, esize, K, N, ldb, box_k, gemm::BN, CU_TENSOR_MAP_SWIZZLE_128B);
+  const bool pair = M >= gemm::PAIR_MIN_ROWS;  // pair: each CTA of a pair stages half of a tile's B rows
+  rc = make_tma_2d(&mb, B, dt, esize, K, N, ldb, box_k, pair ? gemm::BN / 2 : gemm::BN, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
 
   gemm::Args args;
@@ -583,10 +664,13 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
-#define KD_GEMM_CASE(E)                                                         \
-  case E:                                                                       \
-    return fp8 ? gemm::launch<E, true>(ma, mb, mc, mr, args, stream)            \
-               : gemm::launch<E, false>(ma, mb, mc, mr, args, stream);
+#define KD_GEMM_CASE(E)                                                                                \
+  case E:                                                                                              \
+    if (pair)                                                                                          \
+      return fp8 ? gemm::launch<E, true, true>(ma, mb, mc, mr, args, stream)                           \
+                 : gemm::launch<E, false, true>(ma, mb, mc, mr, args, stream);                         \
+    return fp8 ? gemm::launch<E, true, false>(ma, mb, mc, mr, args, stream)                            \
+               : gemm::launch<E, false, false>(ma, mb, mc, mr, args, stream);
   switch (epilogue) {
     KD_GEMM_CASE(KD_EPI_STORE)
     KD_GEMM_CASE(KD_EPI_RESIDUAL)
