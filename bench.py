@@ -63,7 +63,13 @@ def workload(config: str, seed: int, tokens: int = 0) -> dict:
     tokens = tokens or default
     spec = CONFIGS[config]
     lengths = synthetic_lengths(tokens, low, high, seed, log_uniform=log)
-    return synthetic_pack_arrays(lengths, spec.vocab, seed + 1, (1, 4))
+    return synthetic_pack_arrays(lengths, spec.vocab, seed + 1, markers_per(spec))
+
+
+def markers_per(spec) -> tuple[int, int]:
+    """Readout markers per sequence: 1-4 (Qwen's joint layouts, tests/gpu/test_packed_qwen.py:52-60); Gemma reads
+    out one marker per block, at its last token (families/gemma/packed.py:136-143)."""
+    return (1, 4) if spec.family == "qwen" else (1, 1)
 
 
 def dist_env() -> tuple[int, int, int]:
@@ -91,7 +97,7 @@ def cpu_sample_rate(config: str, seconds: float, fp8: bool = False) -> dict:
     seed = 100
     while elapsed < seconds or packs == 0:
         lengths = synthetic_lengths(256, 32, 256, seed, log_uniform=True)
-        arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, (1, 4))
+        arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, markers_per(spec))
         start = time.perf_counter()
         hidden = forward(weights, spec.as_dict(), arrays, mode="fp32", fp8=fp8)
         oracle.readout(hidden, weights["readout"], spec.logit_cap)
@@ -138,8 +144,11 @@ def run_reference(args: argparse.Namespace) -> None:
 def config_block(args: argparse.Namespace, world: int) -> dict:
     tokens, (low, high), log = WORKLOADS[args.config]
     tokens = args.tokens or tokens
+    from karpo_decision_b200.synthetic import CONFIGS
+
+    lo, hi = markers_per(CONFIGS[args.config])
     return {"workload": f"{args.config} packed prefill, packs of {tokens} tokens, lengths "
-                        f"{'log-uniform' if log else 'uniform'} [{low},{high}], 1-4 markers/sequence, causal"
+                        f"{'log-uniform' if log else 'uniform'} [{low},{high}], {lo}-{hi} markers/sequence, causal"
                         + (", FP8 projections" if args.fp8 else ""),
             "tokens_per_pack": tokens, "parallelism": f"replicas x{world}",
             "path": "graphs" if getattr(args, "graphs", False) else "plain",
@@ -365,7 +374,7 @@ def request_latency(model, head, args, dev, n: int) -> dict:
     requests = []
     for i in range(n):
         length = synthetic_lengths(high, low, high, seed=int(rng.integers(1 << 30)), log_uniform=log)[0]
-        requests.append(synthetic_pack_arrays([length], spec.vocab, seed=i, markers_per_seq=(1, 4)))
+        requests.append(synthetic_pack_arrays([length], spec.vocab, seed=i, markers_per_seq=markers_per(spec)))
     longest = max(len(r["input_ids"]) for r in requests)
     buckets = tuple(1 << k for k in range(7, max(8, int(np.ceil(np.log2(longest)))) + 1))
     graphs = Graphs(model, buckets=buckets, max_sequences=1)

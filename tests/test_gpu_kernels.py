@@ -26,9 +26,11 @@ def rng(seed=0):
 # ------------------------------------------------------------------------------------------------ GEMM
 
 
-@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (128, 256, 64), (300, 768, 256), (1000, 1024, 1024),
-                                   (513, 6144, 1024), (77, 96, 200), (4096, 2560, 2560)])
+@pytest.mark.parametrize("m,n,k", [(1, 256, 64), (128, 256, 64), (255, 256, 64), (256, 256, 64), (257, 512, 128),
+                                   (300, 768, 256), (1000, 1024, 1024), (513, 6144, 1024), (77, 96, 200),
+                                   (4096, 2560, 2560), (384, 32, 64)])
 def test_gemm_bf16_matches_fp32(m, n, k):
+    """Single-CTA tiles below 256 rows, CTA pairs from 256 (a pair's second half partly or wholly past M)."""
     g = rng(m + n + k)
     a = bf16(g.standard_normal((m, k)))
     w = bf16(g.standard_normal((n, k)) * 0.05)
