@@ -7,7 +7,7 @@
 //
 // The delta rule here is the recurrent form: one CTA per (sequence, value head) holds the head's state S (dk x dv,
 // float32) in registers, two threads per value column each owning half of its dk rows, and walks the sequence token
-// by token. Queries and keys are L2-normalized (the reference's use_qk_l2norm_in_kernel), per chunk of tokens staged
+// by token (the next rows fetched while it walks); CTAs take the longest sequences first. Queries and keys are L2-normalized (the reference's use_qk_l2norm_in_kernel), per chunk of tokens staged
 // in shared memory by the CTA's warps before the sequential walk.
 #include "common.cuh"
 #include "kd_internal.h"
@@ -106,12 +106,15 @@ __global__ void conv_silu_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld
 // ------------------------------------------------------------------------------------------------ delta rule
 
 constexpr int CHUNK = 16;  // tokens staged in shared memory per step of the walk
+constexpr int ORDER_MAX = 1024;  // packs of up to this many sequences walk their longest sequences first
 
 template <int DK, int DV>
 struct Cfg {
-  static constexpr int THREADS = 2 * DV;  // two threads per value column
-  static constexpr int ROWS = DK / 2;     // state rows per thread
-  static constexpr int KSTRIDE = DK + 4;  // staged q / k row (the second half 16 bytes further: no bank conflict)
+  static constexpr int TPC = 2;           // threads per value column, each owning DK / TPC of its rows
+  static constexpr int THREADS = TPC * DV;
+  static constexpr int ROWS = DK / TPC;   // state rows per thread
+  static constexpr int SEG = ROWS + 4;    // a staged q / k row: TPC segments 16 bytes apart (no bank conflicts)
+  static constexpr int KSTRIDE = TPC * SEG;
   // shared memory: q and k rows (float32), v rows (float32), then g and beta
   static constexpr int SMEM = (2 * CHUNK * KSTRIDE + CHUNK * DV + 2 * CHUNK) * 4;
 };
@@ -124,6 +127,7 @@ struct Args {
   const __nv_bfloat16* a_log;
   const __nv_bfloat16* dt_bias;
   const int32_t* cu;
+  int num_seqs;
   int nk, nv;
   __nv_bfloat16* out;
   int64_t ldo;
@@ -132,6 +136,14 @@ struct Args {
 KD_DEVICE float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// The sum over the TPC adjacent lanes that share a value column.
+template <int TPC>
+KD_DEVICE float column_sum(float v) {
+#pragma unroll
+  for (int o = 1; o < TPC; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
 
@@ -146,13 +158,31 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
   float* v_s = k_s + CHUNK * C::KSTRIDE;        // [CHUNK][DV]
   float* g_s = v_s + CHUNK * DV;                // [CHUNK]: decay factor exp(g)
   float* b_s = g_s + CHUNK;                     // [CHUNK]: beta
-  const int seq = blockIdx.x;
-  const int head = blockIdx.y;                  // value head
+  // Longest sequences first: CTA b takes value head b % Hv of the (b / Hv)-th longest sequence, so the long walks
+  // start in the first wave and the short ones fill in behind them. The order is computed here from the device
+  // bounds (every CTA the same way; packs of more than ORDER_MAX sequences keep their order).
+  __shared__ int order_s[ORDER_MAX];
+  const int rank = blockIdx.x / a.nv;
+  const int head = blockIdx.x % a.nv;           // value head
+  int seq = rank;
+  if (a.num_seqs <= ORDER_MAX) {
+    for (int s0 = threadIdx.x; s0 < a.num_seqs; s0 += blockDim.x) {
+      const int len = a.cu[s0 + 1] - a.cu[s0];
+      int before = 0;
+      for (int s1 = 0; s1 < a.num_seqs; ++s1) {
+        const int l1 = a.cu[s1 + 1] - a.cu[s1];
+        before += (l1 > len) || (l1 == len && s1 < s0);
+      }
+      order_s[before] = s0;
+    }
+    __syncthreads();
+    seq = order_s[rank];
+  }
   const int khead = head / (a.nv / a.nk);       // its key head (repeat_interleave)
   const int64_t t0 = a.cu[seq], t1 = a.cu[seq + 1];
   const int tid = threadIdx.x;
-  const int col = tid >> 1;                     // value column
-  const int half = tid & 1;                     // rows [half * ROWS, half * ROWS + ROWS)
+  const int col = tid / C::TPC;                 // value column
+  const int part = tid % C::TPC;                // rows [part * ROWS, part * ROWS + ROWS)
   const int warp = tid / 32, lane = tid & 31;
   constexpr int WARPS = C::THREADS / 32;
   const float qscale = rsqrtf((float)DK);
@@ -160,23 +190,50 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
   const float dt_bias = __bfloat162float(a.dt_bias[head]);
   const int64_t kd = (int64_t)a.nk * DK;
 
-  float S[C::ROWS];
+  float S[C::ROWS];  // this thread's rows of its column of S / gamma
 #pragma unroll
   for (int i = 0; i < C::ROWS; ++i) S[i] = 0.f;
+  float gamma = 1.f;
 
+  // The next chunk's rows are fetched into registers while the current chunk is walked, then normalized into
+  // shared memory: one warp per token row (q and k L2-normalized with eps 1e-6, q scaled by dk^-1/2).
+  constexpr int PER_WARP = CHUNK / WARPS;
+  static_assert(CHUNK % WARPS == 0, "whole rows per warp");
+  __nv_bfloat16 rq[PER_WARP][DK / 32], rk[PER_WARP][DK / 32], rv[PER_WARP][DV / 32];
+  float ra[PER_WARP], rb[PER_WARP];
+  auto fetch = [&](int64_t base, int cnt) {
+#pragma unroll
+    for (int i = 0; i < PER_WARP; ++i) {
+      const int r = warp + i * WARPS;
+      if (r >= cnt) break;
+      const __nv_bfloat16* row = a.qkv + (base + r) * a.ldqkv;
+#pragma unroll
+      for (int e = 0; e < DK / 32; ++e) {
+        rq[i][e] = row[(int64_t)khead * DK + lane + 32 * e];
+        rk[i][e] = row[kd + (int64_t)khead * DK + lane + 32 * e];
+      }
+#pragma unroll
+      for (int e = 0; e < DV / 32; ++e) rv[i][e] = row[2 * kd + (int64_t)head * DV + lane + 32 * e];
+      if (lane == 0) {
+        const __nv_bfloat16* abr = a.ab + (base + r) * a.ldab;
+        rb[i] = __bfloat162float(abr[head]);
+        ra[i] = __bfloat162float(abr[a.nv + head]);
+      }
+    }
+  };
+  if (t1 > t0) fetch(t0, t1 - t0 < CHUNK ? (int)(t1 - t0) : CHUNK);
   for (int64_t c0 = t0; c0 < t1; c0 += CHUNK) {
     const int n = t1 - c0 < CHUNK ? (int)(t1 - c0) : CHUNK;
     __syncthreads();  // the previous chunk's rows have been read
-    // stage: one warp per token row at a time; q and k L2-normalized (eps 1e-6), q scaled by dk^-1/2
-    for (int r = warp; r < n; r += WARPS) {
-      const __nv_bfloat16* row = a.qkv + (c0 + r) * a.ldqkv;
-      const __nv_bfloat16* qr = row + (int64_t)khead * DK;
-      const __nv_bfloat16* kr = row + kd + (int64_t)khead * DK;
+#pragma unroll
+    for (int i = 0; i < PER_WARP; ++i) {
+      const int r = warp + i * WARPS;
+      if (r >= n) break;
       float qv[DK / 32], kv[DK / 32], sq = 0.f, sk = 0.f;
 #pragma unroll
       for (int e = 0; e < DK / 32; ++e) {
-        qv[e] = __bfloat162float(qr[lane + 32 * e]);
-        kv[e] = __bfloat162float(kr[lane + 32 * e]);
+        qv[e] = __bfloat162float(rq[i][e]);
+        kv[e] = __bfloat162float(rk[i][e]);
         sq += qv[e] * qv[e];
         sk += kv[e] * kv[e];
       }
@@ -185,56 +242,65 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
 #pragma unroll
       for (int e = 0; e < DK / 32; ++e) {
         const int d = lane + 32 * e;
-        const int at = d < C::ROWS ? d : d + 4;  // the second half of a staged row sits 16 bytes further
+        const int at = (d / C::ROWS) * C::SEG + d % C::ROWS;  // each thread's segment sits 16 bytes further
         q_s[r * C::KSTRIDE + at] = qv[e] * iq;
         k_s[r * C::KSTRIDE + at] = kv[e] * ik;
       }
-      const __nv_bfloat16* vr = row + 2 * kd + (int64_t)head * DV;
 #pragma unroll
-      for (int e = 0; e < DV / 32; ++e) v_s[r * DV + lane + 32 * e] = __bfloat162float(vr[lane + 32 * e]);
+      for (int e = 0; e < DV / 32; ++e) v_s[r * DV + lane + 32 * e] = __bfloat162float(rv[i][e]);
       if (lane == 0) {
-        const __nv_bfloat16* abr = a.ab + (c0 + r) * a.ldab;
-        const float b = __bfloat162float(abr[head]);
-        const float av = __bfloat162float(abr[a.nv + head]);
-        g_s[r] = expf(decay_a * softplus(av + dt_bias));               // exp(g), g = -exp(A_log) softplus(a + dt)
-        b_s[r] = bf16_round(1.0f / (1.0f + expf(-b)));                 // beta = sigmoid(b), a bf16 tensor op
+        g_s[r] = expf(decay_a * softplus(ra[i] + dt_bias));            // exp(g), g = -exp(A_log) softplus(a + dt)
+        b_s[r] = bf16_round(1.0f / (1.0f + expf(-rb[i])));             // beta = sigmoid(b), a bf16 tensor op
       }
     }
     __syncthreads();
-    // the walk: S = alpha S + k d^T with d = (v - alpha S^T k) beta, then o = S^T q
+    if (c0 + CHUNK < t1) fetch(c0 + CHUNK, t1 - c0 - CHUNK < CHUNK ? (int)(t1 - c0 - CHUNK) : CHUNK);
+    // the walk: S = alpha S + k d^T with d = (v - alpha S^T k) beta, then o = S^T q. The decay stays factored out:
+    // the registers hold S / gamma with gamma the product of the decays since the last renormalization, folded back
+    // into the registers when it falls below 2^-60 (so 1 / gamma stays far from overflow), which saves the per-element
+    // multiply by alpha at every token.
     for (int r = 0; r < n; ++r) {
-      const float* kr = k_s + r * C::KSTRIDE + half * (C::ROWS + 4);
-      const float* qr = q_s + r * C::KSTRIDE + half * (C::ROWS + 4);
-      const float alpha = g_s[r], beta = b_s[r];
+      const float* kr = k_s + r * C::KSTRIDE + part * C::SEG;
+      const float* qr = q_s + r * C::KSTRIDE + part * C::SEG;
+      const float beta = b_s[r];
+      gamma *= g_s[r];
+      if (gamma < 0x1p-60f) {  // uniform over the CTA (one decay per head and token)
+#pragma unroll
+        for (int i = 0; i < C::ROWS; ++i) S[i] *= gamma;
+        gamma = 1.f;
+      }
+      float kreg[C::ROWS];
       float acc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < C::ROWS; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
+        kreg[i] = k4.x;
+        kreg[i + 1] = k4.y;
+        kreg[i + 2] = k4.z;
+        kreg[i + 3] = k4.w;
         acc[0] = fmaf(S[i], k4.x, acc[0]);
         acc[1] = fmaf(S[i + 1], k4.y, acc[1]);
         acc[2] = fmaf(S[i + 2], k4.z, acc[2]);
         acc[3] = fmaf(S[i + 3], k4.w, acc[3]);
       }
-      float kvm = (acc[0] + acc[1]) + (acc[2] + acc[3]);
-      kvm += __shfl_xor_sync(0xffffffffu, kvm, 1);
-      const float delta = (v_s[r * DV + col] - alpha * kvm) * beta;
+      const float kvm = column_sum<C::TPC>((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      const float delta = (v_s[r * DV + col] - gamma * kvm) * beta;  // S^T k of the decayed state = gamma (S/gamma)^T k
+      const float dscaled = delta / gamma;
       float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < C::ROWS; i += 4) {
-        const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
         const float4 q4 = *reinterpret_cast<const float4*>(qr + i);
-        S[i] = fmaf(k4.x, delta, S[i] * alpha);
-        S[i + 1] = fmaf(k4.y, delta, S[i + 1] * alpha);
-        S[i + 2] = fmaf(k4.z, delta, S[i + 2] * alpha);
-        S[i + 3] = fmaf(k4.w, delta, S[i + 3] * alpha);
+        S[i] = fmaf(kreg[i], dscaled, S[i]);
+        S[i + 1] = fmaf(kreg[i + 1], dscaled, S[i + 1]);
+        S[i + 2] = fmaf(kreg[i + 2], dscaled, S[i + 2]);
+        S[i + 3] = fmaf(kreg[i + 3], dscaled, S[i + 3]);
         o[0] = fmaf(S[i], q4.x, o[0]);
         o[1] = fmaf(S[i + 1], q4.y, o[1]);
         o[2] = fmaf(S[i + 2], q4.z, o[2]);
         o[3] = fmaf(S[i + 3], q4.w, o[3]);
       }
-      float ov = (o[0] + o[1]) + (o[2] + o[3]);
-      ov += __shfl_xor_sync(0xffffffffu, ov, 1);
-      if (half == 0) a.out[(c0 + r) * a.ldo + (int64_t)head * DV + col] = __float2bfloat16_rn(ov);
+      const float ov = column_sum<C::TPC>((o[0] + o[1]) + (o[2] + o[3]));
+      if (part == 0) a.out[(c0 + r) * a.ldo + (int64_t)head * DV + col] = __float2bfloat16_rn(gamma * ov);
     }
   }
 }
@@ -254,7 +320,7 @@ int launch_delta(const Args& a, int num_seqs, cudaStream_t stream) {
       configured[dev] = true;
     }
   }
-  dim3 grid((unsigned)num_seqs, (unsigned)a.nv);
+  dim3 grid((unsigned)(num_seqs * a.nv));
   kernel<<<grid, C::THREADS, C::SMEM, stream>>>(a);
   return record_cuda_error(cudaGetLastError(), "gated_delta_rule: launch");
 }
@@ -341,6 +407,7 @@ extern "C" int kd_gated_delta_rule(const void* qkv, int64_t ldqkv, const void* a
   a.a_log = static_cast<const __nv_bfloat16*>(a_log);
   a.dt_bias = static_cast<const __nv_bfloat16*>(dt_bias);
   a.cu = cu;
+  a.num_seqs = num_seqs;
   a.nk = num_k_heads;
   a.nv = num_v_heads;
   a.out = static_cast<__nv_bfloat16*>(out);

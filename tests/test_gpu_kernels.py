@@ -69,9 +69,11 @@ def test_gemm_gated_epilogues(epilogue):
     assert (got - want).abs().max().item() <= 2 ** -7 * want.abs().max().item() + 1e-3
 
 
-def test_gemm_fp8_matches_dequantized_product():
+@pytest.mark.parametrize("m", [100, 517])
+def test_gemm_fp8_matches_dequantized_product(m):
+    """Single-CTA tiles (100 rows) and CTA pairs (517 rows)."""
     g = rng(3)
-    m, n, k = 517, 1024, 768
+    n, k = 1024, 768
     a = bf16(g.standard_normal((m, k)))
     w = bf16(g.standard_normal((n, k)) * 0.05)
     qa, sa = ops.quantize_rows_e4m3(a)
