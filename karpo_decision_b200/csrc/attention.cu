@@ -78,6 +78,29 @@ KD_DEVICE float fast_exp2(float x) {
   return y;
 }
 
+// Paired float32 arithmetic (sm_100 f32x2 instructions: one issue slot for two lanes' worth of values).
+KD_DEVICE float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
+        "l"(*reinterpret_cast<uint64_t*>(&c)));
+  return *reinterpret_cast<float2*>(&d);
+}
+KD_DEVICE float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
+  return *reinterpret_cast<float2*>(&d);
+}
+// max(a, b, c) in one instruction.
+KD_DEVICE float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
 template <int HD, int DV>
 __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
@@ -276,9 +299,8 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
 #pragma unroll
       for (int e = 0; e < 8; ++e) mx[e] = sv[e];
 #pragma unroll
-      for (int e = 8; e < BN; ++e) mx[e & 7] = fmaxf(mx[e & 7], sv[e]);
-      const float mraw = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int e = 8; e < BN; e += 2) mx[(e / 2) & 7] = max3(mx[(e / 2) & 7], sv[e], sv[e + 1]);
+      const float mraw = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       const float mt = mraw * a.scale_log2;  // the scale is positive: max commutes with it
       const float m_new = fmaxf(m_used, mt);
       const bool need = m_new > m_used + RESCALE_THRESHOLD || (m_used == -INFINITY && m_new != -INFINITY);
@@ -304,20 +326,23 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         m_used = m_new;
       }
       const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
-      float part[4] = {0.f, 0.f, 0.f, 0.f};  // the row sum over independent chains
+      float2 part[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // the row sum over independent chains
+      const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
+      const float2 base2 = make_float2(neg_base, neg_base);
 #pragma unroll
       for (int c = 0; c < BN; c += 64) {
         uint32_t pk[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
-          const float p0 = fast_exp2(fmaf(sv[c + 2 * e], a.scale_log2, neg_base));
-          const float p1 = fast_exp2(fmaf(sv[c + 2 * e + 1], a.scale_log2, neg_base));
-          part[e & 3] += p0 + p1;
-          pk[e] = pack_bf16x2(p0, p1);
+          const float2 x = fma2(make_float2(sv[c + 2 * e], sv[c + 2 * e + 1]), scale2, base2);
+          const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+          part[e & 3] = add2(part[e & 3], p);
+          pk[e] = pack_bf16x2(p.x, p.y);
         }
         tmem_st32(s_addr + c / 2, pk);  // P_j over the score columns this thread has already read
       }
-      l_sum += (part[0] + part[1]) + (part[2] + part[3]);
+      const float2 ps = add2(add2(part[0], part[1]), add2(part[2], part[3]));
+      l_sum += ps.x + ps.y;
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(&p_full[j & 1]);
