@@ -161,12 +161,14 @@ int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* s
  * (read when the kernel runs); q holds total_q rows and k/v total_k rows. max_q bounds every Lq. When gate != NULL,
  * out = bf16(bf16(o) * sigmoid(gate))
  * (Qwen's output gate, families/qwen/fused.py:38-39). head_dim 64, 128, 256 or 512 (Gemma 4's global layers,
- * families/gemma/global_attention.py: two 256-wide value slices per head, each CTA forming the full scores). */
+ * families/gemma/global_attention.py: two 256-wide value slices per head, each CTA forming the full scores).
+ * sched: two ints of device scratch for the persistent CTAs' work counter, zero before the first launch and left
+ * zero by every launch; launches that may run at the same time need separate pairs. */
 int kd_attention_varlen(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v, int64_t ldv, void* out,
                         int64_t ldo, const void* gate, int64_t ldg, const int32_t* cu_q, const int32_t* cu_k,
                         int num_seqs, int max_q, int64_t total_q, int64_t total_k, int num_heads_q,
                         int num_heads_kv, int head_dim, float scale, int window_left, int window_right, int* status,
-                        cudaStream_t stream);
+                        int* sched, cudaStream_t stream);
 
 /* dst[i, :] = src[rows[i], :] for n bf16 rows of `width` elements (width % 8 == 0): the key and value rows of a
  * branched block layout's virtual sequences (the shared block, or its last window - 1 rows, then the branch).

@@ -41,7 +41,7 @@ SIGNATURES: dict[str, list] = {
     "kd_qkv_norm_rope": [P, c_int64, c_int64, P, c_int, c_int, c_int, c_int, P, P, c_int, c_int, c_float, P, P,
                          c_int, P, P, P, P, P],
     "kd_attention_varlen": [P, c_int64, P, c_int64, P, c_int64, P, c_int64, P, c_int64, P, P, c_int, c_int, c_int64,
-                            c_int64, c_int, c_int, c_int, c_float, c_int, c_int, P, P],
+                            c_int64, c_int, c_int, c_int, c_float, c_int, c_int, P, P, P],
     "kd_gather_rows": [P, c_int64, P, c_int64, c_int, P, c_int64, P],
     "kd_scatter_rows": [P, c_int64, P, c_int64, c_int, P, c_int64, P],
     "kd_conv_silu": [P, c_int64, c_int64, c_int, P, c_int, P, P, c_int64, P],

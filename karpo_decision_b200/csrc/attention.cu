@@ -10,17 +10,24 @@
 // Sequence boundaries are read from device memory when the kernel runs, so a captured graph serves any pack
 // composition with the same token count.
 //
-// One CTA per (128-query tile of one sequence, query head, value slice), two CTAs per SM where memory allows (head
-// dim <= 128). Head dim 512 (Gemma 4's global layers) exceeds tensor memory for a whole output row block next to the
-// scores, so its output is computed in two 256-wide value slices by separate CTAs, each forming the full scores
-// (K and V single-buffered to fit the 128 KB query tile). 6 warps:
-//   warp 0      TMA producer: the Q tile once, then K and V tiles through a ring (2 stages; 1 for head dim 512);
+// Persistent CTAs, as many as fit on the device (two per SM for head dim <= 128), take work items: a 128-query tile of
+// one sequence for one query head (and value slice). Each CTA's first item is its index; the rest come from a
+// device counter that the last CTA to finish returns to zero. Items are ordered sequence by sequence, each
+// sequence's tiles from the last (the most expensive when causal) to the first, query heads innermost, so the heads
+// of one key/value group run at about the same time and share the key/value reads in L2. Head dim 512 (Gemma 4's
+// global layers) exceeds tensor memory for a whole output row block next to the scores, so its output is computed in
+// two 256-wide value slices (separate items), each forming the full scores (K and V single-buffered to fit the
+// 128 KB query tile). 6 warps:
+//   warp 0      work fetch + TMA producer: publishes each item to the other roles through a two-slot ring, then its
+//               Q tile and its K and V tiles through a ring (2 stages; 1 for head dim 512) counted across items;
 //   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers, then O += P_j V_j with
 //               P_j read from TMEM (A operand, written over S_j) and V_j as an MN-major B operand from shared memory;
+//               an item's first S can run while the previous item's epilogue reads O;
 //   warps 2..5  softmax, one query row per thread (its TMEM lane): scores -> masked, scaled, exp2 against a running
 //               maximum, bf16 probabilities stored back to TMEM. O is rescaled only when the row maximum grows by
 //               more than 2^8 (the exponent base stays stale otherwise, which is exact: O and the row sum share it);
-//               at the end they normalize O, apply the optional output gate and store bf16 rows.
+//               at the end of an item they normalize O, apply the optional output gate (its tile brought into L2 by
+//               the producer) and store bf16 rows.
 #include "common.cuh"
 #include "kd_internal.h"
 
@@ -41,7 +48,12 @@ struct Cfg {
   static constexpr int V_BYTES = KV_CHUNK * V_CHUNKS;
   static constexpr int STAGE_BYTES = K_BYTES + V_BYTES;
   static constexpr int STAGES = HD <= 256 ? 2 : 1;
-  static constexpr int SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 256;
+  static constexpr int BASE_SMEM = Q_BYTES + STAGES * STAGE_BYTES + 1024 + 512;  // + alignment, items, barriers
+  // The epilogue's staging areas: 32 rows x 32 columns of bf16 (2 KB) per softmax warp, for coalesced gate loads and
+  // output stores; left out where shared memory has no room (head dim 512 stores row by row).
+  static constexpr bool STAGED = BASE_SMEM + 4 * 2048 <= 227 * 1024;
+  static constexpr int EPI_BYTES = STAGED ? 4 * 2048 : 0;
+  static constexpr int SMEM = BASE_SMEM + EPI_BYTES;
   // Tensor-memory columns (fp32): O [0, DV), then two score buffers of BN; the bf16 probabilities P_j overwrite the
   // first BN / 2 columns of their own score buffer once the softmax has read it.
   static constexpr int O_COL = 0;
@@ -65,6 +77,16 @@ struct Args {
   float scale_log2;  // softmax scale * log2(e)
   int left, right;
   int* status;
+  int* sched;  // [2]: the work counter beyond the first item of each CTA, and the number of CTAs finished
+};
+
+// One unit of work: a 128-query tile of one sequence for one query head and value slice.
+struct Item {
+  int q0, lq, k0, lk;       // the sequence's first query and key rows, its query and key lengths
+  int qs;                   // the tile's first query within the sequence
+  int head, slice;
+  int first_tile, n_tiles;  // visible key tiles; n_tiles < 0: no more work
+  int pad[3];
 };
 
 constexpr int THREADS = 192;
@@ -101,63 +123,107 @@ KD_DEVICE float max3(float a, float b, float c) {
   return d;
 }
 
+// The next work item: item `idx` in the order sequences (pack order) > query tiles of the sequence, from its last
+// (the most expensive when causal) to its first > query heads > value slices. (cs, cbase) is the caller's cursor: a
+// sequence and the number of query tiles before it. A CTA's item indices only grow, so the cursor only moves forward.
+template <int HD, int DV>
+KD_DEVICE void next_item(const Args& a, int idx, int& cs, int& cbase, Item& w) {
+  using C = Cfg<HD, DV>;
+  constexpr int BM = C::BM, BN = C::BN;
+  const int rest = idx / C::SLICES;
+  w.slice = idx - rest * C::SLICES;
+  w.head = rest % a.hq;
+  const int tile = rest / a.hq;
+  w.n_tiles = -1;
+  while (cs < a.num_seqs) {
+    const int qa = a.cu_q[cs], qb = a.cu_q[cs + 1];
+    const int n = (qb - qa + BM - 1) / BM;
+    if (tile < cbase + n) {
+      w.q0 = qa;
+      w.lq = qb - qa;
+      w.k0 = a.cu_k[cs];
+      w.lk = a.cu_k[cs + 1] - w.k0;
+      w.qs = (n - 1 - (tile - cbase)) * BM;
+      const int off = w.lk - w.lq;  // end alignment of queries to keys
+      const int qe = min(w.qs + BM, w.lq);
+      int kmin = 0, kmax = w.lk - 1;
+      if (a.left >= 0) kmin = max(0, w.qs + off - a.left);
+      if (a.right >= 0) kmax = min(w.lk - 1, qe - 1 + off + a.right);
+      w.first_tile = kmin / BN;
+      w.n_tiles = kmax < kmin ? 0 : kmax / BN - w.first_tile + 1;
+      return;
+    }
+    cbase += n;
+    ++cs;
+  }
+}
+
+// 16 bytes of the gate tensor (read-only for the kernel's lifetime).
+KD_DEVICE uint4 load_gate16(const __nv_bfloat16* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Two gated outputs: bf16 pairs o and g -> bf16(o * sigmoid(g)) (the product rounded once). sigmoid(x) =
+// 1 / (1 + 2^(-x log2 e)): the exponential on the MUFU, the reciprocal by Newton steps on the FMA pipe (the epilogue
+// would otherwise issue two MUFU operations per output): a first guess with the exponent reflected (bits
+// 254 * 2^23 - bits(y), within 12.5% of 1 / y for y in [1, 2^126]) and three steps r <- r + r (1 - y r), relative
+// error 0.125 -> 1.6e-2 -> 2.4e-4 -> 6e-8.
+KD_DEVICE uint32_t gate_pair(uint32_t o, uint32_t g) {
+  const float2 ov = unpack_bf16x2(o), gv = unpack_bf16x2(g);
+  const float2 xs = fma2(gv, make_float2(-1.4426950408889634f, -1.4426950408889634f), make_float2(0.f, 0.f));
+  const float2 e = make_float2(fast_exp2(fminf(xs.x, 126.f)), fast_exp2(fminf(xs.y, 126.f)));
+  const float2 y = add2(e, make_float2(1.f, 1.f));  // in [1, 2^126]
+  float2 r = make_float2(__int_as_float(0x7F000000 - __float_as_int(y.x)),
+                         __int_as_float(0x7F000000 - __float_as_int(y.y)));
+  const float2 ny = make_float2(-y.x, -y.y);
+#pragma unroll
+  for (int i = 0; i < 3; ++i) r = fma2(r, fma2(ny, r, make_float2(1.f, 1.f)), r);
+  return pack_bf16x2(ov.x * r.x, ov.y * r.y);
+}
+
+// Brings a tile of a tensor into L2 ahead of its use.
+KD_DEVICE void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 template <int HD, int DV>
 __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,
                      const __grid_constant__ CUtensorMap map_v, const __grid_constant__ CUtensorMap map_g, Args a) {
   using C = Cfg<HD, DV>;
-  constexpr int BM = C::BM, BN = C::BN;
+  constexpr int BM = C::BM, BN = C::BN, ST = C::STAGES;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* s_q = smem;
   uint8_t* s_kv = smem + C::Q_BYTES;  // stage s: K at s * STAGE_BYTES, V right after
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::Q_BYTES + C::STAGES * C::STAGE_BYTES);
+  uint8_t* s_epi = smem + C::Q_BYTES + ST * C::STAGE_BYTES;  // [4 warps][2 KB] when staged
+  Item* items = reinterpret_cast<Item*>(s_epi + C::EPI_BYTES);  // [2]: the work item ring
+  uint64_t* bars = reinterpret_cast<uint64_t*>(items + 2);
   uint64_t* q_full = bars;
-  uint64_t* k_full = bars + 1;                  // [STAGES]
-  uint64_t* v_full = k_full + C::STAGES;        // [STAGES]
-  uint64_t* k_empty = v_full + C::STAGES;       // [STAGES]: released by the S = Q K^T that read the stage's K
-  uint64_t* v_empty = k_empty + C::STAGES;      // [STAGES]: released by the O += P V that read its V
-  uint64_t* s_full = v_empty + C::STAGES;       // [2]
-  uint64_t* p_full = s_full + 2;                // [2]
-  uint64_t* pv_done = p_full + 2;               // [2]
-  uint64_t* q_free = pv_done + 2;              // the last S has read Q: its buffer takes the gate tile
-  uint64_t* g_full = q_free + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(g_full + 1);
-
-  // ---- this CTA's (sequence, query tile), numbered sequence by sequence from the device bounds
-  int tile = blockIdx.x;
-  int seq = -1, qs = 0, lq = 0, lk = 0, q0 = 0, k0 = 0;
-  for (int s = 0; s < a.num_seqs; ++s) {
-    const int qa = a.cu_q[s], qb = a.cu_q[s + 1];
-    const int n = (qb - qa + BM - 1) / BM;
-    if (tile < n) {
-      seq = s;
-      q0 = qa;
-      lq = qb - qa;
-      k0 = a.cu_k[s];
-      lk = a.cu_k[s + 1] - k0;
-      qs = (n - 1 - tile) * BM;  // the last (most expensive when causal) tiles of a sequence first
-      break;
-    }
-    tile -= n;
-  }
-  if (seq < 0) return;  // uniform across the CTA: nothing allocated yet
-  const int head = blockIdx.y;
-  const int kvh = head / (a.hq / a.hkv);
-  const int vcol = (int)blockIdx.z * DV;  // this CTA's value slice within the head
-  const int off = lk - lq;  // end alignment of queries to keys
-  const int qe = min(qs + BM, lq);
-  int kmin = 0, kmax = lk - 1;
-  if (a.left >= 0) kmin = max(0, qs + off - a.left);
-  if (a.right >= 0) kmax = min(lk - 1, qe - 1 + off + a.right);
-  const int first_tile = kmin / BN;
-  const int n_tiles = kmax < kmin ? 0 : kmax / BN - first_tile + 1;
+  uint64_t* q_empty = bars + 1;         // released by an item's last S = Q K^T
+  uint64_t* k_full = bars + 2;          // [ST]
+  uint64_t* v_full = k_full + ST;       // [ST]
+  uint64_t* k_empty = v_full + ST;      // [ST]: released by the S = Q K^T that read the stage's K
+  uint64_t* v_empty = k_empty + ST;     // [ST]: released by the O += P V that read its V
+  uint64_t* s_full = v_empty + ST;      // [2]
+  uint64_t* p_full = s_full + 2;        // [2]
+  uint64_t* pv_done = p_full + 2;       // [2]
+  uint64_t* item_full = pv_done + 2;    // [2]
+  uint64_t* item_empty = item_full + 2; // [2]: read by the MMA thread and the four softmax warps
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 2);
 
   const int warp = threadIdx.x / 32;
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int s = 0; s < C::STAGES; ++s) {
+    mbar_init(q_empty, 1);
+    for (int s = 0; s < ST; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&k_empty[s], 1);
@@ -167,9 +233,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 128);
       mbar_init(&pv_done[b], 1);
+      mbar_init(&item_full[b], 1);
+      mbar_init(&item_empty[b], 5);
     }
-    mbar_init(q_free, 1);
-    mbar_init(g_full, 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -180,83 +246,111 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  const int group = a.hq / a.hkv;
 
+  // Every role walks the same item sequence; K/V ring slots, score buffers and the Q buffer are counted across items.
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
-    if (n_tiles > 0 && elect_one()) {
+    // ------------------------------------------------------------ work fetch + TMA producer
+    if (elect_one()) {
       tma_prefetch_desc(&map_q);
       tma_prefetch_desc(&map_k);
       tma_prefetch_desc(&map_v);
-      mbar_arrive_expect_tx(q_full, C::Q_BYTES);
-      for (int c = 0; c < C::CHUNKS; ++c)
-        tma_load_2d(&map_q, q_full, s_q + c * C::Q_CHUNK, head * HD + c * 64, q0 + qs);
-      for (int j = 0; j < n_tiles; ++j) {
-        const int st = j % C::STAGES;
-        const uint32_t ph = (j / C::STAGES) & 1;
-        const int row = k0 + (first_tile + j) * BN;
-        uint8_t* sk = s_kv + st * C::STAGE_BYTES;
-        uint8_t* sv = sk + C::K_BYTES;
-        if (!mbar_wait(&k_empty[st], ph ^ 1, a.status)) goto done;
-        mbar_arrive_expect_tx(&k_full[st], C::K_BYTES);
-        for (int c = 0; c < C::CHUNKS; ++c) tma_load_2d(&map_k, &k_full[st], sk + c * C::KV_CHUNK, kvh * HD + c * 64, row);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, a.status)) goto done;
-        mbar_arrive_expect_tx(&v_full[st], C::V_BYTES);
-        for (int c = 0; c < C::V_CHUNKS; ++c)
-          tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + vcol + c * 64, row);
-      }
-      if (a.gate) {
-        // Qwen's output gate tile, into the Q buffer once the last S = Q K^T has read it: the epilogue then reads
-        // its row from shared memory instead of scattered global loads.
-        if (!mbar_wait(q_free, 0, a.status)) goto done;
-        mbar_arrive_expect_tx(g_full, C::V_CHUNKS * C::Q_CHUNK);
-        for (int c = 0; c < C::V_CHUNKS; ++c)
-          tma_load_2d(&map_g, g_full, s_q + c * C::Q_CHUNK, head * HD + vcol + c * 64, q0 + qs);
+      if (a.gate) tma_prefetch_desc(&map_g);
+      int cs = 0, cbase = 0;
+      uint32_t slot = 0, nq = 0;
+      for (uint32_t it = 0;; ++it) {
+        Item w;
+        const int idx = it == 0 ? (int)blockIdx.x : (int)gridDim.x + atomicAdd(a.sched, 1);
+        next_item<HD, DV>(a, idx, cs, cbase, w);
+        if (!mbar_wait(&item_empty[it & 1], ((it >> 1) & 1) ^ 1, a.status)) goto done;
+        items[it & 1] = w;
+        mbar_arrive(&item_full[it & 1]);
+        if (w.n_tiles < 0) break;
+        const int kvh = w.head / group;
+        const int vcol = w.slice * DV;
+        if (w.n_tiles > 0) {
+          if (!mbar_wait(q_empty, (nq & 1) ^ 1, a.status)) goto done;
+          ++nq;
+          mbar_arrive_expect_tx(q_full, C::Q_BYTES);
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_2d(&map_q, q_full, s_q + c * C::Q_CHUNK, w.head * HD + c * 64, w.q0 + w.qs);
+        }
+        for (int j = 0; j < w.n_tiles; ++j, ++slot) {
+          const int st = slot % ST;
+          const uint32_t ph = (slot / ST) & 1;
+          const int row = w.k0 + (w.first_tile + j) * BN;
+          uint8_t* sk = s_kv + st * C::STAGE_BYTES;
+          uint8_t* sv = sk + C::K_BYTES;
+          if (!mbar_wait(&k_empty[st], ph ^ 1, a.status)) goto done;
+          mbar_arrive_expect_tx(&k_full[st], C::K_BYTES);
+          for (int c = 0; c < C::CHUNKS; ++c)
+            tma_load_2d(&map_k, &k_full[st], sk + c * C::KV_CHUNK, kvh * HD + c * 64, row);
+          if (!mbar_wait(&v_empty[st], ph ^ 1, a.status)) goto done;
+          mbar_arrive_expect_tx(&v_full[st], C::V_BYTES);
+          for (int c = 0; c < C::V_CHUNKS; ++c)
+            tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + vcol + c * 64, row);
+        }
+        // Qwen's output gate for this tile, into L2 while the last key tiles run: the epilogue reads it from there.
+        if (a.gate && w.n_tiles > 0)
+          for (int c = 0; c < C::V_CHUNKS; ++c) tma_prefetch_l2(&map_g, w.head * HD + vcol + c * 64, w.q0 + w.qs);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (n_tiles > 0 && elect_one()) {
+    if (elect_one()) {
       constexpr uint32_t idesc_s = mma_idesc(1, BM, BN);          // bf16, K-major A and B
       constexpr uint32_t idesc_o = mma_idesc(1, BM, DV, 1);       // bf16, A from TMEM, MN-major B (V)
       const uint32_t sq = smem_u32(s_q);
-      if (!mbar_wait(q_full, 0, a.status)) goto done;
-      auto issue_s = [&](int j) -> bool {
-        const int st = j % C::STAGES;
-        if (!mbar_wait(&k_full[st], (j / C::STAGES) & 1, a.status)) return false;
-        tc_fence_after();
-        const uint32_t sk = smem_u32(s_kv + st * C::STAGE_BYTES);
-        const uint32_t d = tmem + C::S_COL + (j & 1) * BN;
+      uint32_t slot = 0, g = 0, nq = 0;
+      for (uint32_t it = 0;; ++it) {
+        if (!mbar_wait(&item_full[it & 1], (it >> 1) & 1, a.status)) goto done;
+        const int n = items[it & 1].n_tiles;
+        mbar_arrive(&item_empty[it & 1]);
+        if (n < 0) break;
+        if (n == 0) continue;
+        if (!mbar_wait(q_full, nq & 1, a.status)) goto done;
+        ++nq;
+        // S_G = Q K^T of the item's tile j (G = g + j counts tiles across items) into score buffer G & 1, whose
+        // probabilities P_{G-2} were read by P_{G-2} V_{G-2}: that product must have completed.
+        auto issue_s = [&](int j) -> bool {
+          const uint32_t G = g + j, sl = slot + j;
+          const int st = sl % ST;
+          if (G >= 2 && !mbar_wait(&pv_done[G & 1], ((G - 2) >> 1) & 1, a.status)) return false;
+          if (!mbar_wait(&k_full[st], (sl / ST) & 1, a.status)) return false;
+          tc_fence_after();
+          const uint32_t sk = smem_u32(s_kv + st * C::STAGE_BYTES);
+          const uint32_t d = tmem + C::S_COL + (G & 1) * BN;
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; ++kk) {
-          const int c = kk / 4, w = (kk % 4) * 32;
-          mma_f16_ss(d, sw128_kmajor_desc(sq + c * C::Q_CHUNK + w), sw128_kmajor_desc(sk + c * C::KV_CHUNK + w),
-                     idesc_s, kk > 0);
-        }
-        mma_commit(&k_empty[st]);  // the stage's K is free once these MMAs have read it
-        mma_commit(&s_full[j & 1]);
-        if (j == n_tiles - 1) mma_commit(q_free);  // Q is free once the last S has completed
-        return true;
-      };
-      if (!issue_s(0)) goto done;
-      for (int j = 0; j < n_tiles; ++j) {
-        // S_{j+1} first, so the softmax of tile j+1 can start while P_j V_j runs. Its score buffer last held
-        // P_{j-1}, read by P_{j-1} V_{j-1}: that product must have completed.
-        if (j + 1 < n_tiles) {
-          if (j >= 1 && !mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status)) goto done;
-          if (!issue_s(j + 1)) goto done;
-        }
-        const int st = j % C::STAGES;
-        if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1, a.status)) goto done;
-        if (!mbar_wait(&v_full[st], (j / C::STAGES) & 1, a.status)) goto done;
-        tc_fence_after();
-        const uint32_t sv = smem_u32(s_kv + st * C::STAGE_BYTES + C::K_BYTES);
-        const uint32_t p = tmem + C::S_COL + (j & 1) * BN;  // P_j over the first BN / 2 columns of S_j
+          for (int kk = 0; kk < HD / 16; ++kk) {
+            const int c = kk / 4, w = (kk % 4) * 32;
+            mma_f16_ss(d, sw128_kmajor_desc(sq + c * C::Q_CHUNK + w), sw128_kmajor_desc(sk + c * C::KV_CHUNK + w),
+                       idesc_s, kk > 0);
+          }
+          mma_commit(&k_empty[st]);  // the stage's K is free once these MMAs have read it
+          mma_commit(&s_full[G & 1]);
+          if (j == n - 1) mma_commit(q_empty);  // Q is free once the item's last S has completed
+          return true;
+        };
+        if (!issue_s(0)) goto done;
+        for (int j = 0; j < n; ++j) {
+          // S_{j+1} first, so the softmax of tile j+1 can start while P_j V_j runs.
+          if (j + 1 < n && !issue_s(j + 1)) goto done;
+          const uint32_t G = g + j, sl = slot + j;
+          const int st = sl % ST;
+          if (!mbar_wait(&p_full[G & 1], (G >> 1) & 1, a.status)) goto done;
+          if (!mbar_wait(&v_full[st], (sl / ST) & 1, a.status)) goto done;
+          tc_fence_after();
+          const uint32_t sv = smem_u32(s_kv + st * C::STAGE_BYTES + C::K_BYTES);
+          const uint32_t p = tmem + C::S_COL + (G & 1) * BN;  // P_G over the first BN / 2 columns of S_G
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per instruction: 8 columns of bf16 pairs, 2 KB of V rows
-          mma_f16_ts(tmem + C::O_COL, p + kk * 8, sw128_mnmajor_desc(sv + kk * 2048, C::KV_CHUNK), idesc_o,
-                     (j | kk) != 0);
-        mma_commit(&v_empty[st]);
-        mma_commit(&pv_done[j & 1]);
+          for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per instruction: 8 columns of bf16 pairs, 2 KB of V rows
+            mma_f16_ts(tmem + C::O_COL, p + kk * 8, sw128_mnmajor_desc(sv + kk * 2048, C::KV_CHUNK), idesc_o,
+                       (j | kk) != 0);
+          mma_commit(&v_empty[st]);
+          mma_commit(&pv_done[G & 1]);
+        }
+        slot += n;
+        g += n;
       }
     }
   } else {
@@ -264,141 +358,228 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-    const int qi = qs + r + off;  // the row's position on the key axis
-    float m_used = -INFINITY, l_sum = 0.f;  // running maximum (log2 units, possibly stale) and row sum
-    for (int j = 0; j < n_tiles; ++j) {
-      if (!mbar_wait(&s_full[j & 1], (j >> 1) & 1, a.status)) goto done;
-      tc_fence_after();
-      const uint32_t s_addr = lane_base + C::S_COL + (j & 1) * BN;
-      float sv[BN];
-#pragma unroll
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t t[32];
-        tmem_ld32(s_addr + c, t);
-        tmem_ld_wait_regs(t);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) sv[c + e] = __uint_as_float(t[e]);
-      }
-      const int n0 = (first_tile + j) * BN;
-      // Only tiles that cross the causal diagonal, the window's left edge or the sequence end need a mask; the
-      // condition is the same for every row of the CTA.
-      const bool edge = (n0 + BN > lk) || (a.right >= 0 && n0 + BN - 1 > qs + off + a.right) ||
-                        (a.left >= 0 && n0 < qe - 1 + off - a.left);
-      if (edge) {
-#pragma unroll
-        for (int e = 0; e < BN; ++e) {
-          const int key = n0 + e;
-          bool ok = key < lk;
-          if (a.right >= 0) ok = ok && key <= qi + a.right;
-          if (a.left >= 0) ok = ok && key >= qi - a.left;
-          if (!ok) sv[e] = -INFINITY;
-        }
-      }
-      // row maximum over 8 independent chains (a single chain would serialize BN dependent max operations)
-      float mx[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx[e] = sv[e];
-#pragma unroll
-      for (int e = 8; e < BN; e += 2) mx[(e / 2) & 7] = max3(mx[(e / 2) & 7], sv[e], sv[e + 1]);
-      const float mraw = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
-      const float mt = mraw * a.scale_log2;  // the scale is positive: max commutes with it
-      const float m_new = fmaxf(m_used, mt);
-      const bool need = m_new > m_used + RESCALE_THRESHOLD || (m_used == -INFINITY && m_new != -INFINITY);
-      const float f = !need ? 1.f : (m_used == -INFINITY ? 0.f : fast_exp2(m_used - m_new));
-      // tcgen05.ld/st are warp-collective: the warp rescales its O rows together (factor 1 where a row needs none).
-      if (j > 0 && __any_sync(0xffffffffu, need && m_used != -INFINITY)) {
-        // O holds P_{0..j-1} V: wait for the last product before rescaling it in place.
-        if (!mbar_wait(&pv_done[(j - 1) & 1], ((j - 1) >> 1) & 1, a.status)) goto done;
+    uint32_t g = 0;
+    for (uint32_t it = 0;; ++it) {
+      if (!mbar_wait(&item_full[it & 1], (it >> 1) & 1, a.status)) goto done;
+      const Item w = items[it & 1];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&item_empty[it & 1]);
+      if (w.n_tiles < 0) break;
+      const int n = w.n_tiles;
+      const int off = w.lk - w.lq;
+      const int qe = min(w.qs + BM, w.lq);
+      const int qi = w.qs + r + off;  // the row's position on the key axis
+      // the row's visible keys [key_lo, key_hi] (the mask of an edge tile is two compares and a select per key)
+      const int key_lo = a.left >= 0 ? qi - a.left : INT_MIN / 2;
+      const int key_hi = min(w.lk - 1, a.right >= 0 ? qi + a.right : INT_MAX / 2);
+      float m_used = -INFINITY, l_sum = 0.f;  // running maximum (log2 units, possibly stale) and row sum
+      for (int j = 0; j < n; ++j) {
+        const uint32_t G = g + j;
+        if (!mbar_wait(&s_full[G & 1], (G >> 1) & 1, a.status)) goto done;
         tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < DV; c += 32) {
+        const uint32_t s_addr = lane_base + C::S_COL + (G & 1) * BN;
+        float sv[BN];
+#pragma unroll
+        for (int c = 0; c < BN; c += 32) {
           uint32_t t[32];
-          tmem_ld32(lane_base + C::O_COL + c, t);
+          tmem_ld32(s_addr + c, t);
           tmem_ld_wait_regs(t);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) t[e] = __float_as_uint(__uint_as_float(t[e]) * f);
-          tmem_st32(lane_base + C::O_COL + c, t);
+          for (int e = 0; e < 32; ++e) sv[c + e] = __uint_as_float(t[e]);
         }
-        tmem_st_wait();
-      }
-      if (need) {
-        l_sum *= f;
-        m_used = m_new;
-      }
-      const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
-      float2 part[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // the row sum over independent chains
-      const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
-      const float2 base2 = make_float2(neg_base, neg_base);
+        const int n0 = (w.first_tile + j) * BN;
+        // Only tiles that cross the causal diagonal, the window's left edge or the sequence end need a mask; the
+        // condition is the same for every row of the tile.
+        const bool edge = (n0 + BN > w.lk) || (a.right >= 0 && n0 + BN - 1 > w.qs + off + a.right) ||
+                          (a.left >= 0 && n0 < qe - 1 + off - a.left);
+        if (edge) {
+          const int lo = key_lo - n0, hi = key_hi - n0;
 #pragma unroll
-      for (int c = 0; c < BN; c += 64) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const float2 x = fma2(make_float2(sv[c + 2 * e], sv[c + 2 * e + 1]), scale2, base2);
-          const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
-          part[e & 3] = add2(part[e & 3], p);
-          pk[e] = pack_bf16x2(p.x, p.y);
+          for (int e = 0; e < BN; ++e) sv[e] = (e >= lo && e <= hi) ? sv[e] : -INFINITY;
         }
-        tmem_st32(s_addr + c / 2, pk);  // P_j over the score columns this thread has already read
-      }
-      const float2 ps = add2(add2(part[0], part[1]), add2(part[2], part[3]));
-      l_sum += ps.x + ps.y;
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[j & 1]);
-    }
-    // ---- epilogue: O / l, optional gate, bf16 row
-    if (n_tiles > 0) {
-      if (!mbar_wait(&pv_done[(n_tiles - 1) & 1], ((n_tiles - 1) >> 1) & 1, a.status)) goto done;
-      tc_fence_after();
-    }
-    // The gate tile sits in the Q buffer (128-byte swizzled rows); without visible keys the output is 0 and needs
-    // no gate.
-    const bool gated = a.gate != nullptr && n_tiles > 0;
-    if (gated && !mbar_wait(g_full, 0, a.status)) goto done;
-    const int row = qs + r;
-    const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-    __nv_bfloat16* orow = a.out + (int64_t)(q0 + row) * a.ldo + (int64_t)head * HD + vcol;
+        // row maximum over 8 independent chains (a single chain would serialize BN dependent max operations)
+        float mx[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) mx[e] = sv[e];
+#pragma unroll
+        for (int e = 8; e < BN; e += 2) mx[(e / 2) & 7] = max3(mx[(e / 2) & 7], sv[e], sv[e + 1]);
+        const float mraw = max3(max3(mx[0], mx[1], mx[2]), max3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
+        const float mt = mraw * a.scale_log2;  // the scale is positive: max commutes with it
+        const float m_new = fmaxf(m_used, mt);
+        const bool need = m_new > m_used + RESCALE_THRESHOLD || (m_used == -INFINITY && m_new != -INFINITY);
+        const float f = !need ? 1.f : (m_used == -INFINITY ? 0.f : fast_exp2(m_used - m_new));
+        // tcgen05.ld/st are warp-collective: the warp rescales its O rows together (factor 1 where a row needs none).
+        if (j > 0 && __any_sync(0xffffffffu, need && m_used != -INFINITY)) {
+          // O holds P_{0..j-1} V: wait for the last product before rescaling it in place.
+          if (!mbar_wait(&pv_done[(G - 1) & 1], ((G - 1) >> 1) & 1, a.status)) goto done;
+          tc_fence_after();
 #pragma unroll 1
-    for (int c = 0; c < DV; c += 32) {
-      uint32_t t[32];
-      if (n_tiles > 0) {
-        tmem_ld32(lane_base + C::O_COL + c, t);  // warp-collective: every lane loads, valid rows store
-        tmem_ld_wait_regs(t);
+          for (int c = 0; c < DV; c += 32) {
+            uint32_t t[32];
+            tmem_ld32(lane_base + C::O_COL + c, t);
+            tmem_ld_wait_regs(t);
+#pragma unroll
+            for (int e = 0; e < 32; ++e) t[e] = __float_as_uint(__uint_as_float(t[e]) * f);
+            tmem_st32(lane_base + C::O_COL + c, t);
+          }
+          tmem_st_wait();
+        }
+        if (need) {
+          l_sum *= f;
+          m_used = m_new;
+        }
+        const float neg_base = m_used == -INFINITY ? 0.f : -m_used;
+        float2 part[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // the row sum over independent chains
+        const float2 scale2 = make_float2(a.scale_log2, a.scale_log2);
+        const float2 base2 = make_float2(neg_base, neg_base);
+#pragma unroll
+        for (int c = 0; c < BN; c += 64) {
+          uint32_t pk[32];
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float2 x = fma2(make_float2(sv[c + 2 * e], sv[c + 2 * e + 1]), scale2, base2);
+            const float2 p = make_float2(fast_exp2(x.x), fast_exp2(x.y));
+            part[e & 3] = add2(part[e & 3], p);
+            pk[e] = pack_bf16x2(p.x, p.y);
+          }
+          tmem_st32(s_addr + c / 2, pk);  // P_G over the score columns this thread has already read
+        }
+        const float2 ps = add2(add2(part[0], part[1]), add2(part[2], part[3]));
+        l_sum += ps.x + ps.y;
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[G & 1]);
+      }
+      // ---- epilogue: O / l, optional gate, bf16 rows. The gate rows (in L2 by now) are read while the last product
+      // completes; without visible keys the output is 0 and needs no gate.
+      const bool gated = a.gate != nullptr && n > 0;
+      const int64_t col0 = (int64_t)w.head * HD + w.slice * DV;
+      constexpr int GC = DV < 128 ? DV : 128;  // gate columns held in registers at a time
+      if constexpr (C::STAGED) {
+        // Through this warp's staging area (32 rows x 64 bytes: row i at 64 i, its 16-byte piece p at slot
+        // (p + i / 2) % 4, conflict-free both for a row per lane and for 8 rows of 4 lanes): each lane writes its
+        // row's normalized bf16 values, then reads back 4 pieces of 8 rows, multiplies them by the gate pieces it
+        // loaded (coalesced, two 32-column chunks ahead) and stores 64 contiguous bytes per row.
+        uint8_t* ws = s_epi + quarter * 2048;
+        const int tr_row = lane >> 2, tr_piece = lane & 3;  // the transposed access: rows tr_row + 8 m, one piece
+        const int wrow0 = w.qs + quarter * 32;              // the warp's first row within the sequence
+        auto at = [&](int i, int p) -> uint4* {
+          return reinterpret_cast<uint4*>(ws + i * 64 + (((p + (i >> 1)) & 3) << 4));
+        };
+        constexpr int NCH = DV / 32;
+        uint4 g4[2][4];
+        auto load_gates = [&](int cc) {
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {
+            const int row = wrow0 + tr_row + 8 * m;
+            g4[cc & 1][m] = row < w.lq ? load_gate16(a.gate + (int64_t)(w.q0 + row) * a.ldg + col0 + cc * 32 +
+                                                     tr_piece * 8)
+                                       : make_uint4(0, 0, 0, 0);
+          }
+        };
+        if (gated) {
+          load_gates(0);
+          if (NCH > 1) load_gates(1);
+        }
+        if (n > 0) {
+          const uint32_t G = g + n - 1;
+          if (!mbar_wait(&pv_done[G & 1], (G >> 1) & 1, a.status)) goto done;
+          tc_fence_after();
+        }
+        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll
+        for (int cc = 0; cc < NCH; ++cc) {
+          {  // this row's 32 columns: bf16(o / l)
+            uint32_t t[32];
+            if (n > 0) {
+              tmem_ld32(lane_base + C::O_COL + cc * 32, t);  // warp-collective
+              tmem_ld_wait_regs(t);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) t[e] = 0u;
+            }
+#pragma unroll
+            for (int pc = 0; pc < 4; ++pc) {
+              uint32_t pk[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e)
+                pk[e] = pack_bf16x2(__uint_as_float(t[8 * pc + 2 * e]) * inv,
+                                    __uint_as_float(t[8 * pc + 2 * e + 1]) * inv);
+              *at(lane, pc) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int m = 0; m < 4; ++m) {  // 8 rows x 4 pieces out
+            const int row = wrow0 + tr_row + 8 * m;
+            uint4 x = *at(tr_row + 8 * m, tr_piece);
+            if (gated) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
+              const uint4 gq = g4[cc & 1][m];
+              x.x = gate_pair(x.x, gq.x);
+              x.y = gate_pair(x.y, gq.y);
+              x.z = gate_pair(x.z, gq.z);
+              x.w = gate_pair(x.w, gq.w);
+            }
+            if (row < w.lq)
+              *reinterpret_cast<uint4*>(a.out + (int64_t)(w.q0 + row) * a.ldo + col0 + cc * 32 + tr_piece * 8) = x;
+          }
+          if (gated && cc + 2 < NCH) load_gates(cc + 2);
+          __syncwarp();
+        }
       } else {
+        const int row = w.qs + r;
+        const bool live = row < w.lq;
+        const __nv_bfloat16* grow = gated && live ? a.gate + (int64_t)(w.q0 + row) * a.ldg + col0 : nullptr;
+        uint4 g4[GC / 8];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) t[e] = 0u;
-      }
-      if (row < lq) {
-        uint32_t gw[16];
-        if (gated) {  // this row's 32 gate values: four 16-byte pieces of its swizzled 128-byte row
-          const uint8_t* grow = s_q + (c / 64) * C::Q_CHUNK + r * 128;
+        for (int e = 0; e < GC / 8; ++e) g4[e] = grow ? load_gate16(grow + 8 * e) : make_uint4(0, 0, 0, 0);
+        if (n > 0) {
+          const uint32_t G = g + n - 1;
+          if (!mbar_wait(&pv_done[G & 1], (G >> 1) & 1, a.status)) goto done;
+          tc_fence_after();
+        }
+        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+        __nv_bfloat16* orow = a.out + (int64_t)(w.q0 + row) * a.ldo + col0;
 #pragma unroll
-          for (int k4 = 0; k4 < 4; ++k4) {
-            const uint4 g4 = *reinterpret_cast<const uint4*>(grow + ((((c % 64) / 8 + k4) ^ (r & 7)) << 4));
-            gw[4 * k4] = g4.x;
-            gw[4 * k4 + 1] = g4.y;
-            gw[4 * k4 + 2] = g4.z;
-            gw[4 * k4 + 3] = g4.w;
+        for (int h = 0; h < DV; h += GC) {
+          if (h > 0) {
+#pragma unroll
+            for (int e = 0; e < GC / 8; ++e) g4[e] = grow ? load_gate16(grow + h + 8 * e) : make_uint4(0, 0, 0, 0);
+          }
+#pragma unroll
+          for (int c = 0; c < GC; c += 32) {
+            uint32_t t[32];
+            if (n > 0) {
+              tmem_ld32(lane_base + C::O_COL + h + c, t);  // warp-collective: every lane loads, valid rows store
+              tmem_ld_wait_regs(t);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 32; ++e) t[e] = 0u;
+            }
+            if (live) {
+              uint32_t packed[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                float v0 = bf16_round(__uint_as_float(t[2 * e]) * inv);
+                float v1 = bf16_round(__uint_as_float(t[2 * e + 1]) * inv);
+                if (grow) {
+                  const uint4 q4 = g4[(c + 2 * e) / 8];
+                  const int k = ((c + 2 * e) % 8) / 2;
+                  const float2 gv = unpack_bf16x2(k == 0 ? q4.x : k == 1 ? q4.y : k == 2 ? q4.z : q4.w);
+                  v0 *= sigmoid(gv.x);
+                  v1 *= sigmoid(gv.y);
+                }
+                packed[e] = pack_bf16x2(v0, v1);
+              }
+#pragma unroll
+              for (int q4 = 0; q4 < 4; ++q4)
+                *reinterpret_cast<uint4*>(orow + h + c + 8 * q4) =
+                    make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
+            }
           }
         }
-        uint32_t packed[16];
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float v0 = bf16_round(__uint_as_float(t[2 * e]) * inv);
-          float v1 = bf16_round(__uint_as_float(t[2 * e + 1]) * inv);
-          if (gated) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
-            const float2 gv = unpack_bf16x2(gw[e]);
-            v0 *= sigmoid(gv.x);
-            v1 *= sigmoid(gv.y);
-          }
-          packed[e] = pack_bf16x2(v0, v1);
-        }
-#pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-          *reinterpret_cast<uint4*>(orow + c + 8 * q4) =
-              make_uint4(packed[4 * q4], packed[4 * q4 + 1], packed[4 * q4 + 2], packed[4 * q4 + 3]);
       }
+      g += n > 0 ? n : 0;
     }
   }
 done:
@@ -408,6 +589,15 @@ done:
   if (warp == 1) {
     __syncwarp();
     tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    // The last CTA to finish returns the work counter to zero for the next launch: every CTA stopped fetching work
+    // before counting itself here.
+    __threadfence();
+    if (atomicAdd(a.sched + 1, 1) == (int)gridDim.x - 1) {
+      atomicExch(a.sched, 0);
+      atomicExch(a.sched + 1, 0);
+    }
   }
 }
 
@@ -438,14 +628,16 @@ int launch(const void* q, int64_t ldq, const void* k, int64_t ldk, const void* v
     if (e != cudaSuccess) return record_cuda_error(e, "attention: cudaFuncSetAttribute");
     configured[dev] = true;
   }
-  // Upper bound on query tiles over all sequences: sum(ceil(Lq / BM)) <= total_q / BM + num_seqs.
-  const int64_t tiles = total_q / C::BM + a.num_seqs;
-  if (tiles > 0x7fffffff) return set_error(KD_ERR_ARGUMENT, "attention: too many query tiles");
-  dim3 grid((unsigned)tiles, (unsigned)a.hq, (unsigned)C::SLICES);
+  // Work items: sum over sequences of ceil(Lq / BM) query tiles <= total_q / BM + num_seqs, times heads and slices.
+  // Persistent CTAs (as many as fit on the device at once) take them in order, the first one each by its index and
+  // the rest from the shared counter.
+  const int64_t items = (total_q / C::BM + a.num_seqs) * a.hq * C::SLICES;
+  if (items > 0x7fffffff - 4096) return set_error(KD_ERR_ARGUMENT, "attention: too many work items");
+  const int64_t resident = (int64_t)num_sms(dev) * C::CTAS_PER_SM;
+  const int grid = (int)(items < resident ? items : resident);
   kernel<<<grid, THREADS, C::SMEM, stream>>>(mq, mk, mv, mg, a);
   return record_cuda_error(cudaGetLastError(), "attention: launch");
 }
-
 }  // namespace fa
 }  // namespace kd
 
@@ -455,13 +647,13 @@ extern "C" int kd_attention_varlen(const void* q, int64_t ldq, const void* k, in
                                    void* out, int64_t ldo, const void* gate, int64_t ldg, const int32_t* cu_q,
                                    const int32_t* cu_k, int num_seqs, int max_q, int64_t total_q, int64_t total_k,
                                    int num_heads_q, int num_heads_kv, int head_dim, float scale, int window_left,
-                                   int window_right, int* status, cudaStream_t stream) {
+                                   int window_right, int* status, int* sched, cudaStream_t stream) {
   (void)max_q;
   if (num_seqs < 0 || total_q < 0 || total_k < 0) return set_error(KD_ERR_ARGUMENT, "attention: negative sizes");
   if (num_seqs == 0 || total_q == 0) return KD_OK;
   if (num_heads_q <= 0 || num_heads_kv <= 0 || num_heads_q % num_heads_kv)
     return set_error(KD_ERR_ARGUMENT, "attention: query heads must be a multiple of key/value heads");
-  if (!q || !k || !v || !out || !cu_q || !cu_k || !status) return set_error(KD_ERR_ARGUMENT, "attention: null pointer");
+  if (!q || !k || !v || !out || !cu_q || !cu_k || !status || !sched) return set_error(KD_ERR_ARGUMENT, "attention: null pointer");
   auto a16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!a16(q) || !a16(k) || !a16(v) || !a16(out) || (gate && !a16(gate)) || ldq % 8 || ldk % 8 || ldv % 8 ||
       ldo % 8 || (gate && ldg % 8))
@@ -483,6 +675,7 @@ extern "C" int kd_attention_varlen(const void* q, int64_t ldq, const void* k, in
   a.left = window_left;
   a.right = window_right;
   a.status = status;
+  a.sched = sched;
   const int64_t tk = total_k;
   switch (head_dim) {
     case 64:

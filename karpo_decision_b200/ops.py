@@ -14,9 +14,10 @@ __all__ = ["EPI_GEGLU", "EPI_RESIDUAL", "EPI_STORE", "EPI_SWIGLU", "NORM_NONE", 
            "add_rmsnorm", "attention_varlen", "check_status", "embed", "gather_rows", "gemm", "gemm_fp8", "marker_norm",
            "norm_add", "qkv_norm_rope", "qkv_projection", "quantize_rows_e4m3", "readout", "rmsnorm", "rmsnorm_e4m3",
            "rope_gather", "rope_table",
-           "status_word"]
+           "sched_pair", "status_word"]
 
 _STATUS: dict[int, torch.Tensor] = {}
+_SCHED: dict[int, torch.Tensor] = {}
 
 
 def status_word(device: torch.device) -> torch.Tensor:
@@ -25,6 +26,15 @@ def status_word(device: torch.device) -> torch.Tensor:
     if index not in _STATUS:
         _STATUS[index] = torch.zeros(1, dtype=torch.int32, device=torch.device("cuda", index))
     return _STATUS[index]
+
+
+def sched_pair(device: torch.device) -> torch.Tensor:
+    """The device's default int32[2] work counter for attention launches (zero between launches). Launches that can
+    run at the same time (different streams, no ordering) take their own pair through ``attention_varlen(sched=)``."""
+    index = device.index if device.index is not None else torch.cuda.current_device()
+    if index not in _SCHED:
+        _SCHED[index] = torch.zeros(2, dtype=torch.int32, device=torch.device("cuda", index))
+    return _SCHED[index]
 
 
 def check_status(device: torch.device) -> None:
@@ -205,21 +215,26 @@ def qkv_norm_rope(qkv: torch.Tensor, seqpos: torch.Tensor, heads: int, kv_heads:
 
 def attention_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_q: torch.Tensor, cu_k: torch.Tensor,
                      max_q: int, scale: float, window: tuple[int, int], gate: torch.Tensor | None = None,
-                     out: torch.Tensor | None = None) -> torch.Tensor:
+                     out: torch.Tensor | None = None, sched: torch.Tensor | None = None) -> torch.Tensor:
     """Varlen attention (the reference's varlen contract, end-aligned window); q (Tq, Hq, d), k/v (Tk, Hkv, d),
-    int32 boundaries on the device; returns (Tq, Hq * d), gated by sigmoid(gate) when given."""
+    int32 boundaries on the device; returns (Tq, Hq * d), gated by sigmoid(gate) when given. ``sched`` is the
+    launch's int32[2] work counter (default: the device's, ``sched_pair``)."""
     _require(q.dim() == 3 and k.dim() == 3 and v.dim() == 3, "q, k, v must be (rows, heads, head_dim)")
     _require(q.stride(2) == 1 and k.stride(2) == 1 and v.stride(2) == 1, "head_dim must be contiguous")
     _require(q.stride(1) == q.shape[2] and k.stride(1) == k.shape[2] and v.stride(1) == v.shape[2],
              "heads must be packed within a row")
     _require(cu_q.dtype == torch.int32 and cu_k.dtype == torch.int32, "boundaries must be int32")
     tq, hq, d = q.shape
+    if sched is None:
+        sched = sched_pair(q.device)
+    _require(sched.dtype == torch.int32 and sched.numel() >= 2 and sched.is_contiguous(),
+             "sched must be a contiguous int32 pair")
     if out is None:
         out = torch.empty(tq, hq * d, dtype=torch.bfloat16, device=q.device)
     call("kd_attention_varlen", q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
          out.data_ptr(), out.stride(0), _ptr(gate), gate.stride(0) if gate is not None else 0, cu_q.data_ptr(),
          cu_k.data_ptr(), cu_q.numel() - 1, int(max_q), tq, k.shape[0], hq, k.shape[1], d, float(scale), int(window[0]),
-         int(window[1]), status_word(q.device).data_ptr(), _stream(q))
+         int(window[1]), status_word(q.device).data_ptr(), sched.data_ptr(), _stream(q))
     return out
 
 

@@ -127,6 +127,7 @@ class Workspace:
         q_cols = max((spec.heads * spec.attn_dims(kind)[0] for kind in kinds), default=0)
         kv_cols = max((spec.attn_dims(kind)[0] * spec.attn_dims(kind)[1] for kind in kinds), default=0)
         self.capacity = capacity
+        self.sched = torch.zeros(2, dtype=torch.int32, device=device)  # the attention launches' work counter
         self.h = torch.empty(t, h, **bf)
         self.x = torch.empty(t, h, **bf)
         # the stored projection, only for layers that take the unfused QKV path
@@ -540,19 +541,19 @@ class Packed(torch.nn.Module):
             o_buf = ws.o(s, layer.kind, t)
             if plan is None:
                 o = ops.attention_varlen(q, k, v, p.cu, p.cu, int(p.max_length), self._scale, window, gate=gate,
-                                         out=o_buf)
+                                         out=o_buf, sched=ws.sched)
             else:  # each virtual sequence's keys: the shared block (or its window tail), then its own rows
                 rows, k_cu = (plan.s_rows, plan.s_cu) if layer.kind == "sliding_attention" else \
                     (plan.g_rows, plan.g_cu)
                 kg, vg = ops.gather_rows(k, rows), ops.gather_rows(v, rows)
                 o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, self._scale, window, gate=gate,
-                                         out=o_buf)
+                                         out=o_buf, sched=ws.sched)
             if images is not None and layer.kind == "sliding_attention":
                 # each image's rows again, over the window before the image and the whole image
                 # (families/gemma/vision.py:199-210)
                 oi = ops.attention_varlen(ops.gather_rows(q, images.rows), ops.gather_rows(k, images.keys),
                                           ops.gather_rows(v, images.keys), images.q_cu, images.k_cu, images.max_q,
-                                          self._scale, (self.window - 1, -1))
+                                          self._scale, (self.window - 1, -1), sched=ws.sched)
                 ops.scatter_rows(oi, images.rows, o)
             self._after_attention(layer, h, o, ws)
         return h
@@ -657,7 +658,7 @@ class Packed(torch.nn.Module):
             k, v = ops.gather_rows(k, plan.g_rows), ops.gather_rows(v, plan.g_rows)
         max_q = int(p.max_markers) if plan is None else 1  # a virtual sequence reads out at most one marker
         o = ops.attention_varlen(qm, k, v, q_cu, k_cu, max_q, self._scale, (-1, -1), gate=gm,
-                                 out=ws.o(self.spec, layer.kind, n))
+                                 out=ws.o(self.spec, layer.kind, n), sched=ws.sched)
         hm = ops.gather_rows(h, markers)
         self._after_attention(layer, hm, o, ws)
         return hm

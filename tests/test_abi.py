@@ -49,5 +49,5 @@ def test_argument_errors_launch_nothing():
     assert rc == -1
     assert "gemm" in _lib.last_error()
     rc = lib.kd_attention_varlen(None, 0, None, 0, None, 0, None, 0, None, 0, None, None, 2, 8, 16, 16, 3, 2, 128,
-                                 1.0, -1, 0, None, None)  # 3 query heads over 2 kv heads
+                                 1.0, -1, 0, None, None, None)  # 3 query heads over 2 kv heads
     assert rc == -1
