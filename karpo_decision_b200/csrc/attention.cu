@@ -20,7 +20,8 @@
 // 128 KB query tile). 6 warps:
 //   warp 0      work fetch + TMA producer: publishes each item to the other roles through a two-slot ring, then its
 //               Q tile and its K and V tiles through a ring (2 stages; 1 for head dim 512) counted across items;
-//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of two TMEM score buffers, then O += P_j V_j with
+//   warp 1      MMA issuer (one thread): S_j = Q K_j^T into one of 2-4 TMEM score buffers (as many as the allocation
+//               holds beside O), then O += P_j V_j with
 //               P_j read from TMEM (A operand, written over S_j) and V_j as an MN-major B operand from shared memory;
 //               an item's first S can run while the previous item's epilogue reads O;
 //   warps 2..5  softmax, one query row per thread (its TMEM lane): scores -> masked, scaled, exp2 against a running
@@ -59,9 +60,12 @@ struct Cfg {
   static constexpr int O_COL = 0;
   static constexpr int S_COL = DV;
   static constexpr int TMEM_COLS = DV + 2 * BN <= 256 ? 256 : 512;
+  // Score buffers: as many as the allocation holds beyond O (at most 4). Score tile G goes to buffer G % NS, whose
+  // probabilities P_{G-NS} were read by P_{G-NS} V_{G-NS}; more buffers leave that product more time to complete.
+  static constexpr int NS = (TMEM_COLS - DV) / BN < 4 ? (TMEM_COLS - DV) / BN : 4;
   // Two CTAs per SM (their softmax and MMA phases interleave) when shared and tensor memory allow it.
   static constexpr int CTAS_PER_SM = (2 * SMEM <= 227 * 1024 && 2 * TMEM_COLS <= 512) ? 2 : 1;
-  static_assert(S_COL + 2 * BN <= TMEM_COLS, "tensor memory budget");
+  static_assert(NS >= 2 && S_COL + NS * BN <= TMEM_COLS, "tensor memory budget");
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
   static_assert(DV <= 256 && HD % DV == 0, "value slices of at most 256 columns");
 };
@@ -211,10 +215,11 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
   uint64_t* v_full = k_full + ST;       // [ST]
   uint64_t* k_empty = v_full + ST;      // [ST]: released by the S = Q K^T that read the stage's K
   uint64_t* v_empty = k_empty + ST;     // [ST]: released by the O += P V that read its V
-  uint64_t* s_full = v_empty + ST;      // [2]
-  uint64_t* p_full = s_full + 2;        // [2]
-  uint64_t* pv_done = p_full + 2;       // [2]
-  uint64_t* item_full = pv_done + 2;    // [2]
+  constexpr int NS = C::NS;
+  uint64_t* s_full = v_empty + ST;      // [NS]
+  uint64_t* p_full = s_full + NS;       // [NS]
+  uint64_t* pv_done = p_full + NS;      // [NS]
+  uint64_t* item_full = pv_done + NS;   // [2]
   uint64_t* item_empty = item_full + 2; // [2]: read by the MMA thread and the four softmax warps
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(item_empty + 2);
 
@@ -230,11 +235,13 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
       mbar_init(&v_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
+      mbar_init(&item_full[b], 1);
+      mbar_init(&item_empty[b], 5);
+    }
+    for (int b = 0; b < NS; ++b) {
       mbar_init(&s_full[b], 1);
       mbar_init(&p_full[b], 128);
       mbar_init(&pv_done[b], 1);
-      mbar_init(&item_full[b], 1);
-      mbar_init(&item_empty[b], 5);
     }
     fence_barrier_init();
   }
@@ -275,21 +282,31 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
           for (int c = 0; c < C::CHUNKS; ++c)
             tma_load_2d(&map_q, q_full, s_q + c * C::Q_CHUNK, w.head * HD + c * 64, w.q0 + w.qs);
         }
-        for (int j = 0; j < w.n_tiles; ++j, ++slot) {
-          const int st = slot % ST;
-          const uint32_t ph = (slot / ST) & 1;
-          const int row = w.k0 + (w.first_tile + j) * BN;
-          uint8_t* sk = s_kv + st * C::STAGE_BYTES;
-          uint8_t* sv = sk + C::K_BYTES;
-          if (!mbar_wait(&k_empty[st], ph ^ 1, a.status)) goto done;
-          mbar_arrive_expect_tx(&k_full[st], C::K_BYTES);
-          for (int c = 0; c < C::CHUNKS; ++c)
-            tma_load_2d(&map_k, &k_full[st], sk + c * C::KV_CHUNK, kvh * HD + c * 64, row);
-          if (!mbar_wait(&v_empty[st], ph ^ 1, a.status)) goto done;
-          mbar_arrive_expect_tx(&v_full[st], C::V_BYTES);
-          for (int c = 0; c < C::V_CHUNKS; ++c)
-            tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + vcol + c * 64, row);
+        // Keys run one tile ahead of values: a tile's keys wait only for the S = Q K^T that last read their stage,
+        // not behind the previous tile's values (which wait for an O += P V).
+        for (int j = 0; j <= w.n_tiles; ++j) {
+          if (j < w.n_tiles) {
+            const uint32_t sl = slot + j;
+            const int st = sl % ST;
+            uint8_t* sk = s_kv + st * C::STAGE_BYTES;
+            if (!mbar_wait(&k_empty[st], ((sl / ST) & 1) ^ 1, a.status)) goto done;
+            mbar_arrive_expect_tx(&k_full[st], C::K_BYTES);
+            for (int c = 0; c < C::CHUNKS; ++c)
+              tma_load_2d(&map_k, &k_full[st], sk + c * C::KV_CHUNK, kvh * HD + c * 64,
+                          w.k0 + (w.first_tile + j) * BN);
+          }
+          if (j >= 1) {
+            const uint32_t sl = slot + j - 1;
+            const int st = sl % ST;
+            uint8_t* sv = s_kv + st * C::STAGE_BYTES + C::K_BYTES;
+            if (!mbar_wait(&v_empty[st], ((sl / ST) & 1) ^ 1, a.status)) goto done;
+            mbar_arrive_expect_tx(&v_full[st], C::V_BYTES);
+            for (int c = 0; c < C::V_CHUNKS; ++c)
+              tma_load_2d(&map_v, &v_full[st], sv + c * C::KV_CHUNK, kvh * HD + vcol + c * 64,
+                          w.k0 + (w.first_tile + j - 1) * BN);
+          }
         }
+        slot += w.n_tiles > 0 ? w.n_tiles : 0;
         // Qwen's output gate for this tile, into L2 while the last key tiles run: the epilogue reads it from there.
         if (a.gate && w.n_tiles > 0)
           for (int c = 0; c < C::V_CHUNKS; ++c) tma_prefetch_l2(&map_g, w.head * HD + vcol + c * 64, w.q0 + w.qs);
@@ -310,16 +327,16 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         if (n == 0) continue;
         if (!mbar_wait(q_full, nq & 1, a.status)) goto done;
         ++nq;
-        // S_G = Q K^T of the item's tile j (G = g + j counts tiles across items) into score buffer G & 1, whose
-        // probabilities P_{G-2} were read by P_{G-2} V_{G-2}: that product must have completed.
+        // S_G = Q K^T of the item's tile j (G = g + j counts tiles across items) into score buffer G % NS, whose
+        // probabilities P_{G-NS} were read by P_{G-NS} V_{G-NS}: that product must have completed.
         auto issue_s = [&](int j) -> bool {
           const uint32_t G = g + j, sl = slot + j;
           const int st = sl % ST;
-          if (G >= 2 && !mbar_wait(&pv_done[G & 1], ((G - 2) >> 1) & 1, a.status)) return false;
+          if (G >= NS && !mbar_wait(&pv_done[G % NS], ((G - NS) / NS) & 1, a.status)) return false;
           if (!mbar_wait(&k_full[st], (sl / ST) & 1, a.status)) return false;
           tc_fence_after();
           const uint32_t sk = smem_u32(s_kv + st * C::STAGE_BYTES);
-          const uint32_t d = tmem + C::S_COL + (G & 1) * BN;
+          const uint32_t d = tmem + C::S_COL + (G % NS) * BN;
 #pragma unroll
           for (int kk = 0; kk < HD / 16; ++kk) {
             const int c = kk / 4, w = (kk % 4) * 32;
@@ -327,7 +344,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
                        idesc_s, kk > 0);
           }
           mma_commit(&k_empty[st]);  // the stage's K is free once these MMAs have read it
-          mma_commit(&s_full[G & 1]);
+          mma_commit(&s_full[G % NS]);
           if (j == n - 1) mma_commit(q_empty);  // Q is free once the item's last S has completed
           return true;
         };
@@ -337,17 +354,17 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
           if (j + 1 < n && !issue_s(j + 1)) goto done;
           const uint32_t G = g + j, sl = slot + j;
           const int st = sl % ST;
-          if (!mbar_wait(&p_full[G & 1], (G >> 1) & 1, a.status)) goto done;
+          if (!mbar_wait(&p_full[G % NS], (G / NS) & 1, a.status)) goto done;
           if (!mbar_wait(&v_full[st], (sl / ST) & 1, a.status)) goto done;
           tc_fence_after();
           const uint32_t sv = smem_u32(s_kv + st * C::STAGE_BYTES + C::K_BYTES);
-          const uint32_t p = tmem + C::S_COL + (G & 1) * BN;  // P_G over the first BN / 2 columns of S_G
+          const uint32_t p = tmem + C::S_COL + (G % NS) * BN;  // P_G over the first BN / 2 columns of S_G
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk)  // 16 keys per instruction: 8 columns of bf16 pairs, 2 KB of V rows
             mma_f16_ts(tmem + C::O_COL, p + kk * 8, sw128_mnmajor_desc(sv + kk * 2048, C::KV_CHUNK), idesc_o,
                        (j | kk) != 0);
           mma_commit(&v_empty[st]);
-          mma_commit(&pv_done[G & 1]);
+          mma_commit(&pv_done[G % NS]);
         }
         slot += n;
         g += n;
@@ -375,9 +392,9 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
       float m_used = -INFINITY, l_sum = 0.f;  // running maximum (log2 units, possibly stale) and row sum
       for (int j = 0; j < n; ++j) {
         const uint32_t G = g + j;
-        if (!mbar_wait(&s_full[G & 1], (G >> 1) & 1, a.status)) goto done;
+        if (!mbar_wait(&s_full[G % NS], (G / NS) & 1, a.status)) goto done;
         tc_fence_after();
-        const uint32_t s_addr = lane_base + C::S_COL + (G & 1) * BN;
+        const uint32_t s_addr = lane_base + C::S_COL + (G % NS) * BN;
         float sv[BN];
 #pragma unroll
         for (int c = 0; c < BN; c += 32) {
@@ -411,7 +428,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         // tcgen05.ld/st are warp-collective: the warp rescales its O rows together (factor 1 where a row needs none).
         if (j > 0 && __any_sync(0xffffffffu, need && m_used != -INFINITY)) {
           // O holds P_{0..j-1} V: wait for the last product before rescaling it in place.
-          if (!mbar_wait(&pv_done[(G - 1) & 1], ((G - 1) >> 1) & 1, a.status)) goto done;
+          if (!mbar_wait(&pv_done[(G - 1) % NS], ((G - 1) / NS) & 1, a.status)) goto done;
           tc_fence_after();
 #pragma unroll 1
           for (int c = 0; c < DV; c += 32) {
@@ -448,7 +465,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         l_sum += ps.x + ps.y;
         tmem_st_wait();
         tc_fence_before();
-        mbar_arrive(&p_full[G & 1]);
+        mbar_arrive(&p_full[G % NS]);
       }
       // ---- epilogue: O / l, optional gate, bf16 rows. The gate rows (in L2 by now) are read while the last product
       // completes; without visible keys the output is 0 and needs no gate.
@@ -483,7 +500,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         }
         if (n > 0) {
           const uint32_t G = g + n - 1;
-          if (!mbar_wait(&pv_done[G & 1], (G >> 1) & 1, a.status)) goto done;
+          if (!mbar_wait(&pv_done[G % NS], (G / NS) & 1, a.status)) goto done;
           tc_fence_after();
         }
         const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
@@ -535,7 +552,7 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         for (int e = 0; e < GC / 8; ++e) g4[e] = grow ? load_gate16(grow + 8 * e) : make_uint4(0, 0, 0, 0);
         if (n > 0) {
           const uint32_t G = g + n - 1;
-          if (!mbar_wait(&pv_done[G & 1], (G >> 1) & 1, a.status)) goto done;
+          if (!mbar_wait(&pv_done[G % NS], (G / NS) & 1, a.status)) goto done;
           tc_fence_after();
         }
         const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
