@@ -104,22 +104,6 @@ KD_DEVICE float fast_exp2(float x) {
   return y;
 }
 
-// Paired float32 arithmetic (sm_100 f32x2 instructions: one issue slot for two lanes' worth of values).
-KD_DEVICE float2 fma2(float2 a, float2 b, float2 c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)),
-        "l"(*reinterpret_cast<uint64_t*>(&c)));
-  return *reinterpret_cast<float2*>(&d);
-}
-KD_DEVICE float2 add2(float2 a, float2 b) {
-  uint64_t d;
-  asm("add.rn.f32x2 %0, %1, %2;"
-      : "=l"(d)
-      : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
-  return *reinterpret_cast<float2*>(&d);
-}
 // max(a, b, c) in one instruction.
 KD_DEVICE float max3(float a, float b, float c) {
   float d;

@@ -32,6 +32,7 @@ constexpr int THREADS = 64 + EPI_GROUPS * 128;
 constexpr int OUT_BOX_COLS = 64;
 constexpr int OUT_BOX_BYTES = 32 * OUT_BOX_COLS * 2;
 constexpr int NORM_BYTES = 2 * 256 * 2;  // the QKV epilogue's q and k norm weights (bf16, head_dim <= 256)
+constexpr int NORM_F32_HD = 128;         // up to this head_dim they are stored as float multipliers instead
 
 // The pipeline of one CTA. Single: a 128 x 256 tile per CTA, A (128 rows) and B (256 rows) per stage. Pair (a
 // cluster of two CTAs, one cta_group::2 MMA over 256 x 256): each CTA stages its 128 rows of A and its 128 rows of B,
@@ -95,10 +96,15 @@ KD_DEVICE void load16(const Args& a, uint32_t taddr, int col, float sa, float (&
 template <bool FP8>
 KD_DEVICE void to_bf16_16(const Args& a, const uint32_t (&r)[16], int col, float sa, float (&x)[16]) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    float v = __uint_as_float(r[j]);
-    if constexpr (FP8) v = v * sa * a.scale_b[col + j];
-    x[j] = bf16_round(v);
+  for (int j = 0; j < 16; j += 2) {
+    float v0 = __uint_as_float(r[j]), v1 = __uint_as_float(r[j + 1]);
+    if constexpr (FP8) {
+      v0 = v0 * sa * a.scale_b[col + j];
+      v1 = v1 * sa * a.scale_b[col + j + 1];
+    }
+    const float2 b = bf16_round2(v0, v1);
+    x[j] = b.x;
+    x[j + 1] = b.y;
   }
 }
 
@@ -110,11 +116,24 @@ KD_DEVICE void store16(__nv_bfloat16* dst, const float (&x)[16]) {
   reinterpret_cast<uint4*>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
 }
 
-// The norm multipliers of 16 consecutive head dims (none, w or 1 + w), from two 16-byte loads (shared memory).
-KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
+// The norm multipliers of 16 consecutive head dims (none, w or 1 + w) from shared memory: for head_dim <= 128 the
+// kernel stored them as float (four 16-byte loads), for wider heads as the bf16 weights (two loads, then 1 + w).
+KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, int hd, float (&m)[16]) {
   if (mode != KD_NORM_WEIGHT && mode != KD_NORM_ONE_PLUS) {
 #pragma unroll
     for (int j = 0; j < 16; ++j) m[j] = 1.0f;
+    return;
+  }
+  if (hd <= NORM_F32_HD) {
+    const float4* f = reinterpret_cast<const float4*>(reinterpret_cast<const float*>(w) + d);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 v = f[q];
+      m[4 * q] = v.x;
+      m[4 * q + 1] = v.y;
+      m[4 * q + 2] = v.z;
+      m[4 * q + 3] = v.w;
+    }
     return;
   }
   const uint4 lo = *reinterpret_cast<const uint4*>(w + d);
@@ -128,6 +147,20 @@ KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
   }
 }
 
+// This lane's 16 values as bf16 into row `lane` of a 32-row x 16-column staging segment (1 KB, 32-byte rows) in the
+// TMA 32-byte swizzle: row i's 16-byte half p at i * 32 + ((p ^ (i / 4 % 2)) << 4), conflict-free for a row per lane.
+KD_DEVICE void put16(uint8_t* seg, int lane, const float (&x)[16]) {
+  uint32_t p[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) p[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
+  const int sw = (lane >> 2) & 1;
+  *reinterpret_cast<uint4*>(seg + lane * 32 + (sw << 4)) = make_uint4(p[0], p[1], p[2], p[3]);
+  *reinterpret_cast<uint4*>(seg + lane * 32 + ((sw ^ 1) << 4)) = make_uint4(p[4], p[5], p[6], p[7]);
+}
+
+// Waits until at most 3 of this thread's bulk stores still read shared memory.
+KD_DEVICE void bulk_wait_read_3() { asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); }
+
 // One row's heads inside the 256 columns [n0, n0 + 256) of the QKV projection: per-head RMSNorm over head_dim, then
 // rotate-half RoPE on the first `rot` dims (q, k); Gemma's weightless v norm; gate and plain v copied. Two passes
 // over tensor memory: the sum of squares, then the normalized, rotated head in 16-column pieces (a piece below rot / 2
@@ -135,13 +168,18 @@ KD_DEVICE void norm16(const __nv_bfloat16* w, int mode, int d, float (&m)[16]) {
 // group takes all of a 256-wide head). Each step issues its tensor-memory loads, its rotary factors (the per-pack
 // table `cs`, [rot / 2][M]: a warp's lanes read consecutive rows, one coalesced line per pair index) and its norm
 // weights (a shared-memory copy: q_norm then k_norm) before waiting on any of them, so their latencies overlap.
+// Outputs leave by TMA stores of 16-column pieces of the warp's 32 rows, staged in a ring of four 1 KB segments of
+// the warp's box (`nseg` counts the pieces the warp has stored): the tensor copy writes whole 32-byte row pieces,
+// where a row per lane would issue 32 scattered 16-byte stores per instruction. Rows past M are clipped by the copy.
 template <bool FP8>
-KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, float sa, int group,
-                            const __nv_bfloat16* norm_s) {
+KD_DEVICE void qkv_epilogue(const Args& a, int n0, uint32_t t_row, float sa, int group, const __nv_bfloat16* norm_s,
+                            uint8_t* box, int row0, int lane, uint32_t& nseg, const CUtensorMap* map_q,
+                            const CUtensorMap* map_g, const CUtensorMap* map_k, const CUtensorMap* map_v) {
   const Qkv& g = a.qkv;
   const int hd = g.hd;
   const int q_cols = g.hq * hd * (g.gated ? 2 : 1);
   const int k_end = q_cols + g.hkv * hd;
+  const int row = row0 + lane;
   const int crow = row < a.M ? row : a.M - 1;  // rows past M compute (warp-collective loads) but store nothing
   const uint32_t* cs = g.cs + crow;
   const int half = g.rot / 2;
@@ -167,15 +205,26 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
       head = (c0 - k_end) / hd;
       kind = 3;
     }
-    __nv_bfloat16* dst = kind == 0   ? g.q + ((int64_t)row * g.hq + head) * hd
-                         : kind == 1 ? g.gate + ((int64_t)row * g.hq + head) * hd
-                         : kind == 2 ? g.k + ((int64_t)row * g.hkv + head) * hd
-                                     : g.v + ((int64_t)row * g.hkv + head) * hd;
+    const CUtensorMap* map = kind == 0 ? map_q : kind == 1 ? map_g : kind == 2 ? map_k : map_v;
+    // 16 columns of the warp's 32 rows to columns [col, col + 16) of their heads
+    auto emit = [&](int col, const float (&x)[16]) {
+      uint8_t* seg = box + (nseg & 3) * 1024;
+      if (lane == 0) bulk_wait_read_3();  // the store that last read this segment is done
+      __syncwarp();
+      put16(seg, lane, x);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(map, seg, head * hd + col, row0);
+        bulk_commit();
+      }
+      ++nseg;
+    };
     const bool normed = kind == 0 || kind == 2 || (kind == 3 && g.v_mode >= 0);
     const bool rotated = kind == 0 || kind == 2;
     float inv = 1.0f;
     if (normed) {
-      float ss0 = 0.f, ss1 = 0.f;
+      float2 ss0 = make_float2(0.f, 0.f), ss1 = make_float2(0.f, 0.f);
       for (int d = 0; d < hd; d += 32) {
         uint32_t r0[16], r1[16];
         tmem_ld16(th + d, r0);
@@ -186,12 +235,13 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
         to_bf16_16<FP8>(a, r0, c0 + d, sa, x);
         to_bf16_16<FP8>(a, r1, c0 + d + 16, sa, y);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) {
-          ss0 = fmaf(x[j], x[j], ss0);
-          ss1 = fmaf(y[j], y[j], ss1);
+        for (int j = 0; j < 16; j += 2) {
+          const float2 x2 = make_float2(x[j], x[j + 1]), y2 = make_float2(y[j], y[j + 1]);
+          ss0 = fma2(x2, x2, ss0);
+          ss1 = fma2(y2, y2, ss1);
         }
       }
-      inv = 1.0f / sqrtf((ss0 + ss1) / (float)hd + g.eps);
+      inv = 1.0f / sqrtf(((ss0.x + ss0.y) + (ss1.x + ss1.y)) / (float)hd + g.eps);
     }
     if (!rotated) {  // gate, v: pieces of 32 columns, normalized for Gemma's v
       for (int d = 0; d < hd; d += 32) {
@@ -204,20 +254,26 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
         to_bf16_16<FP8>(a, r0, c0 + d, sa, x);
         to_bf16_16<FP8>(a, r1, c0 + d + 16, sa, y);
         if (normed) {
+          const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            x[j] *= inv;
-            y[j] *= inv;
+          for (int j = 0; j < 16; j += 2) {
+            const float2 xs = mul2(make_float2(x[j], x[j + 1]), inv2), ys = mul2(make_float2(y[j], y[j + 1]), inv2);
+            x[j] = xs.x;
+            x[j + 1] = xs.y;
+            y[j] = ys.x;
+            y[j + 1] = ys.y;
           }
         }
-        if (row < a.M) {
-          store16(dst + d, x);
-          store16(dst + d + 16, y);
-        }
+        emit(d, x);
+        emit(d + 16, y);
       }
       continue;
     }
-    const __nv_bfloat16* w = norm_s + (kind == 0 ? 0 : hd);
+    // this head's norm multipliers: float for head_dim <= 128, else the bf16 weights
+    const __nv_bfloat16* w = hd <= NORM_F32_HD
+                                 ? reinterpret_cast<const __nv_bfloat16*>(reinterpret_cast<const float*>(norm_s) +
+                                                                          (kind == 0 ? 0 : hd))
+                                 : norm_s + (kind == 0 ? 0 : hd);
     // rotation pairs: the piece at d < rot / 2 with its partner at d + rot / 2
     for (int d = 0; d < half; d += 16) {
       uint32_t rx[16], ry[16], f[16];
@@ -226,46 +282,54 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
 #pragma unroll
       for (int j = 0; j < 16; ++j) f[j] = cs[(int64_t)(d + j) * a.M];
       float mx[16], my[16];
-      norm16(w, g.qk_mode, d, mx);
-      norm16(w, g.qk_mode, d + half, my);
+      norm16(w, g.qk_mode, d, hd, mx);
+      norm16(w, g.qk_mode, d + half, hd, my);
       tmem_ld_wait_regs(rx);
       tmem_ld_wait_regs(ry);
       float x[16], y[16];
       to_bf16_16<FP8>(a, rx, c0 + d, sa, x);
       to_bf16_16<FP8>(a, ry, c0 + d + half, sa, y);
       float ox[16], oy[16];
+      const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        float xn = (x[j] * inv) * mx[j];
-        float yn = (y[j] * inv) * my[j];
+      for (int j = 0; j < 16; j += 2) {  // two rotation pairs at a time, on paired float instructions
+        float2 xn = mul2(mul2(make_float2(x[j], x[j + 1]), inv2), make_float2(mx[j], mx[j + 1]));
+        float2 yn = mul2(mul2(make_float2(y[j], y[j + 1]), inv2), make_float2(my[j], my[j + 1]));
         if (g.gated) {  // Qwen: the norm is its own op (rounded), RoPE another
-          xn = bf16_round(xn);
-          yn = bf16_round(yn);
+          xn = bf16_round2(xn.x, xn.y);
+          yn = bf16_round2(yn.x, yn.y);
         }
-        const float2 c_s = unpack_bf16x2(f[j]);  // cos and sin of pair d + j (the same for d + j + half)
-        ox[j] = xn * c_s.x - yn * c_s.y;
-        oy[j] = yn * c_s.x + xn * c_s.y;
+        // cos and sin of pairs d + j, d + j + 1 (the same for their partners rot / 2 further on)
+        const float2 c0s = unpack_bf16x2(f[j]), c1s = unpack_bf16x2(f[j + 1]);
+        const float2 cc = make_float2(c0s.x, c1s.x), sn = make_float2(c0s.y, c1s.y);
+        const float2 o1 = fma2(xn, cc, mul2(yn, make_float2(-sn.x, -sn.y)));  // x cos - y sin
+        const float2 o2 = fma2(yn, cc, mul2(xn, sn));                         // y cos + x sin
+        ox[j] = o1.x;
+        ox[j + 1] = o1.y;
+        oy[j] = o2.x;
+        oy[j + 1] = o2.y;
       }
-      if (row < a.M) {
-        store16(dst + d, ox);
-        store16(dst + d + half, oy);
-      }
+      emit(d, ox);
+      emit(d + half, oy);
     }
     // the unrotated rest, pieces of 16 columns
     for (int d = g.rot; d < hd; d += 16) {
       uint32_t r[16];
       tmem_ld16(th + d, r);
       float m[16];
-      norm16(w, g.qk_mode, d, m);
+      norm16(w, g.qk_mode, d, hd, m);
       tmem_ld_wait_regs(r);
       float x[16];
       to_bf16_16<FP8>(a, r, c0 + d, sa, x);
+      const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-      for (int j = 0; j < 16; ++j) {
-        x[j] = (x[j] * inv) * m[j];
-        if (g.gated) x[j] = bf16_round(x[j]);
+      for (int j = 0; j < 16; j += 2) {
+        float2 xn = mul2(mul2(make_float2(x[j], x[j + 1]), inv2), make_float2(m[j], m[j + 1]));
+        if (g.gated) xn = bf16_round2(xn.x, xn.y);
+        x[j] = xn.x;
+        x[j + 1] = xn.y;
       }
-      if (row < a.M) store16(dst + d, x);
+      emit(d, x);
     }
   }
 }
@@ -273,7 +337,8 @@ KD_DEVICE void qkv_epilogue(const Args& a, int row, int n0, uint32_t t_row, floa
 template <int EPI, bool FP8, bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b,
-                const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r, Args args) {
+                const __grid_constant__ CUtensorMap map_c, const __grid_constant__ CUtensorMap map_r,
+                const __grid_constant__ CUtensorMap map_k, const __grid_constant__ CUtensorMap map_v, Args args) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   using P = Pipe<PAIR>;
@@ -290,9 +355,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   if constexpr (EPI == KD_EPI_QKV) {  // q / k norm weights into shared memory: the epilogue reads them per head piece
     const int hd = args.qkv.hd;
     const bool weighted = args.qkv.qk_mode == KD_NORM_WEIGHT || args.qkv.qk_mode == KD_NORM_ONE_PLUS;
-    for (int i = threadIdx.x; weighted && i < 2 * hd / 8; i += THREADS) {
-      const __nv_bfloat16* src = i < hd / 8 ? args.qkv.q_norm + 8 * i : args.qkv.k_norm + 8 * (i - hd / 8);
-      reinterpret_cast<uint4*>(norm_s)[i] = *reinterpret_cast<const uint4*>(src);
+    if (hd <= NORM_F32_HD) {  // float multipliers (w or 1 + w, as the reference forms them in float)
+      for (int i = threadIdx.x; weighted && i < 2 * hd; i += THREADS) {
+        const float w = __bfloat162float(i < hd ? args.qkv.q_norm[i] : args.qkv.k_norm[i - hd]);
+        reinterpret_cast<float*>(norm_s)[i] = args.qkv.qk_mode == KD_NORM_ONE_PLUS ? 1.0f + w : w;
+      }
+    } else {
+      for (int i = threadIdx.x; weighted && i < 2 * hd / 8; i += THREADS) {
+        const __nv_bfloat16* src = i < hd / 8 ? args.qkv.q_norm + 8 * i : args.qkv.k_norm + 8 * (i - hd / 8);
+        reinterpret_cast<uint4*>(norm_s)[i] = *reinterpret_cast<const uint4*>(src);
+      }
     }
   }
 
@@ -430,6 +502,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* box = out_stage + (warp - 2) * OUT_BOX_BYTES;  // this warp's output staging box
     uint64_t* my_res = &res_bar[warp - 2];
     uint32_t res_phase = 0;
+    uint32_t qkv_seg = 0;  // QKV: the 16-column pieces this warp has stored (its staging ring position)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
@@ -442,7 +515,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       float sa = 1.0f;
       if constexpr (FP8) sa = (row < args.M) ? args.scale_a[row] : 0.0f;
       if constexpr (EPI == KD_EPI_QKV) {
-        qkv_epilogue<FP8>(args, row, n0, t_row, sa, group, norm_s);
+        // QKV: map_c is q, map_r the gate
+        qkv_epilogue<FP8>(args, n0, t_row, sa, group, norm_s, box, m0 + quarter * 32, lane, qkv_seg, &map_c, &map_r,
+                          &map_k, &map_v);
       } else {
         // Output through this warp's staging box and TMA stores: 64-column chunks of the warp's 32 rows, written
         // into 128-byte swizzled smem rows (conflict-free: 8 consecutive rows cover all bank groups), then one bulk
@@ -567,7 +642,7 @@ done:
 
 template <int EPI, bool FP8, bool PAIR>
 int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const CUtensorMap& mr,
-           const Args& args, cudaStream_t stream) {
+           const CUtensorMap& mk, const CUtensorMap& mv, const Args& args, cudaStream_t stream) {
   using P = Pipe<PAIR>;
   auto kernel = gemm_kernel<EPI, FP8, PAIR>;
   static bool configured[64] = {false};
@@ -584,7 +659,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, 
   const int tiles = m_tiles * n_tiles;
   if constexpr (!PAIR) {
     const int grid = tiles < num_sms(dev) ? tiles : num_sms(dev);
-    kernel<<<grid, THREADS, P::SMEM, stream>>>(ma, mb, mc, mr, args);
+    kernel<<<grid, THREADS, P::SMEM, stream>>>(ma, mb, mc, mr, mk, mv, args);
   } else {
     const int pairs = num_sms(dev) / 2;
     const int grid = 2 * (tiles < pairs ? tiles : pairs);
@@ -600,7 +675,7 @@ int launch(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, 
     attr[0].val.clusterDim.z = 1;
     config.attrs = attr;
     config.numAttrs = 1;
-    cudaError_t e = cudaLaunchKernelEx(&config, kernel, ma, mb, mc, mr, args);
+    cudaError_t e = cudaLaunchKernelEx(&config, kernel, ma, mb, mc, mr, mk, mv, args);
     if (e != cudaSuccess) return record_cuda_error(e, "gemm: cluster launch");
   }
   return record_cuda_error(cudaGetLastError(), "gemm: launch");
@@ -654,9 +729,19 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
   args.status = status;
   args.qkv = qkv ? *qkv : gemm::Qkv{};
 
-  // output (and residual) boxes for the TMA-store epilogue: 64 columns x 32 rows, 128-byte swizzle
-  CUtensorMap mc = ma, mr = ma;
-  if (epilogue != KD_EPI_QKV) {
+  // output (and residual) boxes for the TMA-store epilogue: 64 columns x 32 rows, 128-byte swizzle; the QKV epilogue
+  // stores 16 columns x 32 rows of q (mc), the gate (mr), k (mk) and v (mv), 32-byte swizzle
+  CUtensorMap mc = ma, mr = ma, mk = ma, mv = ma;
+  if (epilogue == KD_EPI_QKV) {
+    const auto bf = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    const auto sw = CU_TENSOR_MAP_SWIZZLE_32B;
+    const uint64_t qw = (uint64_t)qkv->hq * qkv->hd, kw = (uint64_t)qkv->hkv * qkv->hd;
+    rc = make_tma_2d(&mc, qkv->q, bf, 2, qw, M, qw, 16, 32, sw);
+    if (!rc && qkv->gated) rc = make_tma_2d(&mr, qkv->gate, bf, 2, qw, M, qw, 16, 32, sw);
+    if (!rc) rc = make_tma_2d(&mk, qkv->k, bf, 2, kw, M, kw, 16, 32, sw);
+    if (!rc) rc = make_tma_2d(&mv, qkv->v, bf, 2, kw, M, kw, 16, 32, sw);
+    if (rc) return rc;
+  } else {
     rc = make_tma_2d(&mc, C, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, n_out, M, ldc, gemm::OUT_BOX_COLS, 32,
                      CU_TENSOR_MAP_SWIZZLE_128B);
     if (!rc && epilogue == KD_EPI_RESIDUAL)
@@ -667,10 +752,10 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
 #define KD_GEMM_CASE(E)                                                                                \
   case E:                                                                                              \
     if (pair)                                                                                          \
-      return fp8 ? gemm::launch<E, true, true>(ma, mb, mc, mr, args, stream)                           \
-                 : gemm::launch<E, false, true>(ma, mb, mc, mr, args, stream);                         \
-    return fp8 ? gemm::launch<E, true, false>(ma, mb, mc, mr, args, stream)                            \
-               : gemm::launch<E, false, false>(ma, mb, mc, mr, args, stream);
+      return fp8 ? gemm::launch<E, true, true>(ma, mb, mc, mr, mk, mv, args, stream)                           \
+                 : gemm::launch<E, false, true>(ma, mb, mc, mr, mk, mv, args, stream);                         \
+    return fp8 ? gemm::launch<E, true, false>(ma, mb, mc, mr, mk, mv, args, stream)                            \
+               : gemm::launch<E, false, false>(ma, mb, mc, mr, mk, mv, args, stream);
   switch (epilogue) {
     KD_GEMM_CASE(KD_EPI_STORE)
     KD_GEMM_CASE(KD_EPI_RESIDUAL)
