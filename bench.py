@@ -408,14 +408,13 @@ def attention_flops(spec, lengths) -> float:
     return total
 
 
-#: DRAM bytes per launch from one ncu capture (dram__bytes_read.sum + dram__bytes_write.sum) on a smaller pack of the
-#: same configuration, scaled by the tokens a launch processes (Q, K, V and O each move once per launch).
-# DRAM bytes (read + write) per launch from ncu captures of the same kernels on an 8,192-token pack, scaled to the
-# bench's pack by tokens: attention (one layer's launch), and the GEMM family as the mean of one layer's four launches
-# (QKV + norm + RoPE, o_proj + residual, gate/up + SwiGLU, down + residual). Source: the profiles/ summaries.
-TRAFFIC_CAPTURES = {("qwen-0.8b", "attention"): (8192, 100.771584e6 + 14.428672e6),
-                    ("qwen-0.8b", "gemm"): (8192, (31.583744e6 + 47.450624e6 + 54.546432e6 + 0.334848e6 + 29.390336e6 +
-                                                   5.088512e6 + 73.422592e6 + 1.999104e6) / 4)}
+# DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum) from ncu captures of the same kernels on an
+# 8,192-token pack of the same configuration, scaled to the bench's pack by tokens (every operand moves once per
+# launch): attention (one layer's launch), and the GEMM family as the mean of one layer's four launches (QKV + norm +
+# RoPE, o_proj + residual, gate/up + SwiGLU, down + residual).
+TRAFFIC_CAPTURES = {("qwen-0.8b", "attention"): (8192, 100.882432e6 + 14.541056e6),
+                    ("qwen-0.8b", "gemm"): (8192, (31.640064e6 + 52.296192e6 + 54.548992e6 + 0.698880e6 + 29.403648e6 +
+                                                   6.410752e6 + 73.426176e6 + 3.883264e6) / 4)}
 
 
 def traffic(kernel: str, args, tokens: int) -> float | None:
