@@ -31,13 +31,19 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "packed prefill tokens/s"
 WORKLOADS = {
-    # config: (tokens per pack, length range, log-uniform)
+    # config: (tokens per pack, length range, log-uniform); the model is the configuration's name up to any "@"
     "tiny": (2048, (32, 512), False),
     "qwen-0.8b": (65536, (128, 8192), True),
     "qwen-4b": (32768, (256, 16384), True),
     "gemma-12b": (32768, (512, 32768), True),
     "gemma-31b": (32768, (256, 32768), True),
+    "gemma-31b@131k": (131072, (131072, 131072), False),  # one 131,072-token sequence
 }
+
+
+def model_of(config: str) -> str:
+    """The synthetic model a bench configuration runs."""
+    return config.split("@")[0]
 
 
 def parse() -> argparse.Namespace:
@@ -61,7 +67,7 @@ def workload(config: str, seed: int, tokens: int = 0) -> dict:
 
     default, (low, high), log = WORKLOADS[config]
     tokens = tokens or default
-    spec = CONFIGS[config]
+    spec = CONFIGS[model_of(config)]
     lengths = synthetic_lengths(tokens, low, high, seed, log_uniform=log)
     return synthetic_pack_arrays(lengths, spec.vocab, seed + 1, markers_per(spec))
 
@@ -88,7 +94,7 @@ def cpu_sample_rate(config: str, seconds: float, fp8: bool = False) -> dict:
     import oracle
     from karpo_decision_b200.synthetic import CONFIGS, numpy_weights, synthetic_lengths, synthetic_pack_arrays
 
-    spec = CONFIGS[config]
+    spec = CONFIGS[model_of(config)]
     if config not in _CPU_WEIGHTS:  # drawn once per process: a full-size draw takes seconds
         _CPU_WEIGHTS[config] = numpy_weights(spec, 0)
     weights = _CPU_WEIGHTS[config]
@@ -146,7 +152,7 @@ def config_block(args: argparse.Namespace, world: int) -> dict:
     tokens = args.tokens or tokens
     from karpo_decision_b200.synthetic import CONFIGS
 
-    lo, hi = markers_per(CONFIGS[args.config])
+    lo, hi = markers_per(CONFIGS[model_of(args.config)])
     return {"workload": f"{args.config} packed prefill, packs of {tokens} tokens, lengths "
                         f"{'log-uniform' if log else 'uniform'} [{low},{high}], {lo}-{hi} markers/sequence, causal"
                         + (", FP8 projections" if args.fp8 else ""),
@@ -233,7 +239,7 @@ def run_ours(args: argparse.Namespace) -> None:
     from karpo_decision_b200 import Packed, Readout, from_arrays, ops, profile
     from karpo_decision_b200.synthetic import CONFIGS, device_weights
 
-    spec = CONFIGS[args.config]
+    spec = CONFIGS[model_of(args.config)]
     weights = device_weights(spec, 0, dev)
     model = Packed(spec, weights, dev, fp8=args.fp8)
     head = Readout(weights["readout"].float(), spec.logit_cap, dev)
@@ -368,7 +374,7 @@ def request_latency(model, head, args, dev, n: int) -> dict:
     from karpo_decision_b200.graphs import Graphs
     from karpo_decision_b200.synthetic import CONFIGS, synthetic_lengths, synthetic_pack_arrays
 
-    spec = CONFIGS[args.config]
+    spec = CONFIGS[model_of(args.config)]
     _, (low, high), log = WORKLOADS[args.config]
     rng = np.random.default_rng(7)
     requests = []
