@@ -396,7 +396,8 @@ def request_latency(model, head, args, dev, n: int) -> dict:
             times.append((time.perf_counter() - t0) * 1000.0)
             del logits
         times = times[2:]
-        out[name] = {"p50_ms": round(float(np.median(times)), 3), "mean_ms": round(float(np.mean(times)), 3)}
+        out[name] = {"p50_ms": round(float(np.median(times)), 3), "p90_ms": round(float(np.percentile(times, 90)), 3),
+                     "mean_ms": round(float(np.mean(times)), 3)}
     graphs.release()
     return out
 

@@ -78,20 +78,6 @@ struct Args {
   Qkv qkv;
 };
 
-// 16 accumulator columns of one row as the projection's bf16 outputs (FP8: scaled first).
-template <bool FP8>
-KD_DEVICE void load16(const Args& a, uint32_t taddr, int col, float sa, float (&x)[16]) {
-  uint32_t r[16];
-  tmem_ld16(taddr, r);
-  tmem_ld_wait_regs(r);
-#pragma unroll
-  for (int j = 0; j < 16; ++j) {
-    float v = __uint_as_float(r[j]);
-    if constexpr (FP8) v = v * sa * a.scale_b[col + j];
-    x[j] = bf16_round(v);
-  }
-}
-
 // 16 accumulator columns of one row (raw tcgen05.ld registers) as the projection's bf16 outputs (FP8: scaled first).
 template <bool FP8>
 KD_DEVICE void to_bf16_16(const Args& a, const uint32_t (&r)[16], int col, float sa, float (&x)[16]) {
@@ -106,14 +92,6 @@ KD_DEVICE void to_bf16_16(const Args& a, const uint32_t (&r)[16], int col, float
     x[j] = b.x;
     x[j + 1] = b.y;
   }
-}
-
-KD_DEVICE void store16(__nv_bfloat16* dst, const float (&x)[16]) {
-  uint32_t p[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) p[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
-  reinterpret_cast<uint4*>(dst)[0] = make_uint4(p[0], p[1], p[2], p[3]);
-  reinterpret_cast<uint4*>(dst)[1] = make_uint4(p[4], p[5], p[6], p[7]);
 }
 
 // The norm multipliers of 16 consecutive head dims (none, w or 1 + w) from shared memory: for head_dim <= 128 the

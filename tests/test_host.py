@@ -198,3 +198,16 @@ def test_image_plan_matches_oracle_and_refuses_what_the_reference_refuses():
     long[0:17] = 99
     with pytest.raises(ValueError):
         image_plan(long, arrays["cu"].tolist(), arrays["segment_ids"], arrays["seqpos"], 99, 16, torch.device("cpu"))
+
+
+def test_smoke_packs_pass_the_host_plan():
+    """The round-end smoke forward's packs satisfy the host planning rules the forward enforces before any kernel is
+    queued (a Gemma block's readout marker is its last token, one per block)."""
+    import __graft_entry__
+    from karpo_decision_b200.plan import marker_bounds
+
+    for spec, arrays in __graft_entry__.smoke_cases():
+        cu = np.asarray(arrays["cu"], dtype=np.int64)
+        assert len(arrays["markers"]) >= len(cu) - 1
+        if spec.family == "gemma":
+            marker_bounds(cu.tolist(), np.asarray(arrays["markers"]))
