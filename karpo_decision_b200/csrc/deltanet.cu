@@ -269,37 +269,35 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
         for (int i = 0; i < C::ROWS; ++i) S[i] *= gamma;
         gamma = 1.f;
       }
-      float kreg[C::ROWS];
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      // paired float instructions: two state rows per fma (S^T k, the rank-1 update and S^T q)
+      float2 kreg[C::ROWS / 2];
+      float2 acc[2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
       for (int i = 0; i < C::ROWS; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
-        kreg[i] = k4.x;
-        kreg[i + 1] = k4.y;
-        kreg[i + 2] = k4.z;
-        kreg[i + 3] = k4.w;
-        acc[0] = fmaf(S[i], k4.x, acc[0]);
-        acc[1] = fmaf(S[i + 1], k4.y, acc[1]);
-        acc[2] = fmaf(S[i + 2], k4.z, acc[2]);
-        acc[3] = fmaf(S[i + 3], k4.w, acc[3]);
+        kreg[i / 2] = make_float2(k4.x, k4.y);
+        kreg[i / 2 + 1] = make_float2(k4.z, k4.w);
+        acc[0] = fma2(make_float2(S[i], S[i + 1]), kreg[i / 2], acc[0]);
+        acc[1] = fma2(make_float2(S[i + 2], S[i + 3]), kreg[i / 2 + 1], acc[1]);
       }
-      const float kvm = column_sum<C::TPC>((acc[0] + acc[1]) + (acc[2] + acc[3]));
+      const float kvm = column_sum<C::TPC>((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
       const float delta = (v_s[r * DV + col] - gamma * kvm) * beta;  // S^T k of the decayed state = gamma (S/gamma)^T k
       const float dscaled = delta / gamma;
-      float o[4] = {0.f, 0.f, 0.f, 0.f};
+      const float2 d2 = make_float2(dscaled, dscaled);
+      float2 o[2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
       for (int i = 0; i < C::ROWS; i += 4) {
         const float4 q4 = *reinterpret_cast<const float4*>(qr + i);
-        S[i] = fmaf(kreg[i], dscaled, S[i]);
-        S[i + 1] = fmaf(kreg[i + 1], dscaled, S[i + 1]);
-        S[i + 2] = fmaf(kreg[i + 2], dscaled, S[i + 2]);
-        S[i + 3] = fmaf(kreg[i + 3], dscaled, S[i + 3]);
-        o[0] = fmaf(S[i], q4.x, o[0]);
-        o[1] = fmaf(S[i + 1], q4.y, o[1]);
-        o[2] = fmaf(S[i + 2], q4.z, o[2]);
-        o[3] = fmaf(S[i + 3], q4.w, o[3]);
+        const float2 s0 = fma2(kreg[i / 2], d2, make_float2(S[i], S[i + 1]));
+        const float2 s1 = fma2(kreg[i / 2 + 1], d2, make_float2(S[i + 2], S[i + 3]));
+        S[i] = s0.x;
+        S[i + 1] = s0.y;
+        S[i + 2] = s1.x;
+        S[i + 3] = s1.y;
+        o[0] = fma2(s0, make_float2(q4.x, q4.y), o[0]);
+        o[1] = fma2(s1, make_float2(q4.z, q4.w), o[1]);
       }
-      const float ov = column_sum<C::TPC>((o[0] + o[1]) + (o[2] + o[3]));
+      const float ov = column_sum<C::TPC>((o[0].x + o[0].y) + (o[1].x + o[1].y));
       if (part == 0) a.out[(c0 + r) * a.ldo + (int64_t)head * DV + col] = __float2bfloat16_rn(gamma * ov);
     }
   }
