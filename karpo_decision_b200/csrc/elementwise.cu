@@ -57,6 +57,28 @@ KD_DEVICE void norm_weights(const __nv_bfloat16* w, int mode, int col, float (&m
 // 1 / sqrt(mean(x^2) + eps) with IEEE-rounded sqrt and division.
 KD_DEVICE float inv_rms(float sumsq, int cols, float eps) { return 1.0f / sqrtf(sumsq / (float)cols + eps); }
 
+// x / s rounded to nearest, as the reference's float division, with r = RN(1 / s) formed once per row: one correction
+// step on the product (Markstein's theorem, IBM J. Res. Dev. 34(1), 1990): q0 = RN(x r), e = x - q0 s (exact in one
+// fma), q = RN(q0 + e r) is the correctly rounded quotient when r is the correctly rounded reciprocal.
+KD_DEVICE float div_by(float x, float s, float r) {
+  const float q0 = x * r;
+  return fmaf(fmaf(-q0, s, x), r, q0);
+}
+
+// Eight values x / s to e4m3, round to nearest even, saturating at +-448 (the reference's clamp to +-448 then cast;
+// NaN stays NaN), converted in pairs. A row whose scale is infinite (an infinite input) divides directly.
+KD_DEVICE uint2 quantize8(const float (&f)[8], float s, float r) {
+  uint32_t p[4];
+  const bool finite = isfinite(s);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    const float a = finite ? div_by(f[2 * k], s, r) : f[2 * k] / s;
+    const float b = finite ? div_by(f[2 * k + 1], s, r) : f[2 * k + 1] / s;
+    p[k] = __nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  }
+  return make_uint2(p[0] | (p[1] << 16), p[2] | (p[3] << 16));
+}
+
 // ------------------------------------------------------------------------------------------------ embedding
 
 __global__ void embed_kernel(const int64_t* __restrict__ ids, int64_t T, const __nv_bfloat16* __restrict__ table,
@@ -223,20 +245,148 @@ __global__ void rmsnorm_e4m3_kernel(const __nv_bfloat16* __restrict__ x, int64_t
   // torch on CUDA divides a tensor by a scalar as a multiply by the float32 reciprocal (the reference's
   // amax / E4M3_MAX), so the scale is formed the same way; the values divide by the scale exactly.
   const float s = fmaxf(amax, 1e-12f) * (1.0f / 448.0f);
+  const float rs = __frcp_rn(s);
   if (lane == 0) scale[row] = s;
   __nv_fp8_e4m3* qr = q + row * (int64_t)cols;
   for (int c = lane * 8; c < cols; c += 256) {
     float f[8], m[8];
     load8(xr + c, f);
-    if (mode >= 0) norm_weights(w, mode, c, m);
-    uint8_t b[8];
+    if (mode >= 0) {
+      norm_weights(w, mode, c, m);
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float yv = mode >= 0 ? bf16_round((f[i] * inv) * m[i]) : f[i];
-      const float v = fminf(fmaxf(yv / s, -448.0f), 448.0f);
-      b[i] = (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
+      for (int i = 0; i < 8; ++i) f[i] = bf16_round((f[i] * inv) * m[i]);
     }
-    *reinterpret_cast<uint2*>(qr + c) = *reinterpret_cast<uint2*>(b);
+    *reinterpret_cast<uint2*>(qr + c) = quantize8(f, s, rs);
+  }
+}
+
+// ---- wide rows: one row per 256-thread block, held in registers between the passes, so it is read from memory once
+// (a warp per row re-reads its row for each pass, and rows of several KB from many warps fall out of L1 and L2).
+constexpr int ROW_THREADS = 256;
+constexpr int ROW_PIECES = 12;   // 8-element pieces per thread: rows up to 12 * 256 * 8 = 24,576 columns
+constexpr int WIDE_COLS = 2048;  // from this width the norms take the block path
+
+KD_DEVICE void unpack8(const uint4& v, float (&f)[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float2 t = unpack_bf16x2(w[i]);
+    f[2 * i] = t.x;
+    f[2 * i + 1] = t.y;
+  }
+}
+
+// Block-wide sum and max: warp shuffles, then the eight warp results in a fixed tree (every thread gets the same).
+KD_DEVICE float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  __syncthreads();  // red may still be read by the block's previous reduction
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return ((red[0] + red[1]) + (red[2] + red[3])) + ((red[4] + red[5]) + (red[6] + red[7]));
+}
+KD_DEVICE float block_max(float v, float* red) {
+  v = warp_max(v);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return fmaxf(fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3])), fmaxf(fmaxf(red[4], red[5]), fmaxf(red[6], red[7])));
+}
+
+// This thread's pieces of a row: pieces threadIdx.x, threadIdx.x + 256, ... (zero past the row's end).
+template <int R>
+KD_DEVICE void load_row(const __nv_bfloat16* xr, int cols, uint4 (&v)[R]) {
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int c = (threadIdx.x + r * ROW_THREADS) * 8;
+    v[r] = c < cols ? *reinterpret_cast<const uint4*>(xr + c) : make_uint4(0, 0, 0, 0);
+  }
+}
+
+// 1 / rms of a row held by the block (each thread's pieces summed in order, then block_sum): the same value in
+// rmsnorm_row_kernel and rmsnorm_e4m3_row_kernel, so the fused norm + quantization equals the two separate ops.
+template <int R>
+KD_DEVICE float row_inv(const uint4 (&v)[R], int cols, float eps, float* red) {
+  float ss = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if ((threadIdx.x + r * ROW_THREADS) * 8 >= cols) break;
+    float f[8];
+    unpack8(v[r], f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+  }
+  return inv_rms(block_sum(ss, red), cols, eps);
+}
+
+template <int R>
+__global__ void __launch_bounds__(ROW_THREADS) rmsnorm_row_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                                                  const int64_t* __restrict__ rows_idx,
+                                                                  const __nv_bfloat16* __restrict__ w, int mode,
+                                                                  float eps, __nv_bfloat16* __restrict__ out,
+                                                                  int64_t ldo, int cols) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  const int64_t src_row = rows_idx ? rows_idx[row] : row;
+  uint4 v[R];
+  load_row(x + src_row * ldx, cols, v);
+  const float inv = row_inv(v, cols, eps, red);
+  __nv_bfloat16* orow = out + row * ldo;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int c = (threadIdx.x + r * ROW_THREADS) * 8;
+    if (c >= cols) break;
+    float f[8], m[8];
+    unpack8(v[r], f);
+    norm_weights(w, mode, c, m);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = (f[i] * inv) * m[i];
+    store8(orow + c, f);
+  }
+}
+
+// rmsnorm_e4m3_kernel for wide rows: the normed bf16 row is kept (packed) in registers for the scale and the cast.
+template <int R>
+__global__ void __launch_bounds__(ROW_THREADS) rmsnorm_e4m3_row_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                       int64_t ldx, const __nv_bfloat16* __restrict__ w,
+                                                                       int mode, float eps,
+                                                                       __nv_fp8_e4m3* __restrict__ q,
+                                                                       float* __restrict__ scale, int cols) {
+  __shared__ float red[8];
+  const int64_t row = blockIdx.x;
+  uint4 v[R];
+  load_row(x + row * ldx, cols, v);
+  float amax = 0.f;
+  const float inv = mode >= 0 ? row_inv(v, cols, eps, red) : 1.0f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int c = (threadIdx.x + r * ROW_THREADS) * 8;
+    if (c >= cols) break;
+    float f[8];
+    unpack8(v[r], f);
+    if (mode >= 0) {  // y = bf16(norm(x)), kept for the cast below
+      float m[8];
+      norm_weights(w, mode, c, m);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = (f[i] * inv) * m[i];
+      v[r] = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                        pack_bf16x2(f[6], f[7]));
+      unpack8(v[r], f);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(f[i]));
+  }
+  amax = block_max(amax, red);
+  const float s = fmaxf(amax, 1e-12f) * (1.0f / 448.0f);  // as rmsnorm_e4m3_kernel forms it
+  const float rs = __frcp_rn(s);
+  if (threadIdx.x == 0) scale[row] = s;
+  __nv_fp8_e4m3* qr = q + row * (int64_t)cols;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int c = (threadIdx.x + r * ROW_THREADS) * 8;
+    if (c >= cols) break;
+    float f[8];
+    unpack8(v[r], f);
+    *reinterpret_cast<uint2*>(qr + c) = quantize8(f, s, rs);
   }
 }
 
@@ -439,6 +589,18 @@ extern "C" int kd_rmsnorm(const void* x, int64_t ldx, const void* weight, int no
   if (rc) return rc;
   if (norm_mode < 0) return set_error(KD_ERR_ARGUMENT, "rmsnorm: norm_mode must be KD_NORM_*");
   if (ldx % 8 || ldo % 8 || ldx < cols || ldo < cols) return set_error(KD_ERR_ARGUMENT, "rmsnorm: bad strides");
+  if (cols >= ew::WIDE_COLS && cols <= ew::ROW_PIECES * ew::ROW_THREADS * 8 && rows <= 0x7fffffff) {
+    const int pieces = (cols / 8 + ew::ROW_THREADS - 1) / ew::ROW_THREADS;
+#define KD_ROW_CASE(R)                                                                                          \
+  if (pieces <= R) {                                                                                            \
+    ew::rmsnorm_row_kernel<R><<<(unsigned)rows, ew::ROW_THREADS, 0, stream>>>(                                  \
+        static_cast<const __nv_bfloat16*>(x), ldx, nullptr, static_cast<const __nv_bfloat16*>(weight), norm_mode, \
+        eps, static_cast<__nv_bfloat16*>(out), ldo, cols);                                                      \
+    return record_cuda_error(cudaGetLastError(), "rmsnorm: launch");                                            \
+  }
+    KD_ROW_CASE(2) KD_ROW_CASE(3) KD_ROW_CASE(4) KD_ROW_CASE(6) KD_ROW_CASE(8) KD_ROW_CASE(12)
+#undef KD_ROW_CASE
+  }
   ew::rmsnorm_kernel<<<blocks_for(rows), 32 * WARPS, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, nullptr, static_cast<const __nv_bfloat16*>(weight), norm_mode, eps,
       static_cast<__nv_bfloat16*>(out), ldo, rows, cols);
@@ -479,6 +641,18 @@ extern "C" int kd_rmsnorm_e4m3(const void* x, int64_t ldx, const void* weight, i
   int rc = check_norm(x, q, norm_mode, weight, cols, "rmsnorm_e4m3: null or unaligned x/q");
   if (rc) return rc;
   if (!scale || ldx % 8 || ldx < cols) return set_error(KD_ERR_ARGUMENT, "rmsnorm_e4m3: bad scale or ldx");
+  if (cols >= ew::WIDE_COLS && cols <= ew::ROW_PIECES * ew::ROW_THREADS * 8 && rows <= 0x7fffffff) {
+    const int pieces = (cols / 8 + ew::ROW_THREADS - 1) / ew::ROW_THREADS;
+#define KD_ROW_CASE(R)                                                                                       \
+  if (pieces <= R) {                                                                                         \
+    ew::rmsnorm_e4m3_row_kernel<R><<<(unsigned)rows, ew::ROW_THREADS, 0, stream>>>(                          \
+        static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(weight), norm_mode, eps, \
+        static_cast<__nv_fp8_e4m3*>(q), scale, cols);                                                        \
+    return record_cuda_error(cudaGetLastError(), "rmsnorm_e4m3: launch");                                    \
+  }
+    KD_ROW_CASE(2) KD_ROW_CASE(3) KD_ROW_CASE(4) KD_ROW_CASE(6) KD_ROW_CASE(8) KD_ROW_CASE(12)
+#undef KD_ROW_CASE
+  }
   ew::rmsnorm_e4m3_kernel<<<blocks_for(rows), 32 * WARPS, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), ldx, static_cast<const __nv_bfloat16*>(weight), norm_mode, eps,
       static_cast<__nv_fp8_e4m3*>(q), scale, rows, cols);

@@ -129,14 +129,52 @@ def test_add_rmsnorm_and_norm_add():
     assert np.abs(out.float().cpu().numpy() - want).max() <= 2 ** -7 * np.abs(want).max()
 
 
-def test_rmsnorm_e4m3_equals_norm_then_quantize():
+# every positive finite e4m3 value (bias 7, 3 mantissa bits, no infinities, 0x7F is NaN), ascending
+E4M3_POS = sorted({(m / 8.0) * 2.0 ** -6 if e == 0 else (1 + m / 8.0) * 2.0 ** (e - 7)
+                   for e in range(16) for m in range(8) if (e, m) != (15, 7)})
+
+
+@pytest.mark.parametrize("cols", [768, 2560, 5376, 21504])
+def test_rmsnorm_e4m3_equals_norm_then_quantize(cols):
+    """The fused norm + e4m3 cast equals the two ops, on the warp-per-row path (narrow rows) and the block-per-row
+    path (2,048 columns and wider), and the wide norm matches the oracle."""
     g = rng(7)
-    x = bf16(g.standard_normal((129, 768)))
-    w = bf16(1.0 + g.standard_normal(768) * 0.1)
+    x = bf16(g.standard_normal((129, cols)))
+    w = bf16(1.0 + g.standard_normal(cols) * 0.1)
     y = ops.rmsnorm(x, w, ops.NORM_WEIGHT, 1e-6)
     q1, s1 = ops.quantize_rows_e4m3(y)
     q2, s2 = ops.rmsnorm_e4m3(x, w, ops.NORM_WEIGHT, 1e-6)
     assert torch.equal(s1, s2) and torch.equal(q1.view(torch.uint8), q2.view(torch.uint8))
+    want = oracle.rms_norm(x.float().cpu().numpy(), w.float().cpu().numpy(), 1e-6, False)
+    assert np.abs(y.float().cpu().numpy() - want).max() <= 2 ** -8 * np.abs(want).max()
+    # the quantization alone (amax per row, x / scale) against the definition
+    xf = x.float()
+    sw = torch.clamp(xf.abs().amax(1), min=1e-12) * (1.0 / 448.0)
+    q3, s3 = ops.quantize_rows_e4m3(x)
+    assert torch.equal(s3, sw)
+    assert torch.equal(q3.view(torch.uint8), (xf / sw[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).view(torch.uint8))
+
+
+def test_quantize_rows_e4m3_near_rounding_midpoints():
+    """Rows built so that x / scale lands next to e4m3 rounding midpoints, over many scales (every mantissa pattern of
+    the row maximum, all-ones included): the cast equals torch's float division, clamp and cast bit for bit."""
+    g = rng(17)
+    rows, cols = 512, 1024
+    amax = torch.from_numpy(np.ldexp(1.0 + np.arange(rows) / 128.0, g.integers(-20, 20, rows))).float()
+    amax[0] = 2.0 - 2.0 ** -7  # the widest bf16 mantissa (all ones)
+    scale = amax * (1.0 / 448.0)
+    grid = torch.tensor([0.5 * (a + b) for a, b in zip(E4M3_POS[:-1], E4M3_POS[1:])], dtype=torch.float32)
+    mid = grid[torch.from_numpy(g.integers(0, len(grid), (rows, cols)))] * torch.from_numpy(
+        g.choice([-1.0, 1.0], (rows, cols))).float()
+    x = (mid * scale[:, None] * (1.0 + torch.from_numpy(g.uniform(-2e-3, 2e-3, (rows, cols))).float())).bfloat16()
+    x[:, 0] = amax.bfloat16()
+    x = x.to(DEV)
+    q, s = ops.quantize_rows_e4m3(x)
+    xf = x.float()
+    sw = torch.clamp(xf.abs().amax(1), min=1e-12) * (1.0 / 448.0)
+    assert torch.equal(s, sw)
+    want = (xf / sw[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(q.view(torch.uint8), want.view(torch.uint8))
 
 
 def test_embed_and_scaled_embed():
