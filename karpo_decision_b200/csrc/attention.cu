@@ -104,12 +104,6 @@ KD_DEVICE float fast_exp2(float x) {
   return y;
 }
 
-// max(a, b, c) in one instruction.
-KD_DEVICE float max3(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
 
 // The next work item: item `idx` in the order sequences (pack order) > query tiles of the sequence, from its last
 // (the most expensive when causal) to its first > query heads > value slices. (cs, cbase) is the caller's cursor: a

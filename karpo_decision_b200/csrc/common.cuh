@@ -379,6 +379,12 @@ KD_DEVICE float2 mul2(float2 a, float2 b) {
       : "l"(*reinterpret_cast<uint64_t*>(&a)), "l"(*reinterpret_cast<uint64_t*>(&b)));
   return *reinterpret_cast<float2*>(&d);
 }
+// max(a, b, c) in one instruction.
+KD_DEVICE float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
 KD_DEVICE float2 add2(float2 a, float2 b) {
   uint64_t d;
   asm("add.rn.f32x2 %0, %1, %2;"

@@ -108,21 +108,28 @@ def test_rmsnorm_matches_oracle(mode, one_plus):
     assert np.abs(got - want).max() <= 2 ** -8 * np.abs(want).max()
 
 
-def test_add_rmsnorm_and_norm_add():
+@pytest.mark.parametrize("cols", [512, 5376])
+def test_add_rmsnorm_and_norm_add(cols):
+    """Narrow and wide rows against the oracle."""
     g = rng(6)
-    h = bf16(g.standard_normal((64, 512)))
-    x = bf16(g.standard_normal((64, 512)))
-    w = bf16(g.standard_normal(512) * 0.1)
+    h = bf16(g.standard_normal((64, cols)))
+    x = bf16(g.standard_normal((64, cols)))
+    w = bf16(g.standard_normal(cols) * 0.1)
     hn, xn, wn = (t.float().cpu().numpy() for t in (h, x, w))
     h2 = h.clone()
     y = ops.add_rmsnorm(h2, x, w, ops.NORM_ONE_PLUS, 1e-6)
     s = oracle.bf16(hn + xn)
     assert np.array_equal(h2.float().cpu().numpy(), s)
     assert np.abs(y.float().cpu().numpy() - oracle.rms_norm(s, wn, 1e-6, True)).max() <= 2 ** -8 * 4
-    w1 = bf16(1.0 + g.standard_normal(512) * 0.1)
+    w1 = bf16(1.0 + g.standard_normal(cols) * 0.1)
     out = ops.norm_add(h, x, w1, ops.NORM_WEIGHT, 1e-6)
     want = hn + oracle.rms_norm(xn, w1.float().cpu().numpy(), 1e-6, False)
     assert np.abs(out.float().cpu().numpy() - want).max() <= 2 ** -7 * np.abs(want).max()
+    # the layer-end form: (h + bf16(norm(x))) * scalar
+    scalar = torch.tensor([0.75], device=DEV).bfloat16()
+    out2 = ops.norm_add(h, x, w1, ops.NORM_WEIGHT, 1e-6, scalar=scalar)
+    want2 = (hn + oracle.bf16(oracle.rms_norm(xn, w1.float().cpu().numpy(), 1e-6, False))) * 0.75
+    assert np.abs(out2.float().cpu().numpy() - want2).max() <= 2 ** -7 * np.abs(want2).max()
     scalar = bf16(np.array([0.875]))
     out = ops.norm_add(h, x, w1, ops.NORM_WEIGHT, 1e-6, scalar=scalar)
     want = (hn + oracle.bf16(oracle.rms_norm(xn, w1.float().cpu().numpy(), 1e-6, False))) * 0.875
@@ -137,7 +144,7 @@ E4M3_POS = sorted({(m / 8.0) * 2.0 ** -6 if e == 0 else (1 + m / 8.0) * 2.0 ** (
 @pytest.mark.parametrize("cols", [768, 2560, 5376, 21504])
 def test_rmsnorm_e4m3_equals_norm_then_quantize(cols):
     """The fused norm + e4m3 cast equals the two ops, on the warp-per-row path (narrow rows) and the block-per-row
-    path (2,048 columns and wider), and the wide norm matches the oracle."""
+    path (3,072 columns and wider), and the wide norm matches the oracle."""
     g = rng(7)
     x = bf16(g.standard_normal((129, cols)))
     w = bf16(1.0 + g.standard_normal(cols) * 0.1)
