@@ -312,20 +312,23 @@ KD_DEVICE void load_row(const __nv_bfloat16* xr, int cols, uint4 (&v)[R]) {
   }
 }
 
-// 1 / rms of a row held by the block (each thread's pieces summed in order, then block_sum): the same value in
-// rmsnorm_row_kernel and rmsnorm_e4m3_row_kernel, so the fused norm + quantization equals the two separate ops.
+// 1 / rms of a row held by the block (each thread's pieces summed in order, even and odd elements apart, then
+// block_sum): the same value in rmsnorm_row_kernel and rmsnorm_e4m3_row_kernel, so the fused norm + quantization
+// equals the two separate ops.
 template <int R>
 KD_DEVICE float row_inv(const uint4 (&v)[R], int cols, float eps, float* red) {
-  float ss = 0.f;
+  float2 ss = make_float2(0.f, 0.f);
 #pragma unroll
   for (int r = 0; r < R; ++r) {
     if ((threadIdx.x + r * ROW_THREADS) * 8 >= cols) break;
-    float f[8];
-    unpack8(v[r], f);
+    const uint32_t w[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
 #pragma unroll
-    for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    for (int i = 0; i < 4; ++i) {
+      const float2 t = unpack_bf16x2(w[i]);
+      ss = fma2(t, t, ss);
+    }
   }
-  return inv_rms(block_sum(ss, red), cols, eps);
+  return inv_rms(block_sum(ss.x + ss.y, red), cols, eps);
 }
 
 template <int R>
@@ -354,7 +357,8 @@ __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_row_kernel(const __nv_bfl
   }
 }
 
-// rmsnorm_e4m3_kernel for wide rows: the normed bf16 row is kept (packed) in registers for the scale and the cast.
+// rmsnorm_e4m3_kernel for wide rows: the normed bf16 row is kept (packed) in registers for the scale and the cast;
+// its maximum magnitude is taken on the packed pairs (exact for a maximum).
 template <int R>
 __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_e4m3_row_kernel(const __nv_bfloat16* __restrict__ x,
                                                                        int64_t ldx, const __nv_bfloat16* __restrict__ w,
@@ -365,18 +369,16 @@ __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_e4m3_row_kernel(const __n
   const int64_t row = blockIdx.x;
   uint4 v[R];
   load_row(x + row * ldx, cols, v);
-  float amax = 0.f;
-  const float inv = mode >= 0 ? row_inv(v, cols, eps, red) : 1.0f;
+  if (mode >= 0) {  // y = bf16(norm(x)), kept for the cast below
+    const float inv = row_inv(v, cols, eps, red);
+    const float2 inv2 = make_float2(inv, inv);
 #pragma unroll
-  for (int r = 0; r < R; ++r) {
-    const int c = (threadIdx.x + r * ROW_THREADS) * 8;
-    if (c >= cols) break;
-    float f[8];
-    unpack8(v[r], f);
-    if (mode >= 0) {  // y = bf16(norm(x)), kept for the cast below
-      float m[8];
+    for (int r = 0; r < R; ++r) {
+      const int c = (threadIdx.x + r * ROW_THREADS) * 8;
+      if (c >= cols) break;
+      float f[8], m[8];
+      unpack8(v[r], f);
       norm_weights(w, mode, c, m);
-      const float2 inv2 = make_float2(inv, inv);
       uint32_t pk[4];
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
@@ -384,12 +386,17 @@ __global__ void __launch_bounds__(ROW_THREADS) rmsnorm_e4m3_row_kernel(const __n
         pk[k] = pack_bf16x2(y.x, y.y);
       }
       v[r] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      unpack8(v[r], f);
     }
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) amax = max3(amax, fabsf(f[i]), fabsf(f[i + 1]));
   }
-  amax = block_max(amax, red);
+  __nv_bfloat162 mx2 = __floats2bfloat162_rn(0.f, 0.f);
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    if ((threadIdx.x + r * ROW_THREADS) * 8 >= cols) break;
+    const uint32_t wv[4] = {v[r].x, v[r].y, v[r].z, v[r].w};
+#pragma unroll
+    for (int k = 0; k < 4; ++k) mx2 = __hmax2(mx2, __habs2(*reinterpret_cast<const __nv_bfloat162*>(&wv[k])));
+  }
+  const float amax = block_max(fmaxf(__low2float(mx2), __high2float(mx2)), red);
   const float s = fmaxf(amax, 1e-12f) * (1.0f / 448.0f);  // as rmsnorm_e4m3_kernel forms it
   const float rs = __frcp_rn(s);
   if (threadIdx.x == 0) scale[row] = s;
