@@ -167,6 +167,81 @@ KD_DEVICE uint32_t gate_pair(uint32_t o, uint32_t g) {
   return pack_bf16x2(ov.x * r.x, ov.y * r.y);
 }
 
+// The epilogue of a 128-row tile, one warp's 32 rows: O / l, the optional output gate, bf16 rows. Through the warp's
+// 2 KB staging area (32 rows x 64 bytes: row i at 64 i, its 16-byte piece p at slot (p + i / 2) % 4, conflict-free
+// both for a row per lane and for 8 rows of 4 lanes): each lane writes its row's normalized bf16 values, then reads
+// back 4 pieces of 8 rows, multiplies them by the gate pieces it loaded (coalesced, two 32-column chunks ahead) and
+// stores 64 contiguous bytes per row. The gate rows (brought into L2 by the producer) are read before the wait on
+// `done` (the item's last O += P V); without visible keys (n == 0) the output is 0 and needs no gate.
+template <int DV>
+KD_DEVICE bool staged_epilogue(const Args& a, const Item& w, int n, int64_t col0, uint8_t* ws, int quarter, int lane,
+                               uint32_t o_addr, uint64_t* done, uint32_t parity, float l_sum) {
+  const bool gated = a.gate != nullptr && n > 0;
+  const int tr_row = lane >> 2, tr_piece = lane & 3;  // the transposed access: rows tr_row + 8 m, one piece
+  const int wrow0 = w.qs + quarter * 32;              // the warp's first row within the sequence
+  auto at = [&](int i, int p) -> uint4* {
+    return reinterpret_cast<uint4*>(ws + i * 64 + (((p + (i >> 1)) & 3) << 4));
+  };
+  constexpr int NCH = DV / 32;
+  uint4 g4[2][4];
+  auto load_gates = [&](int cc) {
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int row = wrow0 + tr_row + 8 * m;
+      g4[cc & 1][m] = row < w.lq ? load_gate16(a.gate + (int64_t)(w.q0 + row) * a.ldg + col0 + cc * 32 + tr_piece * 8)
+                                 : make_uint4(0, 0, 0, 0);
+    }
+  };
+  if (gated) {
+    load_gates(0);
+    if (NCH > 1) load_gates(1);
+  }
+  if (n > 0) {
+    if (!mbar_wait(done, parity, a.status)) return false;
+    tc_fence_after();
+  }
+  const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
+#pragma unroll
+  for (int cc = 0; cc < NCH; ++cc) {
+    {  // this row's 32 columns: bf16(o / l)
+      uint32_t t[32];
+      if (n > 0) {
+        tmem_ld32(o_addr + cc * 32, t);  // warp-collective
+        tmem_ld_wait_regs(t);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) t[e] = 0u;
+      }
+#pragma unroll
+      for (int pc = 0; pc < 4; ++pc) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          pk[e] = pack_bf16x2(__uint_as_float(t[8 * pc + 2 * e]) * inv, __uint_as_float(t[8 * pc + 2 * e + 1]) * inv);
+        *at(lane, pc) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+    }
+    __syncwarp();
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {  // 8 rows x 4 pieces out
+      const int row = wrow0 + tr_row + 8 * m;
+      uint4 x = *at(tr_row + 8 * m, tr_piece);
+      if (gated) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
+        const uint4 gq = g4[cc & 1][m];
+        x.x = gate_pair(x.x, gq.x);
+        x.y = gate_pair(x.y, gq.y);
+        x.z = gate_pair(x.z, gq.z);
+        x.w = gate_pair(x.w, gq.w);
+      }
+      if (row < w.lq)
+        *reinterpret_cast<uint4*>(a.out + (int64_t)(w.q0 + row) * a.ldo + col0 + cc * 32 + tr_piece * 8) = x;
+    }
+    if (gated && cc + 2 < NCH) load_gates(cc + 2);
+    __syncwarp();
+  }
+  return true;
+}
+
 // Brings a tile of a tensor into L2 ahead of its use.
 KD_DEVICE void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
@@ -451,76 +526,10 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
       const int64_t col0 = (int64_t)w.head * HD + w.slice * DV;
       constexpr int GC = DV < 128 ? DV : 128;  // gate columns held in registers at a time
       if constexpr (C::STAGED) {
-        // Through this warp's staging area (32 rows x 64 bytes: row i at 64 i, its 16-byte piece p at slot
-        // (p + i / 2) % 4, conflict-free both for a row per lane and for 8 rows of 4 lanes): each lane writes its
-        // row's normalized bf16 values, then reads back 4 pieces of 8 rows, multiplies them by the gate pieces it
-        // loaded (coalesced, two 32-column chunks ahead) and stores 64 contiguous bytes per row.
-        uint8_t* ws = s_epi + quarter * 2048;
-        const int tr_row = lane >> 2, tr_piece = lane & 3;  // the transposed access: rows tr_row + 8 m, one piece
-        const int wrow0 = w.qs + quarter * 32;              // the warp's first row within the sequence
-        auto at = [&](int i, int p) -> uint4* {
-          return reinterpret_cast<uint4*>(ws + i * 64 + (((p + (i >> 1)) & 3) << 4));
-        };
-        constexpr int NCH = DV / 32;
-        uint4 g4[2][4];
-        auto load_gates = [&](int cc) {
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const int row = wrow0 + tr_row + 8 * m;
-            g4[cc & 1][m] = row < w.lq ? load_gate16(a.gate + (int64_t)(w.q0 + row) * a.ldg + col0 + cc * 32 +
-                                                     tr_piece * 8)
-                                       : make_uint4(0, 0, 0, 0);
-          }
-        };
-        if (gated) {
-          load_gates(0);
-          if (NCH > 1) load_gates(1);
-        }
-        if (n > 0) {
-          const uint32_t G = g + n - 1;
-          if (!mbar_wait(&pv_done[G % NS], (G / NS) & 1, a.status)) goto done;
-          tc_fence_after();
-        }
-        const float inv = l_sum > 0.f ? 1.f / l_sum : 0.f;
-#pragma unroll
-        for (int cc = 0; cc < NCH; ++cc) {
-          {  // this row's 32 columns: bf16(o / l)
-            uint32_t t[32];
-            if (n > 0) {
-              tmem_ld32(lane_base + C::O_COL + cc * 32, t);  // warp-collective
-              tmem_ld_wait_regs(t);
-            } else {
-#pragma unroll
-              for (int e = 0; e < 32; ++e) t[e] = 0u;
-            }
-#pragma unroll
-            for (int pc = 0; pc < 4; ++pc) {
-              uint32_t pk[4];
-#pragma unroll
-              for (int e = 0; e < 4; ++e)
-                pk[e] = pack_bf16x2(__uint_as_float(t[8 * pc + 2 * e]) * inv,
-                                    __uint_as_float(t[8 * pc + 2 * e + 1]) * inv);
-              *at(lane, pc) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            }
-          }
-          __syncwarp();
-#pragma unroll
-          for (int m = 0; m < 4; ++m) {  // 8 rows x 4 pieces out
-            const int row = wrow0 + tr_row + 8 * m;
-            uint4 x = *at(tr_row + 8 * m, tr_piece);
-            if (gated) {  // Qwen's output gate: bf16(o) * sigmoid(gate), rounded once
-              const uint4 gq = g4[cc & 1][m];
-              x.x = gate_pair(x.x, gq.x);
-              x.y = gate_pair(x.y, gq.y);
-              x.z = gate_pair(x.z, gq.z);
-              x.w = gate_pair(x.w, gq.w);
-            }
-            if (row < w.lq)
-              *reinterpret_cast<uint4*>(a.out + (int64_t)(w.q0 + row) * a.ldo + col0 + cc * 32 + tr_piece * 8) = x;
-          }
-          if (gated && cc + 2 < NCH) load_gates(cc + 2);
-          __syncwarp();
-        }
+        const uint32_t gl = n > 0 ? g + n - 1 : 0;  // the item's last tile
+        if (!staged_epilogue<DV>(a, w, n, col0, s_epi + quarter * 2048, quarter, lane, lane_base + C::O_COL,
+                                 &pv_done[gl % NS], (gl / NS) & 1, l_sum))
+          goto done;
       } else {
         const int row = w.qs + r;
         const bool live = row < w.lq;

@@ -272,8 +272,10 @@ def attention_case(lengths, hq, hkv, hd, window, scale, gated=False, seed=10):
 
 
 @pytest.mark.parametrize("lengths", [[1], [7, 130, 64, 1, 300], [513], [128, 128]])
-@pytest.mark.parametrize("hd,hq,hkv", [(128, 16, 8), (64, 4, 2), (256, 4, 1), (512, 4, 1)])
+@pytest.mark.parametrize("hd,hq,hkv", [(128, 16, 8), (128, 8, 2), (128, 4, 4), (128, 6, 2), (64, 4, 2), (256, 4, 1),
+                                       (512, 4, 1)])
 def test_attention_causal_matches_oracle(lengths, hd, hq, hkv):
+    """Head dims 64-512; at 128, key/value groups of 1, 2, 3 and 4 query heads (the GQA head mapping)."""
     got, want = attention_case(lengths, hq, hkv, hd, (-1, 0), hd ** -0.5)
     # P is rounded to bf16 before the PV product (flash attention); outputs are O(1)
     assert np.abs(got - want).max() <= 2e-2
@@ -303,6 +305,33 @@ def test_attention_head512_windows_and_separate_key_bounds(window):
                                scale, window)
     want = oracle.attention_varlen(*(x.float().cpu().numpy() for x in (q, k, v)), cu_q, cu_k, scale, window)
     assert np.abs(got.float().cpu().numpy() - oracle.bf16(want).reshape(sum(lq), -1)).max() <= 3e-2
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 8), (4, 4)])
+@pytest.mark.parametrize("gated", [False, True])
+def test_attention_long_sequences(hq, hkv, gated):
+    """Many key tiles per query tile (running-maximum rescales) and several work items per persistent CTA, GQA and
+    MHA, with and without Qwen's output gate."""
+    got, want = attention_case([1500, 2100, 300, 1], hq, hkv, 128, (-1, 0), 128 ** -0.5, gated=gated, seed=21)
+    assert np.abs(got - want).max() <= 2e-2
+
+
+@pytest.mark.parametrize("window", [(-1, 0), (100, 0), (-1, -1)])
+def test_attention_head128_separate_key_bounds(window):
+    """Queries end-aligned to longer or shorter key spans at head dim 128 (8 query / 2 key-value heads), including a
+    query tile that sees no key at all (its output is 0)."""
+    g = rng(16)
+    lq, lk = [5, 300, 1, 300], [40, 300, 260, 100]  # the last one's first query tile sees no key
+    scale = 128 ** -0.5
+    q = bf16(g.standard_normal((sum(lq), 8, 128)))
+    k, v = (bf16(g.standard_normal((sum(lk), 2, 128))) for _ in range(2))
+    cu_q = np.concatenate([[0], np.cumsum(lq)]).astype(np.int32)
+    cu_k = np.concatenate([[0], np.cumsum(lk)]).astype(np.int32)
+    got = ops.attention_varlen(q, k, v, torch.from_numpy(cu_q).to(DEV), torch.from_numpy(cu_k).to(DEV), max(lq),
+                               scale, window)
+    want = oracle.attention_varlen(*(x.float().cpu().numpy() for x in (q, k, v)), cu_q, cu_k, scale, window)
+    want = np.nan_to_num(oracle.bf16(want).reshape(sum(lq), -1))
+    assert np.abs(got.float().cpu().numpy() - want).max() <= 2e-2
 
 
 def test_attention_output_gate():
