@@ -450,12 +450,16 @@ __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
         const uint32_t s_addr = lane_base + C::S_COL + (G % NS) * BN;
         float sv[BN];
 #pragma unroll
-        for (int c = 0; c < BN; c += 32) {
-          uint32_t t[32];
-          tmem_ld32(s_addr + c, t);
-          tmem_ld_wait_regs(t);
+        for (int c = 0; c < BN; c += 64) {  // two loads in flight, one wait
+          uint32_t t0[32], t1[32];
+          tmem_ld32(s_addr + c, t0);
+          tmem_ld32(s_addr + c + 32, t1);
+          tmem_ld_wait_regs(t0, t1);
 #pragma unroll
-          for (int e = 0; e < 32; ++e) sv[c + e] = __uint_as_float(t[e]);
+          for (int e = 0; e < 32; ++e) {
+            sv[c + e] = __uint_as_float(t0[e]);
+            sv[c + 32 + e] = __uint_as_float(t1[e]);
+          }
         }
         const int n0 = (w.first_tile + j) * BN;
         // Only tiles that cross the causal diagonal, the window's left edge or the sequence end need a mask; the
