@@ -211,3 +211,13 @@ def test_smoke_packs_pass_the_host_plan():
         assert len(arrays["markers"]) >= len(cu) - 1
         if spec.family == "gemma":
             marker_bounds(cu.tolist(), np.asarray(arrays["markers"]))
+
+
+def test_microbench_work_counts():
+    """The micro-benchmark's algorithmic work: visible query-key pairs under the varlen contract's windows."""
+    from karpo_decision_b200.microbench import parse_lengths, visible_pairs
+    assert visible_pairs([4], (-1, 0)) == 10           # causal: L(L+1)/2
+    assert visible_pairs([4], (1, 0)) == 1 + 2 + 2 + 2  # sliding window of 2
+    assert visible_pairs([3, 2], (-1, -1)) == 9 + 4     # bidirectional: L^2
+    assert visible_pairs([5], (0, 1)) == 2 + 2 + 2 + 2 + 1
+    assert sum(parse_lengths("mix:65536")) == 65536 and parse_lengths("8192,4096") == [8192, 4096]
