@@ -141,7 +141,7 @@ E4M3_POS = sorted({(m / 8.0) * 2.0 ** -6 if e == 0 else (1 + m / 8.0) * 2.0 ** (
                    for e in range(16) for m in range(8) if (e, m) != (15, 7)})
 
 
-@pytest.mark.parametrize("cols", [768, 2560, 5376, 21504])
+@pytest.mark.parametrize("cols", [768, 2560, 3072, 3840, 5376, 9728, 21504])
 def test_rmsnorm_e4m3_equals_norm_then_quantize(cols):
     """The fused norm + e4m3 cast equals the two ops, on the warp-per-row path (narrow rows) and the block-per-row
     path (3,072 columns and wider), and the wide norm matches the oracle."""
