@@ -3,6 +3,7 @@ Kernel profiles are captured on it, so that a capture holds one kernel at a smal
 
     python -m karpo_decision_b200.microbench attention --lengths 8192 --hq 16 --hkv 8 --hd 256 --window=1023,0
     python -m karpo_decision_b200.microbench gemm --m 8192 --n 6144 --k 1024 --fp8 --epilogue swiglu
+    python -m karpo_decision_b200.microbench qkv --lengths mix:8192 --k 1024 --hq 16 --hkv 8 --gate
     python -m karpo_decision_b200.microbench rmsnorm_e4m3 --rows 16384 --cols 5376
     python -m karpo_decision_b200.microbench delta_rule --lengths 8192,4096,2048,2048 --hk 16 --hv 32
 
@@ -91,6 +92,33 @@ def build(args: argparse.Namespace, dev: torch.device):
 
         return run, 2 * m * n * kk, "FLOP", {"m": m, "n": n, "k": kk, "fp8": bool(args.fp8),
                                              "epilogue": args.epilogue}
+    if op == "qkv":
+        # Qwen's fused projection: [q | gate] per head, k, v; q/k norms (1 + w) and RoPE over the full head in the
+        # epilogue; rows are the sequences of --lengths, K = --k
+        lengths = parse_lengths(args.lengths)
+        t, kk, hq, hkv, hd = sum(lengths), args.k, args.hq, args.hkv, args.hd
+        n = (hq * (2 if args.gate else 1) + 2 * hkv) * hd
+        a = bf16(g, t, kk, device=dev)
+        w = bf16(g, n, kk, device=dev, scale=kk ** -0.5)
+        q_norm, k_norm = (bf16(g, hd, device=dev, scale=0.1) for _ in range(2))
+        seqpos = torch.cat([torch.arange(x, dtype=torch.int64) for x in lengths]).to(dev)
+        inv_freq = (1e6 ** (-torch.arange(0, hd, 2, dtype=torch.float32) / hd)).to(dev)
+        cos, sin = ops.rope_table(inv_freq, max(lengths))
+        cs = ops.rope_gather(seqpos, cos, sin)
+        sa = sw = None
+        if args.fp8:
+            (a, sa), (w, sw) = ops.quantize_rows_e4m3(a), ops.quantize_rows_e4m3(w)
+        heads = (torch.empty(t, hq, hd, dtype=torch.bfloat16, device=dev),
+                 torch.empty(t, hkv, hd, dtype=torch.bfloat16, device=dev),
+                 torch.empty(t, hkv, hd, dtype=torch.bfloat16, device=dev),
+                 torch.empty(t, hq * hd, dtype=torch.bfloat16, device=dev) if args.gate else None)
+
+        def run():
+            ops.qkv_projection(a, w, seqpos, hq, hkv, hd, args.gate, q_norm, k_norm, ops.NORM_ONE_PLUS, -1, 1e-6, cs,
+                               hd, out=heads, scale_a=sa, scale_w=sw)
+
+        return run, 2 * t * n * kk, "FLOP", {"m": t, "n": n, "k": kk, "hq": hq, "hkv": hkv, "hd": hd,
+                                             "gate": bool(args.gate), "fp8": bool(args.fp8)}
     if op in ("rmsnorm", "rmsnorm_e4m3", "quantize", "norm_add"):
         rows, cols = args.rows, args.cols
         x = bf16(g, rows, cols, device=dev)
@@ -160,7 +188,7 @@ def build(args: argparse.Namespace, dev: torch.device):
 
 def main(argv: list[str] | None = None) -> dict:
     p = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    p.add_argument("op", choices=["attention", "gemm", "rmsnorm", "rmsnorm_e4m3", "quantize", "norm_add",
+    p.add_argument("op", choices=["attention", "gemm", "qkv", "rmsnorm", "rmsnorm_e4m3", "quantize", "norm_add",
                                   "delta_rule", "conv_silu", "gated_norm"])
     p.add_argument("--lengths", default="mix:8192")
     p.add_argument("--hq", type=int, default=16)
