@@ -190,10 +190,10 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
   const float dt_bias = __bfloat162float(a.dt_bias[head]);
   const int64_t kd = (int64_t)a.nk * DK;
 
-  float S[C::ROWS];  // this thread's rows of its column of S / gamma
+  float2 S[C::ROWS / 2];  // this thread's rows of its column of S / gamma, in pairs
 #pragma unroll
-  for (int i = 0; i < C::ROWS; ++i) S[i] = 0.f;
-  float gamma = 1.f;
+  for (int i = 0; i < C::ROWS / 2; ++i) S[i] = make_float2(0.f, 0.f);
+  float gamma = 1.f, inv_gamma = 1.f;
 
   // The next chunk's rows are fetched into registers while the current chunk is walked, then normalized into
   // shared memory: one warp per token row (q and k L2-normalized with eps 1e-6, q scaled by dk^-1/2).
@@ -266,9 +266,10 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
       gamma *= g_s[r];
       if (gamma < 0x1p-60f) {  // uniform over the CTA (one decay per head and token)
 #pragma unroll
-        for (int i = 0; i < C::ROWS; ++i) S[i] *= gamma;
+        for (int i = 0; i < C::ROWS / 2; ++i) S[i] = mul2(S[i], make_float2(gamma, gamma));
         gamma = 1.f;
       }
+      inv_gamma = 1.0f / gamma;  // off the chain from S^T k to the update
       // paired float instructions: two state rows per fma (S^T k, the rank-1 update and S^T q)
       float2 kreg[C::ROWS / 2];
       float2 acc[2] = {{0.f, 0.f}, {0.f, 0.f}};
@@ -277,23 +278,21 @@ __global__ void __launch_bounds__(Cfg<DK, DV>::THREADS) delta_rule_kernel(Args a
         const float4 k4 = *reinterpret_cast<const float4*>(kr + i);
         kreg[i / 2] = make_float2(k4.x, k4.y);
         kreg[i / 2 + 1] = make_float2(k4.z, k4.w);
-        acc[0] = fma2(make_float2(S[i], S[i + 1]), kreg[i / 2], acc[0]);
-        acc[1] = fma2(make_float2(S[i + 2], S[i + 3]), kreg[i / 2 + 1], acc[1]);
+        acc[0] = fma2(S[i / 2], kreg[i / 2], acc[0]);
+        acc[1] = fma2(S[i / 2 + 1], kreg[i / 2 + 1], acc[1]);
       }
       const float kvm = column_sum<C::TPC>((acc[0].x + acc[0].y) + (acc[1].x + acc[1].y));
       const float delta = (v_s[r * DV + col] - gamma * kvm) * beta;  // S^T k of the decayed state = gamma (S/gamma)^T k
-      const float dscaled = delta / gamma;
+      const float dscaled = delta * inv_gamma;
       const float2 d2 = make_float2(dscaled, dscaled);
       float2 o[2] = {{0.f, 0.f}, {0.f, 0.f}};
 #pragma unroll
       for (int i = 0; i < C::ROWS; i += 4) {
         const float4 q4 = *reinterpret_cast<const float4*>(qr + i);
-        const float2 s0 = fma2(kreg[i / 2], d2, make_float2(S[i], S[i + 1]));
-        const float2 s1 = fma2(kreg[i / 2 + 1], d2, make_float2(S[i + 2], S[i + 3]));
-        S[i] = s0.x;
-        S[i + 1] = s0.y;
-        S[i + 2] = s1.x;
-        S[i + 3] = s1.y;
+        const float2 s0 = fma2(kreg[i / 2], d2, S[i / 2]);
+        const float2 s1 = fma2(kreg[i / 2 + 1], d2, S[i / 2 + 1]);
+        S[i / 2] = s0;
+        S[i / 2 + 1] = s1;
         o[0] = fma2(s0, make_float2(q4.x, q4.y), o[0]);
         o[1] = fma2(s1, make_float2(q4.z, q4.w), o[1]);
       }
