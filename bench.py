@@ -325,6 +325,13 @@ def run_ours(args: argparse.Namespace) -> None:
                      "kd_gemm_fp8 + kd_qkv_projection_fp8", "bound": "tensor", "achieved": gemm_tf,
                      "ms_per_step": g_ms / args.steps, "traffic": traffic("gemm", args, tokens)},
         }
+        # Each family against its own dense peak: bf16 for attention and bf16 GEMMs; e4m3 GEMMs run at twice the bf16
+        # rate on tcgen05 (MEASURED_PEAKS.json holds no FP8 figure, so theirs is twice the measured bf16 one).
+        for k, v in kernels.items():
+            fp8_family = args.fp8 and k == "gemm"
+            v["peak"] = peaks[0] * (2.0 if fp8_family else 1.0)
+            v["peak_source"] = ("2 x " if fp8_family else "") + peaks[1]
+            v["frac"] = v["achieved"] / v["peak"] if v["achieved"] else None
         dominant = max(kernels, key=lambda k: kernels[k]["ms_per_step"])
         top = kernels[dominant]
         achieved = top["achieved"]
@@ -335,11 +342,10 @@ def run_ours(args: argparse.Namespace) -> None:
             "config": config_block(args, world),
             "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": launches,
-            "roofline": {"bound": "tensor", "kernel": top["kernel"], "achieved": achieved, "peak": peaks[0],
-                         "unit": "TFLOP/s", "frac": achieved / peaks[0] if achieved else None,
-                         "traffic": top["traffic"], "peak_source": peaks[1]},
-            "roofline_kernels": {k: {**v, "frac": v["achieved"] / peaks[0] if v["achieved"] else None}
-                                 for k, v in kernels.items()},
+            "roofline": {"bound": "tensor", "kernel": top["kernel"], "achieved": achieved, "peak": top["peak"],
+                         "unit": "TFLOP/s", "frac": top["frac"], "traffic": top["traffic"],
+                         "peak_source": top["peak_source"]},
+            "roofline_kernels": kernels,
             "kernel_shares": prof.shares(),
             "clocks": clocks.summary(),
         }
