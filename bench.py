@@ -374,10 +374,10 @@ def request_latency(model, head, args, dev, n: int) -> dict:
     """Per-request latency of single requests (one sequence each, length drawn from the configuration's range,
     1-4 questions): pinned host pack -> device -> forward -> readout -> host logits, device-synchronized wall time
     per request (the reference's latency definition, serve/engine.py:53-55, from the packed pass on), on the plain
-    path and on the CUDA-graph path (buckets of powers of two up to the longest request)."""
+    path and on the CUDA-graph path (the fine buckets up to the longest request)."""
     import torch
 
-    from karpo_decision_b200.graphs import Graphs
+    from karpo_decision_b200.graphs import Graphs, fine_buckets
     from karpo_decision_b200.synthetic import CONFIGS, synthetic_lengths, synthetic_pack_arrays
 
     spec = CONFIGS[model_of(args.config)]
@@ -388,8 +388,7 @@ def request_latency(model, head, args, dev, n: int) -> dict:
         length = synthetic_lengths(high, low, high, seed=int(rng.integers(1 << 30)), log_uniform=log)[0]
         requests.append(synthetic_pack_arrays([length], spec.vocab, seed=i, markers_per_seq=markers_per(spec)))
     longest = max(len(r["input_ids"]) for r in requests)
-    buckets = tuple(1 << k for k in range(7, max(8, int(np.ceil(np.log2(longest)))) + 1))
-    graphs = Graphs(model, buckets=buckets, max_sequences=1)
+    graphs = Graphs(model, buckets=fine_buckets(longest), max_sequences=1)
     out = {"requests": n, "lengths": f"one sequence each, {'log-uniform' if log else 'uniform'} [{low},{high}]"}
     for name, fwd in (("plain", model), ("graphs", graphs)):
         times = []

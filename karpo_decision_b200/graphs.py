@@ -27,8 +27,32 @@ from .packed import Packed
 
 #: Padding rows form sequences of at most this many tokens (their causal attention stays cheap).
 PAD_SEQUENCE = 256
-#: Default buckets: powers of two from 512 to 65,536 tokens.
-DEFAULT_BUCKETS = tuple(1 << k for k in range(9, 17))
+#: Bucket bands as (step, top): sizes step, 2 step, ... up to top, the step doubling from band to band, so a pack is
+#: padded by at most 64 tokens up to 2,048 and by at most a sixteenth of its size beyond. The reference's fine
+#: buckets, the ones its fast Qwen path captures (serve/qwen_graphs.py:171).
+FINE_BANDS = ((64, 2048), (128, 4096), (256, 8192), (512, 16384), (1024, 32768), (2048, 65536))
+
+
+def fine_buckets(max_tokens: int) -> tuple[int, ...]:
+    """The fine buckets up to the first one holding ``max_tokens`` tokens (at most 65,536)."""
+    if not 0 < max_tokens <= FINE_BANDS[-1][1]:
+        raise ValueError(f"max_tokens must be in [1, {FINE_BANDS[-1][1]}]")
+    out: list[int] = []
+    low = 0
+    for step, top in FINE_BANDS:
+        size = low + step
+        while size <= top:
+            out.append(size)
+            if size >= max_tokens:
+                return tuple(out)
+            size += step
+        low = top
+    return tuple(out)
+
+
+#: Default buckets: the fine buckets up to 65,536 tokens (112 graphs, captured at construction; they share one
+#: workspace, so their cost is capture time, not memory).
+DEFAULT_BUCKETS = fine_buckets(65536)
 
 
 @dataclass

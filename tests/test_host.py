@@ -1,6 +1,7 @@
 """Host-side logic of the B200 path that needs no GPU: weight repacking, workspace layout, packing, shapes."""
 
 import numpy as np
+import pytest
 import torch
 
 from karpo_decision_b200.pack import from_arrays, pack
@@ -221,3 +222,16 @@ def test_microbench_work_counts():
     assert visible_pairs([3, 2], (-1, -1)) == 9 + 4     # bidirectional: L^2
     assert visible_pairs([5], (0, 1)) == 2 + 2 + 2 + 2 + 1
     assert sum(parse_lengths("mix:65536")) == 65536 and parse_lengths("8192,4096") == [8192, 4096]
+
+
+def test_fine_buckets_cover_every_size_with_bounded_padding():
+    """The graph buckets (the reference's fine bands, serve/qwen_graphs.py:171): the first bucket holding a pack
+    pads it by at most 64 tokens up to 2,048 and by at most a sixteenth beyond; the list stops at that bucket."""
+    from karpo_decision_b200.graphs import DEFAULT_BUCKETS, fine_buckets
+    assert len(DEFAULT_BUCKETS) == 112 and DEFAULT_BUCKETS[0] == 64 and DEFAULT_BUCKETS[-1] == 65536
+    for n in (1, 63, 64, 65, 2047, 2048, 2049, 5000, 32769, 65536):
+        b = fine_buckets(n)
+        assert b[-1] >= n and (len(b) == 1 or b[-2] < n)
+        assert b[-1] - n < 64 if n <= 2048 else (b[-1] - n) * 16 <= n
+    with pytest.raises(ValueError):
+        fine_buckets(65537)
