@@ -249,6 +249,67 @@ def gated_delta_rule(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray,
     return out
 
 
+def unit_lower_inverse(a: np.ndarray, block: int = 16) -> np.ndarray:
+    """(I + A)^-1 for a strictly lower-triangular square A, by blocks of ``block`` rows: each diagonal block by forward
+    substitution (row i = e_i - A_i,<i times the rows above), then, block row by block row, the blocks below the
+    diagonal from (I + A) T = I: T_ij = -T_ii sum_{k=j}^{i-1} A_ik T_kj. The chunked delta rule's triangular solve in
+    the blocked order a tensor-core kernel would follow (small diagonal inverses, then block products)."""
+    c = a.shape[0]
+    t = np.zeros_like(a)
+    starts = list(range(0, c, block))
+    spans = [slice(b, min(c, b + block)) for b in starts]
+    for sp in spans:
+        n = sp.stop - sp.start
+        ab, d = a[sp, sp], np.eye(n, dtype=a.dtype)
+        for i in range(1, n):
+            d[i, :i] = -ab[i, :i] @ d[:i, :i]
+        t[sp, sp] = d
+    for bi in range(1, len(spans)):
+        for bj in range(bi):
+            acc = sum(a[spans[bi], spans[bk]] @ t[spans[bk], spans[bj]] for bk in range(bj, bi))
+            t[spans[bi], spans[bj]] = -t[spans[bi], spans[bi]] @ acc
+    return t
+
+
+def gated_delta_rule_chunked(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray, beta: np.ndarray,
+                             cu: np.ndarray, chunk: int = 64) -> np.ndarray:
+    """``gated_delta_rule`` in the chunked (WY) form that flash-linear-attention's chunk_gated_delta_rule evaluates
+    (the kernel families/qwen/packed.py:96-98 calls), with the same normalization and state start per sequence. Per
+    chunk of at most ``chunk`` tokens of a sequence and head, G the running sum of g from the chunk's start:
+        A = strictly lower part of diag(beta) (K K^T o exp(G_i - G_j)),  T = (I + A)^-1,
+        U = T diag(beta) V,  W = T diag(beta exp(G)) K,  D = U - W S,
+        O = diag(exp(G)) Q S + (Q K^T o exp(G_i - G_j), j <= i) D,
+        S <- exp(G_last) S + (diag(exp(G_last - G)) K)^T D.
+    Equal to the recurrent form up to rounding; float32 in, float32 out."""
+    def l2(x):
+        x = x.astype(np.float32)
+        return x / np.sqrt((x * x).sum(-1, keepdims=True) + np.float32(1e-6))
+
+    q, k = l2(q) * np.float32(q.shape[-1] ** -0.5), l2(k)
+    v, g, beta = v.astype(np.float32), g.astype(np.float32), beta.astype(np.float32)
+    heads, dk, dv = q.shape[1], q.shape[2], v.shape[2]
+    out = np.zeros((q.shape[0], heads, dv), dtype=np.float32)
+    for a, b in zip(cu[:-1].tolist(), cu[1:].tolist(), strict=True):
+        for h in range(heads):
+            state = np.zeros((dk, dv), dtype=np.float32)
+            for c0 in range(a, b, chunk):
+                c1 = min(c0 + chunk, b)
+                kc, qc, vc, bc = k[c0:c1, h], q[c0:c1, h], v[c0:c1, h], beta[c0:c1, h]
+                gc = np.cumsum(g[c0:c1, h], dtype=np.float32)
+                n = c1 - c0
+                lower = np.tril(np.ones((n, n), dtype=bool))
+                # exp(G_i - G_j) for j <= i only (the upper part would overflow and is not used)
+                decay = np.exp(np.where(lower, gc[:, None] - gc[None, :], -np.inf)).astype(np.float32)
+                amat = np.tril(bc[:, None] * (kc @ kc.T) * decay, -1)
+                tmat = unit_lower_inverse(amat)
+                u = tmat @ (bc[:, None] * vc)
+                w = tmat @ ((bc * np.exp(gc))[:, None] * kc)
+                d = u - w @ state
+                out[c0:c1, h] = (np.exp(gc)[:, None] * qc) @ state + ((qc @ kc.T) * decay) @ d
+                state = np.exp(gc[-1]) * state + (kc * np.exp(gc[-1] - gc)[:, None]).T @ d
+    return out
+
+
 def softplus(x: np.ndarray) -> np.ndarray:
     return np.where(x > 20.0, x, np.log1p(np.exp(np.minimum(x, 20.0)))).astype(np.float32)
 

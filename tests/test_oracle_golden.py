@@ -70,3 +70,30 @@ def test_e4m3_matches_torch_cast():
                         np.array([0.0, 448.0, -448.0, 1e-4, 0.0009765625, 240.0, 232.0], dtype=np.float32)])
     ref = torch.from_numpy(x).to(torch.float8_e4m3fn).float().numpy()
     assert np.array_equal(oracle.packed.e4m3(x), ref)
+
+
+def test_unit_lower_inverse_by_blocks():
+    """The blocked triangular inverse of the chunked delta rule equals a dense inverse, block multiples or not."""
+    g = np.random.default_rng(3)
+    for c in (64, 100, 7):
+        a = np.tril(g.standard_normal((c, c)) * 0.3, -1)
+        want = np.linalg.inv(np.eye(c) + a)
+        assert np.abs(oracle.packed.unit_lower_inverse(a) - want).max() <= 1e-9 * max(1.0, np.abs(want).max())
+
+
+def test_chunked_delta_rule_equals_recurrent():
+    """The chunked (WY) gated delta rule, the form flash-linear-attention evaluates for the reference, equals the
+    recurrent rule the kernels and goldens follow: sequences shorter than, equal to and longer than a chunk, state
+    restarting at each sequence start, decays and write strengths in their real ranges."""
+    g = np.random.default_rng(4)
+    lengths = [1, 63, 64, 65, 200]
+    cu = np.concatenate([[0], np.cumsum(lengths)]).astype(np.int64)
+    t, heads, dk, dv = cu[-1], 2, 16, 24
+    q, k = (g.standard_normal((t, heads, dk)).astype(np.float32) for _ in range(2))
+    v = g.standard_normal((t, heads, dv)).astype(np.float32)
+    decay = -np.exp(g.uniform(-3.0, 0.5, (t, heads))).astype(np.float32)  # g = -exp(A_log) softplus(.) < 0
+    beta = (1.0 / (1.0 + np.exp(-g.standard_normal((t, heads))))).astype(np.float32)
+    want = oracle.packed.gated_delta_rule(q, k, v, decay, beta, cu)
+    for chunk in (64, 16):
+        got = oracle.packed.gated_delta_rule_chunked(q, k, v, decay, beta, cu, chunk=chunk)
+        assert np.abs(got - want).max() <= 1e-5 * max(1.0, np.abs(want).max())  # measured 7e-7 at 0.4
