@@ -67,9 +67,16 @@ __global__ void conv_silu_kernel(const __nv_bfloat16* __restrict__ x, int64_t ld
       }
     }
   }
+  // the next row's values are loaded while the current row is computed (two loads in flight per thread)
+  uint4 next = r0 < r1 ? *reinterpret_cast<const uint4*>(x + r0 * ldx + c0) : make_uint4(0, 0, 0, 0);
+  int64_t next_pos = r0 < r1 ? seqpos[r0] : 0;
   for (int64_t t = r0; t < r1; ++t) {
-    const int64_t pos = seqpos[t];
-    const uint4 raw = *reinterpret_cast<const uint4*>(x + t * ldx + c0);
+    const int64_t pos = next_pos;
+    const uint4 raw = next;
+    if (t + 1 < r1) {
+      next = *reinterpret_cast<const uint4*>(x + (t + 1) * ldx + c0);
+      next_pos = seqpos[t + 1];
+    }
     const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
     float cur[8];
 #pragma unroll
