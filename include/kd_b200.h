@@ -189,7 +189,7 @@ int kd_scatter_rows(const void* src, int64_t ld_src, const int64_t* rows, int64_
 /* Depthwise causal convolution + silu over the [q | k | v] channels: out[t, c] = bf16(silu(sum_s w[c, K-1-s]
  * x[t-s, c])), float32 sums, over taps s with seqpos[t] >= s (no tap before the token's sequence start). x and out
  * bf16 (T, C) with 16-byte aligned rows, C % 8 == 0; weight bf16 (C, K), K <= 4 (conv1d weight squeezed).
- * Replaces flash-linear-attention's causal_conv1d with cu_seqlens (families/qwen/packed.py:81-83) and packed_conv
+ * Replaces flash-linear-attention's causal_conv1d with cu_seqlens (families/qwen/packed.py:82-87) and packed_conv
  * (:45-53). */
 int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const void* weight, int K, const int64_t* seqpos,
                  void* out, int64_t ldo, cudaStream_t stream);
@@ -197,17 +197,17 @@ int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const void* weigh
 /* The gated delta rule per sequence (cu int32 [num_seqs + 1] on the device) and value head h, its key head
  * h / (Hv / Hk): q, k L2-normalized (eps 1e-6), q scaled by dk^-1/2, state S (dk x dv) from zero at each sequence
  * start, per token S = exp(g) S, d = beta (v - S^T k), S += k d^T, o = S^T q; with g = -exp(A_log)
- * softplus(a + dt_bias) in float32 and beta = sigmoid(b) rounded to bf16 (families/qwen/fused.py:45-47).
+ * softplus(a + dt_bias) in float32 and beta = sigmoid(b) rounded to bf16 (families/qwen/fused.py:42-44).
  * qkv rows [q Hk*dk | k Hk*dk | v Hv*dv] bf16 (the convolution's output); ab rows [b Hv | a Hv] bf16; a_log,
  * dt_bias bf16 [Hv]; out bf16 (T, Hv*dv). dk, dv in {64, 128}.
  * Replaces flash-linear-attention's chunk_gated_delta_rule (use_qk_l2norm_in_kernel, cu_seqlens) as
- * families/qwen/packed.py:88-98 calls it. */
+ * families/qwen/packed.py:88-103 calls it. */
 int kd_gated_delta_rule(const void* qkv, int64_t ldqkv, const void* ab, int64_t ldab, const void* a_log,
                         const void* dt_bias, const int32_t* cu, int num_seqs, int64_t T, int num_k_heads,
                         int num_v_heads, int head_k_dim, int head_v_dim, void* out, int64_t ldo, cudaStream_t stream);
 
 /* Qwen3_5RMSNormGated per (token, head) of head_dim values: out = bf16(bf16(w * bf16(x rsqrt(mean(x^2) + eps))) *
- * silu(z)) (families/qwen/fused.py:29-32). head_dim 64 or 128. */
+ * silu(z)) (families/qwen/fused.py:28-31). head_dim 64 or 128. */
 int kd_gated_norm(const void* x, int64_t ldx, const void* z, int64_t ldz, const void* weight, int64_t T, int heads,
                   int head_dim, float eps, void* out, int64_t ldo, cudaStream_t stream);
 

@@ -209,7 +209,7 @@ def quantize_weights(weights: dict, min_features: int = 0) -> dict:
 
 def causal_conv_silu(x: np.ndarray, weight: np.ndarray, seqpos: np.ndarray) -> np.ndarray:
     """Depthwise causal convolution over rows (T, C) with taps (C, K), cut at every sequence start (a tap reaches
-    back ``shift`` rows only where seqpos >= shift: families/qwen/packed.py:45-53), float32 sums, then silu: the
+    back ``shift`` rows only where seqpos >= shift: families/qwen/packed.py:47-55), float32 sums, then silu: the
     convolution and activation of the Gated DeltaNet (families/qwen/packed.py:81-86, flash-linear-attention's
     causal_conv1d with cu_seqlens)."""
     taps = weight.shape[1]
@@ -227,7 +227,7 @@ def gated_delta_rule(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray,
                      cu: np.ndarray) -> np.ndarray:
     """The gated delta rule per sequence and head, in its recurrent form (Transformers'
     torch_recurrent_gated_delta_rule, the contract of flash-linear-attention's chunk_gated_delta_rule that
-    families/qwen/packed.py:96-98 calls with use_qk_l2norm_in_kernel): q, k L2-normalized (eps 1e-6), q scaled by
+    families/qwen/packed.py:102-103 calls with use_qk_l2norm_in_kernel): q, k L2-normalized (eps 1e-6), q scaled by
     dk^-0.5, state S (dk, dv) from zero at each sequence start; per token S = S exp(g) ; d = (v - S^T k) beta ;
     S = S + k d^T ; o = S^T q. q, k (T, H, dk), v (T, H, dv), g, beta (T, H) -> (T, H, dv) float32."""
     def l2(x):
@@ -274,7 +274,7 @@ def unit_lower_inverse(a: np.ndarray, block: int = 16) -> np.ndarray:
 def gated_delta_rule_chunked(q: np.ndarray, k: np.ndarray, v: np.ndarray, g: np.ndarray, beta: np.ndarray,
                              cu: np.ndarray, chunk: int = 64) -> np.ndarray:
     """``gated_delta_rule`` in the chunked (WY) form that flash-linear-attention's chunk_gated_delta_rule evaluates
-    (the kernel families/qwen/packed.py:96-98 calls), with the same normalization and state start per sequence. Per
+    (the kernel families/qwen/packed.py:102-103 calls), with the same normalization and state start per sequence. Per
     chunk of at most ``chunk`` tokens of a sequence and head, G the running sum of g from the chunk's start:
         A = strictly lower part of diag(beta) (K K^T o exp(G_i - G_j)),  T = (I + A)^-1,
         U = T diag(beta) V,  W = T diag(beta exp(G)) K,  D = U - W S,
@@ -318,8 +318,8 @@ def linear_attention(weights: dict, spec: dict, p: str, x: np.ndarray, pack: dic
                      fp8: bool = False) -> np.ndarray:
     """Qwen3.5's Gated DeltaNet token mixer over the pack (families/qwen/packed.py:74-106): projections, causal
     convolution + silu, decay g = -exp(A_log) softplus(a + dt_bias) and write strength beta = sigmoid(b)
-    (fused.py:45-47), query/key heads repeated to the value heads, the gated delta rule, the gated RMSNorm
-    weight * bf16(norm(core)) * silu(z) (fused.py:29-32, Qwen3_5RMSNormGated) and the output projection."""
+    (fused.py:42-44), query/key heads repeated to the value heads, the gated delta rule, the gated RMSNorm
+    weight * bf16(norm(core)) * silu(z) (fused.py:28-31, Qwen3_5RMSNormGated) and the output projection."""
     la = p + "linear_attn."
     t = x.shape[0]
     nk, nv, dk, dv = spec["lin_k_heads"], spec["lin_v_heads"], spec["lin_k_dim"], spec["lin_v_dim"]
