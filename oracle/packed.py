@@ -210,7 +210,7 @@ def quantize_weights(weights: dict, min_features: int = 0) -> dict:
 def causal_conv_silu(x: np.ndarray, weight: np.ndarray, seqpos: np.ndarray) -> np.ndarray:
     """Depthwise causal convolution over rows (T, C) with taps (C, K), cut at every sequence start (a tap reaches
     back ``shift`` rows only where seqpos >= shift: families/qwen/packed.py:47-55), float32 sums, then silu: the
-    convolution and activation of the Gated DeltaNet (families/qwen/packed.py:81-86, flash-linear-attention's
+    convolution and activation of the Gated DeltaNet (families/qwen/packed.py:82-87, flash-linear-attention's
     causal_conv1d with cu_seqlens)."""
     taps = weight.shape[1]
     xf = x.astype(np.float32)
