@@ -2,8 +2,11 @@
  *
  * Every entry point takes device pointers, element strides, sizes and a cudaStream_t, launches on that stream and
  * returns an int status: KD_OK (0), or a negative code with a message kept for kd_last_error(). Arguments are checked
- * before anything is launched; a rejected call launches nothing. The library allocates no device memory: every
- * buffer, scratch included, belongs to the caller, so the calls can be captured in CUDA graphs.
+ * before anything is launched; a rejected call launches nothing. The library allocates no device memory at run time:
+ * every buffer, scratch included, belongs to the caller, so the calls can be captured in CUDA graphs. The one
+ * exception is kd_qkv_projection_noalloc, whose rotary scratch is a static 16 MiB device array owned by the library
+ * and shared by all its calls on a device (created when the library loads; its first call on a device looks up the
+ * array's address and must come before any stream capture on that device).
  *
  * Pipelined kernels (GEMM, attention) also take `status`, a device int the caller zeroes once: a kernel whose
  * internal wait gives up (KD_WAIT_LIMIT_NS, 4 s) writes KD_DEVICE_TIMEOUT there and returns instead of hanging.
@@ -88,20 +91,23 @@ int kd_qkv_projection_fp8(const void* A, int64_t lda, const float* scale_a, cons
 /* kd_qkv_projection for callers that cannot allocate device memory (a plugin host that owns every allocation and
  * passes only inputs and outputs, a runtime that forbids side allocations): the per-pack rotary scratch lives in a
  * static device array of the library (4 Mi uint32 entries, 16 MiB per device that loads the library, held until exit)
- * instead of a caller buffer. Takes the rotary tables of kd_rope_table; calls needing more than 4 Mi entries
- * ((rot / 2) * M) are rejected. All calls on a device share the array (overlapping calls race); the first call on a
- * device looks up the array's address and should come before any stream capture. Allocates nothing.
+ * instead of a caller buffer. Takes the rotary tables of kd_rope_table and their row count `positions`; calls needing
+ * more than 4 Mi entries ((rot / 2) * M) are rejected. Every argument is checked before the first launch, so a
+ * rejected call launches nothing and leaves the array untouched. All calls on a device share the array (overlapping
+ * calls race); the first call on a device looks up the array's address and should come before any stream capture.
+ * Allocates nothing.
  * No counterpart in the reference: an addition of this library for allocation-free callers. */
 int kd_qkv_projection_noalloc(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
                               const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,
                               const void* q_norm_w, const void* k_norm_w, int qk_norm_mode, int v_norm_mode, float eps,
-                              const float* cos_tab, const float* sin_tab, int rot, void* q, void* k, void* v,
-                              void* gate, int* status, cudaStream_t stream);
+                              const float* cos_tab, const float* sin_tab, int64_t positions, int rot, void* q,
+                              void* k, void* v, void* gate, int* status, cudaStream_t stream);
 
 /* A pack's rotary factors for kd_qkv_projection: cs[i * T + t] = bf16 cos[seqpos[t], i] | bf16 sin[seqpos[t], i] << 16
- * for the rot / 2 distinct pairs i (tables from kd_rope_table). One gather per pack and rotary kind. */
-int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab, int rot,
-                   uint32_t* cs, cudaStream_t stream);
+ * for the rot / 2 distinct pairs i (tables from kd_rope_table, `positions` rows). A position outside [0, positions) is
+ * never read: its entry is the identity rotation (cos 1, sin 0). One gather per pack and rotary kind. */
+int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab, int64_t positions,
+                   int rot, uint32_t* cs, cudaStream_t stream);
 
 /* ---------------------------------------------------------------------------------------------- pointwise
  * out[t, :] = table[ids[t], :] (times bf16(scale) when scale != 0: Gemma's scaled embedding, sqrt(hidden)).

@@ -28,9 +28,9 @@ SIGNATURES: dict[str, list] = {
                           c_int, c_float, P, c_int, P, P, P, P, P, P],
     "kd_qkv_projection_fp8": [P, c_int64, P, P, c_int64, P, c_int, c_int, c_int, P, c_int, c_int, c_int, c_int, P, P,
                               c_int, c_int, c_float, P, c_int, P, P, P, P, P, P],
-    "kd_rope_gather": [P, c_int64, P, P, c_int, P, P],
+    "kd_rope_gather": [P, c_int64, P, P, c_int64, c_int, P, P],
     "kd_qkv_projection_noalloc": [P, c_int64, P, c_int64, c_int, c_int, c_int, P, c_int, c_int, c_int, c_int, P, P,
-                                  c_int, c_int, c_float, P, P, c_int, P, P, P, P, P, P],
+                                  c_int, c_int, c_float, P, P, c_int64, c_int, P, P, P, P, P, P],
     "kd_embed": [P, c_int64, P, c_int64, c_int, c_float, P, P],
     "kd_rmsnorm": [P, c_int64, P, c_int, c_float, P, c_int64, c_int64, c_int, P],
     "kd_add_rmsnorm": [P, P, P, c_int, c_float, P, c_int64, c_int, P],

@@ -518,15 +518,22 @@ __global__ void scatter_rows_kernel(const __nv_bfloat16* __restrict__ src, int64
   for (int c = lane; c < width / 8; c += 32) d[c] = s[c];
 }
 
-// cs[i * T + t] = bf16 cos | bf16 sin << 16 of rotary pair i at seqpos[t] (t fastest: coalesced writes).
+// cs[i * T + t] = bf16 cos | bf16 sin << 16 of rotary pair i at seqpos[t] (t fastest: coalesced writes). A position
+// outside the table's rows [0, positions) is never read: its entry is the identity rotation (cos 1, sin 0).
 __global__ void rope_gather_kernel(const int64_t* __restrict__ seqpos, int64_t T, const float* __restrict__ cos_tab,
-                                   const float* __restrict__ sin_tab, int rot, uint32_t* __restrict__ cs) {
+                                   const float* __restrict__ sin_tab, int64_t positions, int rot,
+                                   uint32_t* __restrict__ cs) {
   const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int half = rot / 2;
   if (idx >= T * half) return;
   const int i = (int)(idx / T);
   const int64_t t = idx % T;
-  const int64_t off = seqpos[t] * rot + i;
+  const int64_t pos = seqpos[t];
+  if (pos < 0 || pos >= positions) {
+    cs[idx] = pack_bf16x2(1.0f, 0.0f);
+    return;
+  }
+  const int64_t off = pos * rot + i;
   cs[idx] = pack_bf16x2(cos_tab[off], sin_tab[off]);
 }
 
@@ -846,13 +853,14 @@ extern "C" int kd_readout(const void* hidden, int64_t M, int hidden_size, const 
   return record_cuda_error(cudaGetLastError(), "readout: launch");
 }
 
-extern "C" int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab, int rot,
-                              uint32_t* cs, cudaStream_t stream) {
-  if (T < 0 || rot <= 0 || rot % 2) return set_error(KD_ERR_ARGUMENT, "rope_gather: bad sizes");
+extern "C" int kd_rope_gather(const int64_t* seqpos, int64_t T, const float* cos_tab, const float* sin_tab,
+                              int64_t positions, int rot, uint32_t* cs, cudaStream_t stream) {
+  if (T < 0 || rot <= 0 || rot % 2 || positions <= 0) return set_error(KD_ERR_ARGUMENT, "rope_gather: bad sizes");
   if (T == 0) return KD_OK;
   if (!seqpos || !cos_tab || !sin_tab || !cs) return set_error(KD_ERR_ARGUMENT, "rope_gather: null pointer");
   const int64_t n = T * (rot / 2);
-  ew::rope_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(seqpos, T, cos_tab, sin_tab, rot, cs);
+  ew::rope_gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(seqpos, T, cos_tab, sin_tab, positions,
+                                                                           rot, cs);
   return record_cuda_error(cudaGetLastError(), "rope_gather: launch");
 }
 

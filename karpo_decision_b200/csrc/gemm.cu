@@ -666,7 +666,8 @@ using namespace kd;
 
 static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, void* C, int64_t ldc, const void* R,
                        int64_t ldr, const float* scale_a, const float* scale_b, int M, int N, int K, int epilogue,
-                       int fp8, int* status, cudaStream_t stream, const gemm::Qkv* qkv = nullptr) {
+                       int fp8, int* status, cudaStream_t stream, const gemm::Qkv* qkv = nullptr,
+                       bool launch = true) {
   if (M < 0 || N <= 0 || K <= 0) return set_error(KD_ERR_ARGUMENT, "gemm: M >= 0, N > 0 and K > 0 required");
   if (M == 0) return KD_OK;
   if (!A || !B || !C || !status) return set_error(KD_ERR_ARGUMENT, "gemm: null pointer");
@@ -727,6 +728,7 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
                        CU_TENSOR_MAP_SWIZZLE_128B);
     if (rc) return rc;
   }
+  if (!launch) return KD_OK;  // a check-only call: every argument and descriptor accepted, nothing launched
 #define KD_GEMM_CASE(E)                                                                                \
   case E:                                                                                              \
     if (pair)                                                                                          \
@@ -750,7 +752,8 @@ static int qkv_common(const void* A, int64_t lda, const float* scale_a, const vo
                       const float* scale_w, int M, int N, int K, const int64_t* seqpos, int num_heads_q,
                       int num_heads_kv, int head_dim, int gated, const void* q_norm_w, const void* k_norm_w,
                       int qk_norm_mode, int v_norm_mode, float eps, const uint32_t* rope_cs, int rot, void* q,
-                      void* k, void* v, void* gate, int fp8, int* status, cudaStream_t stream) {
+                      void* k, void* v, void* gate, int fp8, int* status, cudaStream_t stream,
+                      bool launch = true) {
   if (num_heads_q <= 0 || num_heads_kv <= 0 || num_heads_q % num_heads_kv)
     return set_error(KD_ERR_ARGUMENT, "qkv_projection: bad head counts");
   if (head_dim != 64 && head_dim != 128 && head_dim != 256)
@@ -785,8 +788,19 @@ static int qkv_common(const void* A, int64_t lda, const float* scale_a, const vo
   g.eps = eps;
   // C is unused by this epilogue; q stands in for the pointer checks.
   return gemm_common(A, lda, W, ldw, q, N, nullptr, 0, scale_a, scale_w, M, N, K, KD_EPI_QKV, fp8, status, stream,
-                     &g);
+                     &g, launch);
 }
+
+namespace kd {
+int qkv_projection_check(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+                         const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,
+                         const void* q_norm_w, const void* k_norm_w, int qk_norm_mode, int v_norm_mode, float eps,
+                         const uint32_t* rope_cs, int rot, void* q, void* k, void* v, void* gate, int* status) {
+  return qkv_common(A, lda, nullptr, W, ldw, nullptr, M, N, K, seqpos, num_heads_q, num_heads_kv, head_dim, gated,
+                    q_norm_w, k_norm_w, qk_norm_mode, v_norm_mode, eps, rope_cs, rot, q, k, v, gate, 0, status,
+                    nullptr, false);
+}
+}  // namespace kd
 
 extern "C" int kd_qkv_projection(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
                                  const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,

@@ -27,4 +27,11 @@ int make_tma_3d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, i
                 uint64_t d1, uint64_t d2, uint64_t s1, uint64_t s2, uint32_t b0, uint32_t b1, uint32_t b2,
                 CUtensorMapSwizzle swizzle);
 
+// Every check kd_qkv_projection makes (sizes, pointers, alignment, the TMA descriptors it would encode) without
+// launching anything: KD_OK when that call would be accepted.
+int qkv_projection_check(const void* A, int64_t lda, const void* W, int64_t ldw, int M, int N, int K,
+                         const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim, int gated,
+                         const void* q_norm_w, const void* k_norm_w, int qk_norm_mode, int v_norm_mode, float eps,
+                         const uint32_t* rope_cs, int rot, void* q, void* k, void* v, void* gate, int* status);
+
 }  // namespace kd

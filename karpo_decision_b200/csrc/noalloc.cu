@@ -15,7 +15,9 @@
 //   projection reads, so nothing needs clearing between calls, but two calls whose kernels overlap on the GPU (different
 //   streams without ordering between them) race on the array;
 // - the first call on each device looks up the array's device address (cudaGetSymbolAddress, with that device
-//   current) and caches it; make that first call before any stream capture on the device.
+//   current) and caches it; make that first call before any stream capture on the device;
+// - every argument is checked before the first launch, so a rejected call launches nothing and leaves the array as
+//   it was; positions outside the rotary tables' rows read as the identity rotation, never past the tables.
 // No cudaMalloc, cudaFree or allocating library routine is called.
 #include <mutex>
 
@@ -57,18 +59,30 @@ extern "C" int kd_qkv_projection_noalloc(const void* A, int64_t lda, const void*
                                          const int64_t* seqpos, int num_heads_q, int num_heads_kv, int head_dim,
                                          int gated, const void* q_norm_w, const void* k_norm_w, int qk_norm_mode,
                                          int v_norm_mode, float eps, const float* cos_tab, const float* sin_tab,
-                                         int rot, void* q, void* k, void* v, void* gate, int* status,
-                                         cudaStream_t stream) {
+                                         int64_t positions, int rot, void* q, void* k, void* v, void* gate,
+                                         int* status, cudaStream_t stream) {
+  // Every check comes before the first launch: a rejected call neither launches the gather nor touches the shared
+  // array. Sizes first (no CUDA call), then the gather's own arguments, then the array's address, then every check
+  // of the projection (descriptors included) with that address standing in for the caller's buffer.
   if (M < 0 || rot < 0 || rot % 2) return kd::set_error(KD_ERR_ARGUMENT, "qkv_projection_noalloc: bad sizes");
+  if (rot > head_dim || rot % 32)
+    return kd::set_error(KD_ERR_ARGUMENT,
+                         "qkv_projection_noalloc: rotary width must be a multiple of 32 within head_dim");
   const uint64_t entries = (uint64_t)(rot / 2) * (uint64_t)M;
   if (entries > KD_NOALLOC_ROPE_ENTRIES)
     return kd::set_error(KD_ERR_ARGUMENT,
                          "qkv_projection_noalloc: (rot / 2) * M exceeds the static scratch of 4194304 entries");
+  const bool gather = M > 0 && rot > 0;
+  if (gather && (!seqpos || !cos_tab || !sin_tab || positions <= 0))
+    return kd::set_error(KD_ERR_ARGUMENT, "qkv_projection_noalloc: rotary tables, their rows and seqpos required");
   uint32_t* scratch = nullptr;
   int rc = kd::noalloc::scratch_address(&scratch);
   if (rc) return rc;
-  if (M > 0 && rot > 0) {
-    rc = kd_rope_gather(seqpos, M, cos_tab, sin_tab, rot, scratch, stream);
+  rc = kd::qkv_projection_check(A, lda, W, ldw, M, N, K, seqpos, num_heads_q, num_heads_kv, head_dim, gated, q_norm_w,
+                                k_norm_w, qk_norm_mode, v_norm_mode, eps, scratch, rot, q, k, v, gate, status);
+  if (rc) return rc;
+  if (gather) {
+    rc = kd_rope_gather(seqpos, M, cos_tab, sin_tab, positions, rot, scratch, stream);
     if (rc) return rc;
   }
   return kd_qkv_projection(A, lda, W, ldw, M, N, K, seqpos, num_heads_q, num_heads_kv, head_dim, gated, q_norm_w,

@@ -266,12 +266,14 @@ def readout(hidden: torch.Tensor, weight: torch.Tensor, cap: float | None = None
 
 def rope_gather(seqpos: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor, out: torch.Tensor | None = None
                 ) -> torch.Tensor:
-    """The pack's rotary factors for ``qkv_projection``: int32 (rot / 2, T) of packed bf16 (cos, sin) pairs."""
+    """The pack's rotary factors for ``qkv_projection``: int32 (rot / 2, T) of packed bf16 (cos, sin) pairs. A position
+    past the tables' rows (``cos.shape[0]``) reads as the identity rotation; callers size the tables to the pack."""
     _require(seqpos.dtype == torch.int64 and seqpos.is_contiguous(), "seqpos must be contiguous int64")
     t, rot = seqpos.numel(), cos.shape[1]
     if out is None:
         out = torch.empty(rot // 2, t, dtype=torch.int32, device=seqpos.device)
-    call("kd_rope_gather", seqpos.data_ptr(), t, cos.data_ptr(), sin.data_ptr(), rot, out.data_ptr(), _stream(cos))
+    call("kd_rope_gather", seqpos.data_ptr(), t, cos.data_ptr(), sin.data_ptr(), cos.shape[0], rot, out.data_ptr(),
+         _stream(cos))
     return out
 
 

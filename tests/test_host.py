@@ -202,8 +202,8 @@ def test_image_plan_matches_oracle_and_refuses_what_the_reference_refuses():
 
 
 def test_smoke_packs_pass_the_host_plan():
-    """The round-end smoke forward's packs satisfy the host planning rules the forward enforces before any kernel is
-    queued (a Gemma block's readout marker is its last token, one per block)."""
+    """The packs of ``__graft_entry__.smoke`` satisfy the host planning rules the forward enforces before any kernel
+    is queued (a Gemma block's readout marker is its last token, one per block)."""
     import __graft_entry__
     from karpo_decision_b200.plan import marker_bounds
 
