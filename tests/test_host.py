@@ -235,3 +235,39 @@ def test_fine_buckets_cover_every_size_with_bounded_padding():
         assert b[-1] - n < 64 if n <= 2048 else (b[-1] - n) * 16 <= n
     with pytest.raises(ValueError):
         fine_buckets(65537)
+
+
+def test_block_and_image_plans_match_oracle_on_random_layouts():
+    """Random block layouts (1-5 sequences, 0-3 branches each, windows 1..49) and random image runs inside them:
+    the vectorized host plans equal the oracle's sequence-by-sequence restatement row for row."""
+    import oracle
+    from karpo_decision_b200.plan import block_plan, image_plan
+    from karpo_decision_b200.synthetic import synthetic_block_arrays
+
+    rng = np.random.default_rng(0)
+    cpu = torch.device("cpu")
+    checked_images = 0
+    for trial in range(200):
+        layouts = [(int(rng.integers(1, 40)), [int(rng.integers(1, 30)) for _ in range(int(rng.integers(0, 4)))])
+                   for _ in range(int(rng.integers(1, 6)))]
+        a = synthetic_block_arrays(layouts, 100, seed=trial)
+        window = int(rng.integers(1, 50))
+        plan = block_plan(torch.from_numpy(a["cu"]), torch.from_numpy(a["segment_ids"]), window, cpu,
+                          markers_cpu=a["markers"])
+        want = oracle.packed.block_plan(a["cu"], a["segment_ids"], window)
+        assert plan.q_cu.tolist() == want["q_cu"].tolist()
+        assert plan.g_rows.tolist() == want["g_rows"].tolist() and plan.s_rows.tolist() == want["s_rows"].tolist()
+        # one image run starting at a random row, cut at its block's end and at the window
+        ids, seg, cu = a["input_ids"].copy(), a["segment_ids"], set(a["cu"].tolist())
+        ids[ids == 99] = 0
+        w_img = int(rng.integers(8, 40))
+        s = int(rng.integers(0, len(ids)))
+        e = s + 1
+        while e < len(ids) and e - s < int(rng.integers(1, w_img + 1)) and seg[e] == seg[s] and e not in cu:
+            e += 1
+        ids[s:e] = 99
+        plan = image_plan(ids, a["cu"].tolist(), seg, a["seqpos"], 99, w_img, cpu)
+        spans = oracle.packed.image_spans(dict(a, input_ids=ids, image_token=99), w_img)
+        assert plan.keys.tolist() == np.concatenate([seen for _, _, seen in spans]).tolist()
+        checked_images += 1
+    assert checked_images == 200
