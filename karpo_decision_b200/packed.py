@@ -309,18 +309,26 @@ class Packed(torch.nn.Module):
     # ---------------------------------------------------------------- construction from a Transformers backbone
 
     @classmethod
-    def from_backbone(cls, backbone: Any, attention: str = "causal", fp8: bool = False) -> Packed:
+    def from_backbone(cls, backbone: Any, attention: str = "causal", fp8: bool = False,
+                      device: torch.device | str | None = None) -> Packed:
         """From a Transformers ``Qwen3_5Model`` (full-attention and Gated DeltaNet layers) or a Gemma 4 text model, as
-        the reference's ``family.Packed(backbone, attention)``; the weights are copied into the kernels' layouts."""
+        the reference's ``family.Packed(backbone, attention)``; the weights are copied into the kernels' layouts on
+        ``device`` (default: the backbone's device when it is a GPU, else the current GPU)."""
         lm = getattr(backbone, "language_model", backbone)
         config = lm.config
         model_type = getattr(config, "model_type", "")
         family = "gemma" if "gemma" in model_type else "qwen"
         weights: dict[str, Any] = {"embed_tokens": lm.embed_tokens.weight, "norm": lm.norm.weight}
+        # Gemma reads each layer's kind from the config (families/gemma/packed.py:168); Qwen from the layer
+        # (``layer_type``, or the reference's ``block_type`` alias: families/qwen/packed.py:151)
+        config_kinds = list(getattr(config, "layer_types", None) or []) if family == "gemma" else []
         kinds = []
         for i, layer in enumerate(lm.layers):
             p = f"layers.{i}."
-            kind = getattr(layer, "layer_type", getattr(layer, "block_type", "full_attention"))
+            if config_kinds:
+                kind = config_kinds[i]
+            else:
+                kind = getattr(layer, "layer_type", None) or getattr(layer, "block_type", None) or "full_attention"
             kinds.append(kind)
             for name in ("gate_proj", "up_proj", "down_proj"):
                 weights[p + name] = getattr(layer.mlp, name).weight
@@ -364,7 +372,7 @@ class Packed(torch.nn.Module):
                         lin_v_heads=getattr(config, "linear_num_value_heads", 32),
                         lin_k_dim=getattr(config, "linear_key_head_dim", 128),
                         lin_v_dim=getattr(config, "linear_value_head_dim", 128),
-                        conv_kernel=getattr(config, "linear_conv_kernel_dim", 4))
+                        conv_kernel=getattr(config, "linear_conv_kernel_dim", 4), attention=attention)
             if kinds != spec.layer_types():
                 raise NotImplementedError(f"layer pattern {kinds} is not a full-attention layer every n-th")
         else:
@@ -381,12 +389,14 @@ class Packed(torch.nn.Module):
                         global_kv_heads=getattr(config, "num_global_key_value_heads", None),
                         k_eq_v=bool(getattr(config, "attention_k_eq_v", False)),
                         global_rope="proportional" if proportional else "default",
-                        global_partial_rotary=full.get("partial_rotary_factor", 1.0) if proportional else 0.25)
+                        global_partial_rotary=full.get("partial_rotary_factor", 1.0) if proportional else 0.25,
+                        attention=attention)
             if kinds != spec.layer_types():
                 raise NotImplementedError(f"layer pattern {kinds} is not 5 sliding : 1 global")
-        device = next(lm.parameters()).device
-        if device.type != "cuda":
-            device = torch.device("cuda")
+        if device is None:
+            device = next(lm.parameters()).device
+            if device.type != "cuda":
+                device = torch.device("cuda")
         image_token = getattr(getattr(backbone, "config", None), "image_token_id", None)
         features = None
         if family == "gemma" and (getattr(backbone, "vision_tower", None) is not None or
@@ -674,9 +684,12 @@ class Readout(torch.nn.Module):
         self.cap = cap
 
     @classmethod
-    def from_reference(cls, head: Any) -> Readout:
-        """From the reference's ``Readout`` module (its rows and cap)."""
-        return cls(head.weight.detach().float(), head.cap, head.weight.device if head.weight.is_cuda else "cuda")
+    def from_reference(cls, head: Any, device: torch.device | str | None = None) -> Readout:
+        """From the reference's ``Readout`` module (its rows and cap), on ``device`` (default: the head's device when
+        it is a GPU, else the current GPU)."""
+        if device is None:
+            device = head.weight.device if head.weight.is_cuda else "cuda"
+        return cls(head.weight.detach().float(), head.cap, device)
 
     def forward(self, hidden: torch.Tensor) -> torch.Tensor:
         return ops.readout(hidden.contiguous(), self.weight, self.cap)

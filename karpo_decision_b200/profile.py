@@ -38,7 +38,8 @@ class KernelTimes:
     def launches(self) -> int:
         return len(self.records)
 
-    def _times(self) -> dict[str, list[tuple[float, float]]]:
+    def times(self) -> dict[str, list[tuple[float, float]]]:
+        """Per entry point, each launch's (device milliseconds, FLOPs) in launch order."""
         torch.cuda.synchronize()
         out: dict[str, list[tuple[float, float]]] = defaultdict(list)
         for name, start, end, flops in self.records:
@@ -47,7 +48,7 @@ class KernelTimes:
 
     def summary(self, prefix: str) -> dict:
         """Launch count, mean device ms and mean FLOPs per launch of the kernels whose name contains ``prefix``."""
-        rows = [r for name, rs in self._times().items() if prefix in name for r in rs]
+        rows = [r for name, rs in self.times().items() if prefix in name for r in rs]
         if not rows:
             return {"launches": 0, "mean_ms": None, "flops_per_launch": 0.0}
         total_ms = sum(ms for ms, _ in rows)
@@ -55,7 +56,7 @@ class KernelTimes:
                 "flops_per_launch": sum(f for _, f in rows) / len(rows)}
 
     def shares(self) -> dict:
-        times = self._times()
+        times = self.times()
         total = sum(ms for rs in times.values() for ms, _ in rs) or 1.0
         return {name: {"launches": len(rs), "ms": round(sum(ms for ms, _ in rs), 4),
                        "share": round(sum(ms for ms, _ in rs) / total, 4)} for name, rs in sorted(times.items())}

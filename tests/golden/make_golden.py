@@ -39,8 +39,11 @@ import torch.nn.functional as F
 HERE = Path(__file__).resolve().parent
 sys.path.insert(0, str(HERE.parents[1]))
 
+sys.path.insert(0, str(HERE.parent))
+from backbones import gemma_lm, qwen_backbone, to_dtype, to_torch  # noqa: E402
+
 from karpo_decision_b200.synthetic import (  # noqa: E402
-    CONFIGS, Spec, numpy_weights, small, synthetic_block_arrays, synthetic_pack_arrays)
+    CONFIGS, Spec, numpy_weights, small, synthetic_block_arrays, synthetic_lengths, synthetic_pack_arrays)
 
 
 #: The image soft-token id of the image cases (the last vocabulary id; other tokens never take it).
@@ -126,97 +129,6 @@ def import_reference(root: Path) -> None:
         sys.modules["pybase64"] = stub
 
 
-def to_torch(weights: dict[str, np.ndarray], key: str) -> torch.Tensor:
-    return torch.from_numpy(np.ascontiguousarray(weights[key]))
-
-
-def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
-    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5Config
-    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5Model
-
-    rot = int(spec.head_dim * spec.partial_rotary)
-    half = rot // 2
-    section = [half - 2 * (half // 3), half // 3, half // 3]
-    text = dict(vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
-                num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
-                head_dim=spec.head_dim, rms_norm_eps=spec.eps, layer_types=spec.layer_types(),
-                rope_parameters={"rope_type": "default", "rope_theta": spec.rope_theta,
-                                 "partial_rotary_factor": spec.partial_rotary, "mrope_section": section},
-                attention_bias=False, hidden_act="silu", linear_num_key_heads=spec.lin_k_heads,
-                linear_num_value_heads=spec.lin_v_heads, linear_key_head_dim=spec.lin_k_dim,
-                linear_value_head_dim=spec.lin_v_dim, linear_conv_kernel_dim=spec.conv_kernel)
-    config = Qwen3_5Config(text_config=text, vision_config={"depth": 1, "hidden_size": 32, "intermediate_size": 64,
-                                                           "num_heads": 2, "out_hidden_size": spec.hidden})
-    config._attn_implementation = "sdpa"
-    model = Qwen3_5Model(config).float().eval()
-    lm = model.language_model
-    with torch.no_grad():
-        lm.embed_tokens.weight.copy_(to_torch(weights, "embed_tokens"))
-        lm.norm.weight.copy_(to_torch(weights, "norm"))
-        for i, layer in enumerate(lm.layers):
-            p = f"layers.{i}."
-            layer.block_type = layer.layer_type  # harness alias (Transformers 5.5 naming)
-            if layer.layer_type == "linear_attention":
-                la = layer.linear_attn
-                for name in ("in_proj_qkv", "in_proj_z", "in_proj_b", "in_proj_a", "out_proj"):
-                    getattr(la, name).weight.copy_(to_torch(weights, p + "linear_attn." + name))
-                la.conv1d.weight.copy_(to_torch(weights, p + "linear_attn.conv1d")[:, None, :])
-                la.A_log.copy_(to_torch(weights, p + "linear_attn.A_log"))
-                la.dt_bias.copy_(to_torch(weights, p + "linear_attn.dt_bias"))
-                la.norm.weight.copy_(to_torch(weights, p + "linear_attn.norm"))
-            else:
-                a = layer.self_attn
-                for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
-                    getattr(a, name).weight.copy_(to_torch(weights, p + name))
-                a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
-                a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
-            for name in ("gate_proj", "up_proj", "down_proj"):
-                getattr(layer.mlp, name).weight.copy_(to_torch(weights, p + name))
-            layer.input_layernorm.weight.copy_(to_torch(weights, p + "input_layernorm"))
-            layer.post_attention_layernorm.weight.copy_(to_torch(weights, p + "post_attention_layernorm"))
-    return model
-
-
-def gemma_lm(spec: Spec, weights: dict[str, np.ndarray]):
-    from transformers.models.gemma4.configuration_gemma4 import Gemma4TextConfig
-    from transformers.models.gemma4.modeling_gemma4 import Gemma4TextModel
-
-    global_rope = {"rope_type": "default", "rope_theta": spec.rope_theta}
-    if spec.global_rope == "proportional":
-        global_rope = {"rope_type": "proportional", "rope_theta": spec.rope_theta,
-                       "partial_rotary_factor": spec.global_partial_rotary}
-    config = Gemma4TextConfig(
-        vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
-        num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
-        head_dim=spec.head_dim, global_head_dim=spec.global_head_dim or spec.head_dim,
-        num_global_key_value_heads=spec.global_kv_heads or spec.kv_heads, attention_k_eq_v=spec.k_eq_v,
-        sliding_window=spec.window, layer_types=spec.layer_types(),
-        hidden_size_per_layer_input=0, final_logit_softcapping=spec.logit_cap, rms_norm_eps=spec.eps,
-        hidden_activation="gelu_pytorch_tanh",
-        rope_parameters={"sliding_attention": {"rope_type": "default", "rope_theta": spec.rope_theta_local},
-                         "full_attention": global_rope})
-    config._attn_implementation = "sdpa"
-    lm = Gemma4TextModel(config).float().eval()
-    with torch.no_grad():
-        lm.embed_tokens.weight.copy_(to_torch(weights, "embed_tokens"))
-        lm.norm.weight.copy_(to_torch(weights, "norm"))
-        for i, layer in enumerate(lm.layers):
-            p = f"layers.{i}."
-            a = layer.self_attn
-            for name in ("q_proj", "k_proj", "v_proj", "o_proj"):
-                if getattr(a, name) is not None:  # attention_k_eq_v global layers have no v_proj
-                    getattr(a, name).weight.copy_(to_torch(weights, p + name))
-            a.q_norm.weight.copy_(to_torch(weights, p + "q_norm"))
-            a.k_norm.weight.copy_(to_torch(weights, p + "k_norm"))
-            for name in ("gate_proj", "up_proj", "down_proj"):
-                getattr(layer.mlp, name).weight.copy_(to_torch(weights, p + name))
-            for name in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
-                         "post_feedforward_layernorm"):
-                getattr(layer, name).weight.copy_(to_torch(weights, p + name))
-            layer.layer_scalar.copy_(to_torch(weights, p + "layer_scalar"))
-    return lm
-
-
 def encoded(arrays: dict[str, np.ndarray], blocks: bool):
     from karpo_decision.encoding import Encoded
 
@@ -292,6 +204,31 @@ CASES = {
                                blocks=[(23, []), (21, [5, 7, 3]), (14, [4, 9]), (3, [20, 25])], fp8=False),
 }
 
+#: BASELINE configurations 2-5 at full width, depth cut (a layer's arithmetic depends only on its kind, so a few
+#: layers of each kind cover the whole stack), run through the reference's own bf16 path (the backbone cast to bf16,
+#: as it is served) with ``dtype="bf16"``; the float32 run of the same case is stored beside it as the noise
+#: reference. Gemma's vocabulary is cut to 8,192 rows (the configurations do not fix it).
+WIDE = {
+    # config 2: 0.8B Qwen-shaped, 2 layers, ~4k tokens of the [128, 8192] log-uniform mix, 1-4 markers
+    "qwen_0p8b": dict(spec=small(CONFIGS["qwen-0.8b"], layers=2), lengths=("log", 4096, 128, 8192),
+                      markers=(1, 4), fp8=False, dtype="bf16"),
+    # config 3: 4B Qwen-shaped with FP8 projections, 2 layers, ~3k tokens of the [256, 16384] mix
+    "qwen_4b_fp8": dict(spec=small(CONFIGS["qwen-4b"], layers=2), lengths=("log", 3072, 256, 16384, 2),
+                        markers=(1, 4), fp8=True, dtype="bf16"),
+    # config 4: 12B Gemma-shaped, head 256, window 1024, 5 sliding + 1 global layer; sequences one short of, at and
+    # one past the window, and longer ones (the reference's window cases, tests/test_gemma_blocks.py:108-112)
+    "gemma_12b": dict(spec=small(CONFIGS["gemma-12b"], layers=6, vocab=8192),
+                      lengths=("list", 700, 1023, 1024, 1025, 3000), markers=(1, 1), fp8=False, dtype="bf16"),
+    "gemma_12b_fp8": dict(spec=small(CONFIGS["gemma-12b"], layers=6, vocab=8192),
+                          lengths=("list", 1023, 1025, 2048), markers=(1, 1), fp8=True, dtype="bf16"),
+    # config 5: 31B Gemma-shaped with FP8 projections, 6 layers; multi-question requests as a shared block and
+    # branches (shared blocks longer than the window), beside single-block ones
+    "gemma_31b_fp8": dict(spec=small(CONFIGS["gemma-31b"], layers=6, vocab=8192),
+                          blocks=[(1500, [40, 60, 30]), (900, []), (1200, [50, 50]), (300, [])], fp8=True,
+                          dtype="bf16"),
+}
+CASES.update(WIDE)
+
 
 #: FP8 cases also record, for layer 0, each quantized projection's input (e4m3 values and row scales) and output: the
 #: per-projection pin of the FP8 arithmetic (a random deep model amplifies single e4m3 rounding flips, so the end-to-end
@@ -327,18 +264,77 @@ def _name_pins(packed, module) -> None:
             child._pin_name = name.rsplit(".", 1)[-1]
 
 
-def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
+def reference_forward(case: dict, spec: Spec, weights: dict, arrays: dict, seqs: list, features, dtype: str):
+    """(hidden, logits, layer-0 FP8 pins) of the reference's own forward over ``seqs``: the backbone in float32, or
+    cast to bf16 with ``dtype="bf16"`` (the reference's served precision); FP8 cases quantize it with the reference's
+    own ``quantize`` after the cast, as ``--fp8`` does at load."""
     from karpo_decision.model.packed import pack
     from karpo_decision.model.readout import Readout
 
+    head = Readout.from_rows(to_torch(weights, "readout"), cap=spec.logit_cap)
+    cast = torch.bfloat16 if dtype == "bf16" else torch.float32
+    record = dtype == "fp32"
+    captured: dict = {}
+    with torch.inference_mode(), contextlib.ExitStack() as stack:
+        if case["fp8"]:
+            stack.enter_context(_patched(torch, "_scaled_mm", scaled_mm_contract))
+        if spec.family == "qwen":
+            from karpo_decision.families.qwen import packed as qp
+
+            model = to_dtype(qwen_backbone(spec, weights), cast)
+            stack.enter_context(_patched(qp, "_kernels", lambda: (delta_rule_contract, varlen_contract,
+                                                                   conv_contract)))
+            packed = qp.Packed(model, spec.attention)
+            if case["fp8"]:
+                from karpo_decision.serve import qwen_fp8
+                qwen_fp8.quantize(packed)
+                if record:
+                    _name_pins(packed, qwen_fp8)
+                    _record_fp8(stack, qwen_fp8, captured)
+            p = pack(seqs, model, torch.device("cpu"))
+        else:
+            from karpo_decision.families.gemma import packed as gp
+            from karpo_decision.families.gemma import sliding_attention
+
+            lm = to_dtype(gemma_lm(spec, weights), cast)
+            stack.enter_context(_patched(sliding_attention, "varlen_attn", varlen_contract))
+            stack.enter_context(_patched(gp, "sdpa_kernel", lambda *_: contextlib.nullcontext()))
+            backbone = types.SimpleNamespace(language_model=lm, config=types.SimpleNamespace(image_token_id=IMAGE_TOKEN))
+            if features is not None:  # the vision encoder's output, given
+                given = torch.from_numpy(arrays["image_features"]).to(cast)
+                stack.enter_context(_patched(gp.vision, "embed", lambda *_: given))
+            packed = gp.Packed(backbone, spec.attention)
+            if case["fp8"]:
+                from karpo_decision.serve import fp8
+                stack.enter_context(_patched(fp8, "to_e4m3", fp8._rows_e4m3))
+                stack.enter_context(_patched(fp8, "norm_e4m3", fp8._norm_e4m3))
+                stack.enter_context(_patched(fp8, "gelu_mul_e4m3", fp8._gelu_mul_e4m3))
+                fp8.quantize(packed)
+                if record:
+                    _name_pins(packed, fp8)
+                    _record_fp8(stack, fp8, captured)
+            p = pack(seqs, None, torch.device("cpu"))
+        hidden = packed(p)
+        logits = head(hidden)
+    return hidden, logits, captured
+
+
+def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
     spec: Spec = case["spec"]
     weights = numpy_weights(spec, seed)
     if "blocks" in case:
         arrays = synthetic_block_arrays(case["blocks"], spec.vocab, seed + 1)
     else:
-        kind, n, low, high = case["lengths"]
-        rng = np.random.default_rng(seed)
-        lengths = [int(x) for x in rng.integers(low, high + 1, size=n)]
+        kind, *rest = case["lengths"]
+        if kind == "list":
+            lengths = [int(x) for x in rest]
+        elif kind == "log":  # (total, low, high[, lengths seed])
+            total, low, high, *draw = rest
+            lengths = synthetic_lengths(total, low, high, draw[0] if draw else seed, log_uniform=True)
+        else:
+            n, low, high = rest
+            rng = np.random.default_rng(seed)
+            lengths = [int(x) for x in rng.integers(low, high + 1, size=n)]
         arrays = synthetic_pack_arrays(lengths, spec.vocab, seed + 1, case["markers"])
     features = None
     if "images" in case:  # soft tokens (id vocab - 1) over the given (row, length) runs, and their features
@@ -353,58 +349,22 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
     if features is not None:  # the sequences with soft tokens carry (placeholder) pixels, so the pack has images
         seqs = [dataclasses.replace(q, pixel_values=torch.zeros(1, 1), image_position_ids=torch.zeros(1, 1, 2))
                 if bool((q.input_ids == IMAGE_TOKEN).any()) else q for q in seqs]
-    head = Readout.from_rows(to_torch(weights, "readout"), cap=spec.logit_cap)
-    captured: dict = {}
-    with torch.inference_mode(), contextlib.ExitStack() as stack:
-        if case["fp8"]:
-            stack.enter_context(_patched(torch, "_scaled_mm", scaled_mm_contract))
-        if spec.family == "qwen":
-            from karpo_decision.families.qwen import packed as qp
-
-            model = qwen_backbone(spec, weights)
-            stack.enter_context(_patched(qp, "_kernels", lambda: (delta_rule_contract, varlen_contract,
-                                                                   conv_contract)))
-            packed = qp.Packed(model, spec.attention)
-            if case["fp8"]:
-                from karpo_decision.serve import qwen_fp8
-                qwen_fp8.quantize(packed)
-                _name_pins(packed, qwen_fp8)
-                _record_fp8(stack, qwen_fp8, captured)
-            p = pack(seqs, model, torch.device("cpu"))
-        else:
-            from karpo_decision.families.gemma import packed as gp
-            from karpo_decision.families.gemma import sliding_attention
-
-            lm = gemma_lm(spec, weights)
-            stack.enter_context(_patched(sliding_attention, "varlen_attn", varlen_contract))
-            stack.enter_context(_patched(gp, "sdpa_kernel", lambda *_: contextlib.nullcontext()))
-            backbone = types.SimpleNamespace(language_model=lm, config=types.SimpleNamespace(image_token_id=IMAGE_TOKEN))
-            if features is not None:  # the vision encoder's output, given
-                given = torch.from_numpy(arrays["image_features"])
-                stack.enter_context(_patched(gp.vision, "embed", lambda *_: given))
-            packed = gp.Packed(backbone, spec.attention)
-            if case["fp8"]:
-                from karpo_decision.serve import fp8
-                stack.enter_context(_patched(fp8, "to_e4m3", fp8._rows_e4m3))
-                stack.enter_context(_patched(fp8, "norm_e4m3", fp8._norm_e4m3))
-                stack.enter_context(_patched(fp8, "gelu_mul_e4m3", fp8._gelu_mul_e4m3))
-                fp8.quantize(packed)
-                _name_pins(packed, fp8)
-                _record_fp8(stack, fp8, captured)
-            p = pack(seqs, None, torch.device("cpu"))
-        hidden = packed(p)
-        logits = head(hidden)
+    hidden, logits, captured = reference_forward(case, spec, weights, arrays, seqs, features, case.get("dtype", "fp32"))
+    noise = {}
+    if case.get("dtype", "fp32") == "bf16":  # the float32 run of the same case, the noise reference
+        h32, l32, _ = reference_forward(case, spec, weights, arrays, seqs, features, "fp32")
+        noise = {"hidden_fp32": h32.float().numpy(), "logits_fp32": l32.float().numpy()}
     pins = {}
     for proj, (values, scale, out) in captured.items():
         pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
     extra = {k: arrays[k] for k in ("segment_ids", "image_features") if k in arrays}
     return {
-        **pins, **extra,
+        **pins, **extra, **noise,
         "input_ids": arrays["input_ids"], "seqpos": arrays["seqpos"], "cu": arrays["cu"],
         "markers": arrays["markers"], "marker_cu": arrays["marker_cu"],
         "hidden": hidden.float().numpy(), "logits": logits.float().numpy(),
         "seed": np.array(seed), "weights_sha256": np.array(weights_digest(weights)),
-        "spec": np.array(repr(spec.as_dict())),
+        "spec": np.array(repr(spec.as_dict())), "dtype": np.array(case.get("dtype", "fp32")),
     }
 
 

@@ -14,6 +14,8 @@ GOLDEN = Path(__file__).resolve().parent / "golden"
 IMAGE_TOKEN = 4095  # the image cases' soft-token id
 CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_tiny_fp8", "gemma_tiny_fp8", "qwen_bidir",
          "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid", "gemma_images"]
+#: BASELINE configurations 2-5 at full width (depth cut), from the reference's bf16 path (float32 run beside it).
+WIDE = ["qwen_0p8b", "qwen_4b_fp8", "gemma_12b", "gemma_12b_fp8", "gemma_31b_fp8"]
 
 
 def load(name: str) -> tuple[Spec, dict, dict, dict]:
@@ -32,5 +34,6 @@ def load(name: str) -> tuple[Spec, dict, dict, dict]:
             if k in z.files}
     if "image_features" in pack:  # the image cases' soft-token id (tests/golden/make_golden.py IMAGE_TOKEN)
         pack["image_token"] = IMAGE_TOKEN
-    expected = {"hidden": z["hidden"], "logits": z["logits"]}
+    expected = {k: z[k] for k in ("hidden", "logits", "hidden_fp32", "logits_fp32") if k in z.files}
+    expected["dtype"] = str(z["dtype"]) if "dtype" in z.files else "fp32"
     return spec, weights, pack, expected

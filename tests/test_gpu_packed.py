@@ -2,11 +2,12 @@
 reference's float32 CPU path, tests/golden/) and against the oracle run with bf16 rounding at the reference's bf16
 storage points, on the same seeded weights and packs.
 
-Bounds: readout logits within 2e-2 (max-abs) of the reference and the same top answer; the bf16
-noise floor of the reference itself (its bf16 path against its float32 path, from the oracle) is asserted beside it.
-FP8: a random deep model turns single e4m3 rounding flips into visible output changes, so the whole FP8 forward is
-compared by cosine like the reference's own tests (tests/gpu/test_cuda_qwen_fast.py:60-72), while each FP8 kernel is
-checked exactly in test_gpu_kernels.py."""
+Bounds: readout logits within 2e-2 (max-abs) of the reference and the same top answer for every
+readout; the bf16 noise floor of the reference itself (its bf16 path against its float32 path, from the oracle) is
+printed beside it. The FP8 fixtures here come from the reference's ``--fp8`` path run in float32 (its activations
+quantized from float32 values, ours from bf16 ones), so they are compared by cosine; the FP8 bar itself (2e-2 and the
+same top answers against the reference's served bf16 ``--fp8`` path) is asserted at full width in test_gpu_wide.py, and
+each FP8 kernel is checked exactly in test_gpu_kernels.py."""
 
 import numpy as np
 import pytest
@@ -44,7 +45,7 @@ def test_bf16_forward_matches_reference(name):
     err = np.abs(logits - expected["logits"]).max()
     print(f"{name}: readout max-abs vs reference {err:.3g} (reference bf16 noise floor {floor:.3g})")
     assert err <= 2e-2
-    assert (logits.argmax(-1) == expected["logits"].argmax(-1)).mean() >= 0.999 or err <= floor * 2
+    assert np.array_equal(logits.argmax(-1), expected["logits"].argmax(-1))
     cosine = (hidden * expected["hidden"]).sum(-1) / (np.linalg.norm(hidden, axis=-1) *
                                                       np.linalg.norm(expected["hidden"], axis=-1))
     assert cosine.min() > 0.995, cosine

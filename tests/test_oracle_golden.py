@@ -97,3 +97,17 @@ def test_chunked_delta_rule_equals_recurrent():
     for chunk in (64, 16):
         got = oracle.packed.gated_delta_rule_chunked(q, k, v, decay, beta, cu, chunk=chunk)
         assert np.abs(got - want).max() <= 1e-5 * max(1.0, np.abs(want).max())  # measured 7e-7 at 0.4
+
+
+@pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny"])
+def test_cpu_reference_matches_golden(name):
+    """The torch restatement timed as the CPU baseline (oracle/cpu_reference.py) gives the reference's float32
+    readouts, layer by layer composed as the full forward."""
+    import torch
+
+    from oracle.cpu_reference import Model
+
+    spec, weights, arrays, expected = load(name)
+    torch.set_num_threads(4)
+    logits = Model(weights, spec.as_dict()).forward(arrays).numpy()
+    assert np.abs(logits - expected["logits"]).max() <= 2e-4 * max(1.0, np.abs(expected["logits"]).max())
