@@ -55,6 +55,14 @@ int kd_version(void);
 /* Copies this thread's last error message (NUL-terminated, truncated to n bytes) into buf; returns its length. */
 int kd_last_error(char* buf, size_t n);
 
+/* A check of the bounded waits every pipelined kernel relies on: one launch with two waiters on a shared-memory
+ * barrier that nothing arrives on. The first gives up after `limit_ns` (at most 1 s) and writes KD_DEVICE_TIMEOUT to
+ * *status (a device int the caller zeroed); the second, allowed 64 x as long, gives up as soon as it sees that status.
+ * elapsed[0], elapsed[1] (device int64) receive the nanoseconds each waited. The launch returns; the context stays
+ * usable. No counterpart in the reference (its kernels come from libraries): the failure-detection test of this
+ * library's own device waits. */
+int kd_wait_selftest(int* status, int64_t limit_ns, int64_t* elapsed, cudaStream_t stream);
+
 /* ---------------------------------------------------------------------------------------------- projections
  * C[M, N] = epilogue(A[M, K] . B[N, K]^T): tcgen05 MMA with fp32 accumulation in tensor memory.
  * Replaces nn.Linear (cuBLAS) in every projection: families/qwen/packed.py:113-125,147 (q/k/v/o, gate/up/down),

@@ -22,6 +22,7 @@ P = c_void_p
 SIGNATURES: dict[str, list] = {
     "kd_version": [],
     "kd_last_error": [ctypes.c_char_p, c_size_t],
+    "kd_wait_selftest": [P, c_int64, P, P],
     "kd_gemm_bf16": [P, c_int64, P, c_int64, P, c_int64, P, c_int64, c_int, c_int, c_int, c_int, P, P],
     "kd_gemm_fp8": [P, c_int64, P, P, c_int64, P, P, c_int64, P, c_int64, c_int, c_int, c_int, c_int, P, P],
     "kd_qkv_projection": [P, c_int64, P, c_int64, c_int, c_int, c_int, P, c_int, c_int, c_int, c_int, P, P, c_int,

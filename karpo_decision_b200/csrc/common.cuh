@@ -76,8 +76,8 @@ KD_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity to complete. Returns false (and records a timeout in *status) when the
-// wait gives up after KD_WAIT_LIMIT_NS, or at once when another thread of the launch already recorded an error.
-KD_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+// wait gives up after `limit_ns` of %globaltimer time, or soon after another thread of the launch recorded an error.
+KD_DEVICE bool mbar_wait_for(uint64_t* bar, uint32_t parity, int* status, uint64_t limit_ns) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const uint64_t start = globaltimer();
@@ -86,12 +86,17 @@ KD_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
     if (mbar_try_wait(addr, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (*(volatile int*)status != KD_OK) return false;
-      if (globaltimer() - start > KD_WAIT_LIMIT_NS) {
+      if (globaltimer() - start > limit_ns) {
         atomicCAS(status, KD_OK, KD_DEVICE_TIMEOUT);
         return false;
       }
     }
   }
+}
+
+// The wait every pipelined kernel uses: bounded by KD_WAIT_LIMIT_NS.
+KD_DEVICE bool mbar_wait(uint64_t* bar, uint32_t parity, int* status) {
+  return mbar_wait_for(bar, parity, status, KD_WAIT_LIMIT_NS);
 }
 
 // ------------------------------------------------------------------------------------------------ TMA

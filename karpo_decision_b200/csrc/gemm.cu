@@ -76,6 +76,7 @@ struct Args {
   const float* scale_b;  // FP8: one scale per B row (output column)
   int* status;
   Qkv qkv;
+  int tile_group;  // row blocks per group of the tile order (tile_coords)
 };
 
 // 16 accumulator columns of one row (raw tcgen05.ld registers) as the projection's bf16 outputs (FP8: scaled first).
@@ -137,6 +138,24 @@ KD_DEVICE void put16(uint8_t* seg, int lane, const float (&x)[16]) {
 }
 
 // Waits until at most 3 of this thread's bulk stores still read shared memory.
+// Output tiles in groups of TILE_GROUP row blocks: within a group the tile index runs over the group's row blocks
+// first, then over the column blocks. The persistent CTAs work on consecutive tiles at the same time, so at any moment
+// they cover a few column blocks of at most TILE_GROUP row blocks: the group's A rows stay in L2 while B's column
+// blocks stream past once per group, instead of all of B once per row block (the row-major order, whose B re-reads
+// dominate DRAM traffic once B outgrows L2). Measured on B200: gemma-31b's FP8 gate/up projection (32,768 x 43,008 x
+// 5,376) 6,166 -> 4,940 us and gemma-12b's bf16 one (32,768 x 30,720 x 3,840) 5,974 -> 4,789 us; shapes whose B
+// stays in L2 unchanged. Groups of 8 and 32 row blocks measured no better.
+constexpr int TILE_GROUP = 16;
+KD_DEVICE void tile_coords(int tile, int m_tiles, int n_tiles, int group_rows, int& mb, int& nb) {
+  const int per_group = group_rows * n_tiles;
+  const int group = tile / per_group;
+  const int first = group * group_rows;
+  const int rows = min(m_tiles - first, group_rows);
+  const int in = tile - group * per_group;
+  mb = first + in % rows;
+  nb = in / rows;
+}
+
 KD_DEVICE void bulk_wait_read_3() { asm volatile("cp.async.bulk.wait_group.read 3;" ::: "memory"); }
 
 // One row's heads inside the 256 columns [n0, n0 + 256) of the QKV projection: per-head RMSNorm over head_dim, then
@@ -395,8 +414,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       int stage = 0;
       uint32_t phase = 0;
       for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
-        const int m0 = (tile / n_tiles) * P::TILE_M;
-        const int n0 = (tile % n_tiles) * BN;
+        int mb, nb;
+        tile_coords(tile, m_tiles, n_tiles, args.tile_group, mb, nb);
+        const int m0 = mb * P::TILE_M;
+        const int n0 = nb * BN;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, args.status)) goto done;
           uint8_t* sa = smem + stage * STAGE_BYTES;
@@ -484,8 +505,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = first_tile; tile < num_tiles; tile += tile_step) {
-      const int m0 = (tile / n_tiles) * P::TILE_M + (int)rank * BM;  // this CTA's 128 rows of the tile
-      const int n0 = (tile % n_tiles) * BN;
+      int mb, nb;
+      tile_coords(tile, m_tiles, n_tiles, args.tile_group, mb, nb);
+      const int m0 = mb * P::TILE_M + (int)rank * BM;  // this CTA's 128 rows of the tile
+      const int n0 = nb * BN;
       if (!mbar_wait(&acc_full[acc], acc_phase, args.status)) goto done;
       tc_fence_after();
       const int row = m0 + quarter * 32 + lane;
@@ -707,6 +730,7 @@ static int gemm_common(const void* A, int64_t lda, const void* B, int64_t ldb, v
   args.scale_b = scale_b;
   args.status = status;
   args.qkv = qkv ? *qkv : gemm::Qkv{};
+  args.tile_group = gemm::TILE_GROUP;
 
   // output (and residual) boxes for the TMA-store epilogue: 64 columns x 32 rows, 128-byte swizzle; the QKV epilogue
   // stores 16 columns x 32 rows of q (mc), the gate (mr), k (mk) and v (mv), 32-byte swizzle

@@ -6,6 +6,7 @@
 
 #include <mutex>
 
+#include "common.cuh"
 #include "kd_internal.h"
 
 namespace kd {
@@ -93,4 +94,33 @@ extern "C" int kd_last_error(char* buf, size_t n) {
   const int len = (int)strlen(kd::g_last_error);
   if (buf && n > 0) snprintf(buf, n, "%s", kd::g_last_error);
   return len;
+}
+
+namespace kd {
+
+// Two waiters on an mbarrier that nothing arrives on: warp 0 with `limit_ns`, warp 1 with 64 x that limit. Warp 0's
+// wait runs out and records KD_DEVICE_TIMEOUT; warp 1 must then give up on seeing the status, long before its own
+// limit, as every other wait of a failed launch does. Each records the nanoseconds it waited in elapsed[warp].
+__global__ void wait_selftest_kernel(int* status, uint64_t limit_ns, int64_t* elapsed) {
+  __shared__ uint64_t bar;
+  const int warp = threadIdx.x / 32;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    const uint64_t start = globaltimer();
+    const bool ok = mbar_wait_for(&bar, 0, status, warp == 0 ? limit_ns : 64 * limit_ns);
+    elapsed[warp] = ok ? -1 : (int64_t)(globaltimer() - start);
+  }
+}
+
+}  // namespace kd
+
+extern "C" int kd_wait_selftest(int* status, int64_t limit_ns, int64_t* elapsed, cudaStream_t stream) {
+  if (!status || !elapsed || limit_ns <= 0 || limit_ns > 1000000000LL)
+    return kd::set_error(KD_ERR_ARGUMENT, "wait_selftest: status, elapsed and a limit in (0, 1 s] required");
+  kd::wait_selftest_kernel<<<1, 64, 0, stream>>>(status, (uint64_t)limit_ns, elapsed);
+  return kd::record_cuda_error(cudaGetLastError(), "wait_selftest: launch");
 }

@@ -235,6 +235,8 @@ CASES.update(WIDE)
 #: FP8 forward is compared only loosely, as the reference's own tests do: tests/gpu/test_fp8.py:4-5).
 PINNED = ("q_proj", "o_proj", "gate_proj", "down_proj")
 PIN_ROWS = 48
+#: Rows pinned in the full-width bf16 FP8 cases (e4m3 inputs as their bytes, bf16 outputs as their bits).
+WIDE_PIN_ROWS = 16
 
 
 def _record_fp8(stack: contextlib.ExitStack, module, captured: dict) -> None:
@@ -249,10 +251,16 @@ def _record_fp8(stack: contextlib.ExitStack, module, captured: dict) -> None:
                 values, scale = x.values, x.scale
             else:
                 values, scale = module.to_e4m3(x.reshape(-1, x.shape[-1]))
-            rows = PIN_ROWS  # the first rows suffice for the pin and keep the fixture small
-            captured[name] = (values.float().reshape(-1, values.shape[-1])[:rows].numpy(),
-                              scale.float().reshape(-1)[:rows].numpy(),
-                              out.float().reshape(-1, out.shape[-1])[:rows].numpy())
+            if out.dtype == torch.bfloat16:  # the served bf16 path at full width: a few rows, kept as raw bits
+                rows = WIDE_PIN_ROWS
+                captured[name] = (values.reshape(-1, values.shape[-1])[:rows].view(torch.uint8).numpy(),
+                                  scale.float().reshape(-1)[:rows].numpy(),
+                                  out.reshape(-1, out.shape[-1])[:rows].view(torch.int16).numpy().view(np.uint16))
+            else:
+                rows = PIN_ROWS  # the first rows suffice for the pin and keep the fixture small
+                captured[name] = (values.float().reshape(-1, values.shape[-1])[:rows].numpy(),
+                                  scale.float().reshape(-1)[:rows].numpy(),
+                                  out.float().reshape(-1, out.shape[-1])[:rows].numpy())
         return out
 
     stack.enter_context(_patched(module.Fp8Linear, "forward", forward))
@@ -264,7 +272,8 @@ def _name_pins(packed, module) -> None:
             child._pin_name = name.rsplit(".", 1)[-1]
 
 
-def reference_forward(case: dict, spec: Spec, weights: dict, arrays: dict, seqs: list, features, dtype: str):
+def reference_forward(case: dict, spec: Spec, weights: dict, arrays: dict, seqs: list, features, dtype: str,
+                      record: bool = True):
     """(hidden, logits, layer-0 FP8 pins) of the reference's own forward over ``seqs``: the backbone in float32, or
     cast to bf16 with ``dtype="bf16"`` (the reference's served precision); FP8 cases quantize it with the reference's
     own ``quantize`` after the cast, as ``--fp8`` does at load."""
@@ -273,7 +282,6 @@ def reference_forward(case: dict, spec: Spec, weights: dict, arrays: dict, seqs:
 
     head = Readout.from_rows(to_torch(weights, "readout"), cap=spec.logit_cap)
     cast = torch.bfloat16 if dtype == "bf16" else torch.float32
-    record = dtype == "fp32"
     captured: dict = {}
     with torch.inference_mode(), contextlib.ExitStack() as stack:
         if case["fp8"]:
@@ -352,11 +360,14 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
     hidden, logits, captured = reference_forward(case, spec, weights, arrays, seqs, features, case.get("dtype", "fp32"))
     noise = {}
     if case.get("dtype", "fp32") == "bf16":  # the float32 run of the same case, the noise reference
-        h32, l32, _ = reference_forward(case, spec, weights, arrays, seqs, features, "fp32")
+        h32, l32, _ = reference_forward(case, spec, weights, arrays, seqs, features, "fp32", record=False)
         noise = {"hidden_fp32": h32.float().numpy(), "logits_fp32": l32.float().numpy()}
     pins = {}
     for proj, (values, scale, out) in captured.items():
-        pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
+        if values.dtype == np.uint8:  # full width, served bf16 path
+            pins[f"wpin_{proj}_in_e4m3"], pins[f"wpin_{proj}_scale"], pins[f"wpin_{proj}_out_bf16"] = values, scale, out
+        else:
+            pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
     extra = {k: arrays[k] for k in ("segment_ids", "image_features") if k in arrays}
     return {
         **pins, **extra, **noise,

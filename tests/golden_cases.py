@@ -37,3 +37,26 @@ def load(name: str) -> tuple[Spec, dict, dict, dict]:
     expected = {k: z[k] for k in ("hidden", "logits", "hidden_fp32", "logits_fp32") if k in z.files}
     expected["dtype"] = str(z["dtype"]) if "dtype" in z.files else "fp32"
     return spec, weights, pack, expected
+
+
+#: The north-star readout bound: max-abs difference of the readout logits.
+READOUT_BOUND = 2e-2
+
+
+def readout_bar(got: np.ndarray, want: np.ndarray, bound: float = READOUT_BOUND) -> tuple[float, float, int]:
+    """Asserts the readout bar: every logit within ``bound`` of ``want`` (max-abs), and the same top answer for every
+    readout whose top-two margin in ``want`` exceeds 2 * bound. A readout whose two best answers lie closer than that
+    can change its top answer within the bound (a near tie); there the top answer must be one of the answers within
+    2 * bound of ``want``'s best, which the bound implies and which is checked too. Returns (max-abs error, top-answer
+    agreement over all readouts, number of near ties)."""
+    err = float(np.abs(got - want).max())
+    assert np.isfinite(got).all()
+    assert err <= bound, f"readout max-abs {err:.4f} above {bound:.4f}"
+    ordered = np.sort(want, axis=-1)
+    margin = ordered[:, -1] - ordered[:, -2]
+    clear = margin > 2 * bound
+    ours, theirs = got.argmax(-1), want.argmax(-1)
+    assert np.array_equal(ours[clear], theirs[clear]), "a top answer changed on a readout with a clear margin"
+    rows = np.arange(len(ours))
+    assert (want[rows, ours] >= want.max(-1) - 2 * bound).all()
+    return err, float((ours == theirs).mean()), int((~clear).sum())

@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from backbones import to_dtype
-from golden_cases import load
+from golden_cases import READOUT_BOUND, load, readout_bar
 from karpo_decision_b200 import Packed, Readout, from_arrays
 from test_dropin import DROPIN_CASES, backbone_of
 
@@ -61,8 +61,13 @@ def test_forward_through_the_drop_in_constructors(name):
     logits = head(hidden).cpu().numpy()
     direct = Packed(spec, weights, DEV, fp8=fp8)(from_arrays(arrays, DEV))
     assert torch.equal(hidden, direct)  # the same weights in the same layouts: the same bits
-    err = float(np.abs(logits - expected["logits"]).max())
-    print(f"{name}: readout through from_backbone / from_reference, max-abs vs reference {err:.4f}")
-    if not fp8:  # the FP8 cases' fixtures are the float32 FP8 forward, compared in test_gpu_packed.py
-        assert err <= 2e-2
-        assert np.array_equal(logits.argmax(-1), expected["logits"].argmax(-1))
+    if fp8:  # the tiny FP8 fixtures are the float32 FP8 forward, compared in test_gpu_packed.py
+        return
+    want = expected["logits"]
+    bound = READOUT_BOUND
+    if "logits_fp32" in expected:  # full width: the reference's own bf16 noise (test_gpu_wide.py)
+        want = expected["logits_fp32"]
+        bound = max(READOUT_BOUND, 1.25 * float(np.abs(expected["logits"] - want).max()))
+    err, agree, ties = readout_bar(logits, want, bound)
+    print(f"{name}: readout through from_backbone / from_reference, max-abs vs reference {err:.4f}, top answers "
+          f"agree on {agree:.1%} ({ties} near ties)")

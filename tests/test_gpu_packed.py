@@ -2,9 +2,10 @@
 reference's float32 CPU path, tests/golden/) and against the oracle run with bf16 rounding at the reference's bf16
 storage points, on the same seeded weights and packs.
 
-Bounds: readout logits within 2e-2 (max-abs) of the reference and the same top answer for every
-readout; the bf16 noise floor of the reference itself (its bf16 path against its float32 path, from the oracle) is
-printed beside it. The FP8 fixtures here come from the reference's ``--fp8`` path run in float32 (its activations
+Bounds (``golden_cases.readout_bar``): readout logits within 2e-2 (max-abs) of the reference, and
+the same top answer wherever the reference's two best answers are more than twice that apart (closer ones are near
+ties the bound lets change); the bf16 noise floor of the reference itself (its bf16 path against its float32 path,
+from the oracle) is printed beside it. The FP8 fixtures here come from the reference's ``--fp8`` path run in float32 (its activations
 quantized from float32 values, ours from bf16 ones), so they are compared by cosine; the FP8 bar itself (2e-2 and the
 same top answers against the reference's served bf16 ``--fp8`` path) is asserted at full width in test_gpu_wide.py, and
 each FP8 kernel is checked exactly in test_gpu_kernels.py."""
@@ -14,7 +15,7 @@ import pytest
 import torch
 
 import oracle
-from golden_cases import load
+from golden_cases import load, readout_bar
 from karpo_decision_b200 import Packed, Readout, from_arrays
 
 pytestmark = pytest.mark.gpu
@@ -42,10 +43,9 @@ def test_bf16_forward_matches_reference(name):
     noise = forward(weights, spec.as_dict(), arrays, mode="bf16")
     noise_logits = oracle.readout(noise, weights["readout"], spec.logit_cap)
     floor = np.abs(noise_logits - expected["logits"]).max()
-    err = np.abs(logits - expected["logits"]).max()
-    print(f"{name}: readout max-abs vs reference {err:.3g} (reference bf16 noise floor {floor:.3g})")
-    assert err <= 2e-2
-    assert np.array_equal(logits.argmax(-1), expected["logits"].argmax(-1))
+    err, agree, ties = readout_bar(logits, expected["logits"])
+    print(f"{name}: readout max-abs vs reference {err:.3g} (reference bf16 noise floor {floor:.3g}), top answers "
+          f"agree on {agree:.1%} of {len(logits)} readouts ({ties} near ties)")
     cosine = (hidden * expected["hidden"]).sum(-1) / (np.linalg.norm(hidden, axis=-1) *
                                                       np.linalg.norm(expected["hidden"], axis=-1))
     assert cosine.min() > 0.995, cosine
@@ -129,8 +129,7 @@ def test_gemma_images_match_reference():
     p = from_arrays(dict(arrays, pixel_values=arrays["image_features"]), DEV)
     hidden = model(p)
     logits = head(hidden).cpu().numpy()
-    err = np.abs(logits - expected["logits"]).max()
-    assert err <= 2e-2, err
+    readout_bar(logits, expected["logits"])
     h = hidden.float().cpu().numpy()
     cosine = (h * expected["hidden"]).sum(-1) / (np.linalg.norm(h, axis=-1) * np.linalg.norm(expected["hidden"],
                                                                                                axis=-1))
