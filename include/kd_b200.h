@@ -213,12 +213,17 @@ int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const void* weigh
  * start, per token S = exp(g) S, d = beta (v - S^T k), S += k d^T, o = S^T q; with g = -exp(A_log)
  * softplus(a + dt_bias) in float32 and beta = sigmoid(b) rounded to bf16 (families/qwen/fused.py:42-44).
  * qkv rows [q Hk*dk | k Hk*dk | v Hv*dv] bf16 (the convolution's output); ab rows [b Hv | a Hv] bf16; a_log,
- * dt_bias bf16 [Hv]; out bf16 (T, Hv*dv). dk, dv in {64, 128}.
+ * dt_bias bf16 [Hv]; out bf16 (T, Hv*dv). dk, dv in {64, 128}. dk = dv = 128 (Qwen3.5) runs the chunked form on the
+ * tensor cores (128-token chunks: K K^T, the unit-lower-triangular inverse, W and U, then the state step per chunk with
+ * S in tensor memory; bf16 operands, fp32 accumulation, as flash-linear-attention's chunked kernels compute it);
+ * `status` is its device status word (KD_DEVICE_TIMEOUT when a wait gave up). The other head dims run the recurrent
+ * form on the CUDA cores.
  * Replaces flash-linear-attention's chunk_gated_delta_rule (use_qk_l2norm_in_kernel, cu_seqlens) as
  * families/qwen/packed.py:88-103 calls it. */
 int kd_gated_delta_rule(const void* qkv, int64_t ldqkv, const void* ab, int64_t ldab, const void* a_log,
                         const void* dt_bias, const int32_t* cu, int num_seqs, int64_t T, int num_k_heads,
-                        int num_v_heads, int head_k_dim, int head_v_dim, void* out, int64_t ldo, cudaStream_t stream);
+                        int num_v_heads, int head_k_dim, int head_v_dim, void* out, int64_t ldo, int* status,
+                        cudaStream_t stream);
 
 /* Qwen3_5RMSNormGated per (token, head) of head_dim values: out = bf16(bf16(w * bf16(x rsqrt(mean(x^2) + eps))) *
  * silu(z)) (families/qwen/fused.py:28-31). head_dim 64 or 128. */

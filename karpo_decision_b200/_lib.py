@@ -47,7 +47,7 @@ SIGNATURES: dict[str, list] = {
     "kd_scatter_rows": [P, c_int64, P, c_int64, c_int, P, c_int64, P],
     "kd_conv_silu": [P, c_int64, c_int64, c_int, P, c_int, P, P, c_int64, P],
     "kd_gated_delta_rule": [P, c_int64, P, c_int64, P, P, P, c_int, c_int64, c_int, c_int, c_int, c_int, P, c_int64,
-                            P],
+                            P, P],
     "kd_gated_norm": [P, c_int64, P, c_int64, P, c_int64, c_int, c_int, c_float, P, c_int64, P],
     "kd_marker_norm": [P, c_int, P, c_int64, P, c_int, c_float, P, P],
     "kd_readout": [P, c_int64, c_int, P, c_int, c_float, P, P],

@@ -329,6 +329,523 @@ int launch_delta(const Args& a, int num_seqs, cudaStream_t stream) {
   return record_cuda_error(cudaGetLastError(), "gated_delta_rule: launch");
 }
 
+// ------------------------------------------------------------------------------------------------ chunked form
+//
+// The gated delta rule in its chunked (WY) form on the tensor cores, for 128-dim key and value heads (Qwen3.5's), the
+// form flash-linear-attention's chunk_gated_delta_rule evaluates. One CTA walks one (sequence, value head) chain chunk
+// by chunk, 128 tokens a chunk (one token per thread and TMEM lane), the state S (dk x dv, float32) in tensor memory.
+// Per chunk, with G the running sum of the log decays g from the chunk's start and beta the write strengths (tensor
+// memory: two 128-column accumulators, the state, and the float32 columns of the triangular solve):
+//   K K^T, Q K^T                       tcgen05, bf16 operands, fp32 in TMEM
+//   A = strictly lower (beta_i (K K^T)_ij exp(G_i - G_j)),  P = (Q K^T)_ij exp(G_i - G_j) for j <= i
+//   T = (I + A)^-1                     its two 64 x 64 diagonal blocks T_bd by forward substitution on the CUDA
+//                                      cores (float32, a column per thread), then T = T_bd - T_bd L T_bd with L the
+//                                      lower-left block of A, applied on the tensor cores
+//   W = T diag(beta exp(G)) K,  U = T diag(beta) V         tcgen05
+//   D = U - W S                        tcgen05 (W S), the difference in float32
+//   O = diag(exp(G)) Q S + P D         tcgen05, both products into one accumulator
+//   S = exp(G_last) S + (diag(exp(G_last - G)) K)^T D     the rescale in TMEM, then tcgen05 accumulating into S
+// Queries and keys are L2-normalized (eps 1e-6) and the queries scaled by dk^-1/2 first, as in the recurrent form.
+// Every phase is one MMA issue by thread 0 and a bounded wait on its completion by the whole CTA; on a wait that gives
+// up the CTA records KD_DEVICE_TIMEOUT, frees its tensor memory and returns.
+namespace ck {
+
+// 2^x on the exponential unit (relative error ~2^-22), for the decay factors exp(G_i - G_j) <= 1.
+KD_DEVICE float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+constexpr int C = 128;                // tokens per chunk = MMA rows = TMEM lanes = threads
+constexpr int HD = 128;               // key and value head dim
+constexpr int THREADS = 128;
+constexpr int TILE = C * HD * 2;      // a 128 x 128 bf16 tile: two 64-column halves
+constexpr int HALF = C * 128;         // one half: 128 rows of 128 bytes (128-byte swizzle)
+constexpr int A_FLOATS = 8320;        // the strictly lower A, each row padded to a multiple of 4 floats
+constexpr int A_OFF = 6 * TILE;
+constexpr int G_OFF = A_OFF + A_FLOATS * 4;
+constexpr int MISC_OFF = G_OFF + C * 4;
+constexpr int SMEM = MISC_OFF + 64 + 1024;  // + alignment of the tiles to 1024 bytes
+static_assert(SMEM <= 227 * 1024, "shared memory budget");
+// tiles: kn then P (K-major A) | qn then q~ (K-major A) | X_w = beta e^G kn (MN-major B) then W (K-major A) |
+// X_u = beta v (MN-major B) then S (MN-major B) | k~ = e^(G_last - G) kn (MN-major A) | T (K-major A)
+enum { R_KP = 0, R_Q = 1, R_XW = 2, R_XU = 3, R_KT = 4, R_T = 5 };
+constexpr uint32_t ACC0 = 0, ACC1 = 128, SST = 256, TCOL = 384, TMEM_COLS = 512;
+
+// First float of row j of the packed A: sum over r < j of r rounded up to a multiple of 4.
+KD_DEVICE constexpr int a_row(int j) {
+  const int n = j + 2, q = n >> 2, b = n & 3;
+  return 4 * (2 * q * (q - 1) + q * (b + 1));
+}
+
+// Byte offset of 16-byte unit u (0..15, eight bf16 each) of row r in a 128 x 128 tile stored as a TMA load with
+// 128-byte swizzling writes it (64-column halves of 128-byte rows, unit index XOR row % 8).
+KD_DEVICE uint32_t unit_at(int r, int u) { return (u >> 3) * HALF + r * 128 + (((u & 7) ^ (r & 7)) << 4); }
+
+KD_DEVICE constexpr uint32_t idesc(uint32_t a_mn, uint32_t b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (a_mn << 15) | (b_mn << 16) | ((uint32_t)(HD >> 3) << 17) |
+         ((uint32_t)(C >> 4) << 24);
+}
+
+// D (+)= A B^T over K = 128 in eight K = 16 steps; A and B each K-major (rows of 128-byte swizzled K) or MN-major
+// (one row per K index, 64 M/N elements per 128 bytes, the second half 16 KB on).
+KD_DEVICE void mma128(uint32_t d, uint32_t a, bool a_mn, uint32_t b, bool b_mn, bool accumulate, bool neg_a = false) {
+  const uint32_t id = idesc(a_mn ? 1u : 0u, b_mn ? 1u : 0u) | (neg_a ? (1u << 13) : 0u);  // bit 13: negate A
+#pragma unroll
+  for (int kk = 0; kk < HD / 16; ++kk) {
+    const uint64_t ad = a_mn ? sw128_mnmajor_desc(a + kk * 2048, HALF) : sw128_kmajor_desc(a + (kk / 4) * HALF + (kk % 4) * 32);
+    const uint64_t bd = b_mn ? sw128_mnmajor_desc(b + kk * 2048, HALF) : sw128_kmajor_desc(b + (kk / 4) * HALF + (kk % 4) * 32);
+    mma_f16_ss(d, ad, bd, id, (accumulate || kk > 0) ? 1u : 0u);
+  }
+}
+
+// Row r of a tile from 128 floats times `s`, rounded to bf16 (units in order, 16 bytes at a time).
+KD_DEVICE void put_row(uint8_t* tile, int r, const uint4 (&raw)[16], float s) {
+#pragma unroll
+  for (int u = 0; u < 16; ++u) {
+    const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 f = unpack_bf16x2(w[e]);
+      o[e] = pack_bf16x2(f.x * s, f.y * s);
+    }
+    *reinterpret_cast<uint4*>(tile + unit_at(r, u)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+// 32 accumulator columns [32 cc, 32 cc + 32) of this thread's row, as bf16 into units 4 cc .. 4 cc + 3 of row r.
+KD_DEVICE void put_cols(uint8_t* tile, int r, int cc, const float* x) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = pack_bf16x2(x[8 * q + 2 * e], x[8 * q + 2 * e + 1]);
+    *reinterpret_cast<uint4*>(tile + unit_at(r, 4 * cc + q)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    chunked_delta_kernel(const __grid_constant__ CUtensorMap map_qkv, Args a, int* status) {
+  extern __shared__ uint8_t raw_smem[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(raw_smem) + 1023) & ~uintptr_t(1023));
+  uint8_t* tile_kp = sm + R_KP * TILE;
+  uint8_t* tile_q = sm + R_Q * TILE;
+  uint8_t* tile_xw = sm + R_XW * TILE;
+  uint8_t* tile_xu = sm + R_XU * TILE;
+  uint8_t* tile_kt = sm + R_KT * TILE;
+  uint8_t* tile_t = sm + R_T * TILE;
+  float* apk = reinterpret_cast<float*>(sm + A_OFF);
+  uint8_t* tile_d = sm + A_OFF;  // D reuses A's space once T is built
+  float* g_s = reinterpret_cast<float*>(sm + G_OFF);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(sm + MISC_OFF);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + MISC_OFF + 8);
+  int* seq_s = reinterpret_cast<int*>(sm + MISC_OFF + 12);
+  float* wtot = reinterpret_cast<float*>(sm + MISC_OFF + 16);  // [4]
+  uint64_t* load_bar = reinterpret_cast<uint64_t*>(sm + MISC_OFF + 32);
+
+  const int i = threadIdx.x, warp = i >> 5, lane = i & 31;
+  // the chain: value head `head` of the `rank`-th longest sequence (ties in pack order), so long chains start first
+  const int rank = blockIdx.x / a.nv, head = blockIdx.x % a.nv;
+  if (i == 0) {
+    *seq_s = rank;
+    mbar_init(bar, 1);
+    mbar_init(load_bar, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&map_qkv);
+  }
+  __syncthreads();
+  for (int s0 = i; s0 < a.num_seqs; s0 += THREADS) {
+    const int len = a.cu[s0 + 1] - a.cu[s0];
+    int before = 0;
+    for (int s1 = 0; s1 < a.num_seqs; ++s1) {
+      const int l1 = a.cu[s1 + 1] - a.cu[s1];
+      before += (l1 > len) || (l1 == len && s1 < s0);
+    }
+    if (before == rank) *seq_s = s0;
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  const int seq = *seq_s;
+  const int64_t t0 = a.cu[seq], t1 = a.cu[seq + 1];
+  const int khead = head / (a.nv / a.nk);
+  const float qscale = rsqrtf((float)HD);
+  const float decay_a = -expf(__bfloat162float(a.a_log[head]));
+  const float dt_bias = __bfloat162float(a.dt_bias[head]);
+  const int64_t kd = (int64_t)a.nk * HD;
+  const uint32_t s_kp = smem_u32(tile_kp), s_q = smem_u32(tile_q), s_xw = smem_u32(tile_xw),
+                 s_xu = smem_u32(tile_xu), s_kt = smem_u32(tile_kt), s_t = smem_u32(tile_t),
+                 s_d = smem_u32(tile_d);
+  uint32_t phase = 0, load_phase = 0;
+  bool ok = true;
+  // the raw k, q and v rows of the chunk at c0: k into kn's tile, q into qn's, v into X_u's (128-row boxes of 64
+  // columns; rows past the pack read as zero, rows of the next sequence are overwritten by the threads past n)
+  auto load_chunk = [&](int64_t c0) {
+    mbar_arrive_expect_tx(load_bar, 3 * TILE);
+    const int y = (int)c0;
+    for (int h = 0; h < 2; ++h) {
+      tma_load_2d(&map_qkv, load_bar, tile_kp + h * HALF, (int)(kd + (int64_t)khead * HD) + 64 * h, y);
+      tma_load_2d(&map_qkv, load_bar, tile_q + h * HALF, khead * HD + 64 * h, y);
+      tma_load_2d(&map_qkv, load_bar, tile_xu + h * HALF, (int)(2 * kd + (int64_t)head * HD) + 64 * h, y);
+    }
+  };
+  // one MMA group's completion, agreed by the whole CTA (a wait that gives up ends every thread's walk together)
+  auto wait_mma = [&]() -> bool {
+    bool mine = mbar_wait(bar, phase, status);
+    phase ^= 1u;
+    tc_fence_after();
+    return __syncthreads_and(mine) != 0;
+  };
+  {  // S = 0
+    uint32_t z[32];
+#pragma unroll
+    for (int e = 0; e < 32; ++e) z[e] = 0u;
+#pragma unroll
+    for (int cc = 0; cc < 4; ++cc) tmem_st32(lane_base + SST + 32 * cc, z);
+    tmem_st_wait();
+  }
+  if (i == 0 && t0 < t1) load_chunk(t0);
+
+  for (int64_t c0 = t0; c0 < t1 && ok; c0 += C) {
+    const int n = t1 - c0 < C ? (int)(t1 - c0) : C;
+    const bool live = i < n;
+    // ---------------------------------------------------------------- this row's decay, write strength, q, k, v
+    float g = 0.f, beta = 0.f;
+    if (live) {
+      const __nv_bfloat16* abr = a.ab + (c0 + i) * a.ldab;
+      beta = bf16_round(1.0f / (1.0f + expf(-__bfloat162float(abr[head]))));
+      g = decay_a * softplus(__bfloat162float(abr[a.nv + head]) + dt_bias);
+    }
+    float gi = g;  // inclusive running sum over the chunk's rows
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, gi, o);
+      if (lane >= o) gi += y;
+    }
+    if (lane == 31) wtot[warp] = gi;
+    __syncthreads();
+    for (int w2 = 0; w2 < warp; ++w2) gi += wtot[w2];
+    g_s[i] = gi;
+    __syncthreads();
+    const float g_last = g_s[n - 1];
+    const float e_g = live ? expf(gi) : 0.f, e_tail = live ? expf(g_last - gi) : 0.f;
+    {
+      const bool loaded = mbar_wait(load_bar, load_phase, status);
+      load_phase ^= 1u;
+      if (!(ok = __syncthreads_and(loaded) != 0)) break;
+      uint4 rk[16];
+      auto take = [&](uint8_t* tile) -> float {  // this row of a tile (zeros past n), and its sum of squares
+        float ss = 0.f;
+#pragma unroll
+        for (int u = 0; u < 16; ++u) {
+          rk[u] = live ? *reinterpret_cast<const uint4*>(tile + unit_at(i, u)) : make_uint4(0, 0, 0, 0);
+          const uint32_t w[4] = {rk[u].x, rk[u].y, rk[u].z, rk[u].w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float2 f = unpack_bf16x2(w[e]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+        return ss;
+      };
+      const float ik = rsqrtf(take(tile_kp) + 1e-6f);
+      put_row(tile_kp, i, rk, ik);
+      put_row(tile_xw, i, rk, ik * beta * e_g);
+      put_row(tile_kt, i, rk, ik * e_tail);
+      const float iq = rsqrtf(take(tile_q) + 1e-6f) * qscale;
+      put_row(tile_q, i, rk, iq);
+      take(tile_xu);
+      put_row(tile_xu, i, rk, beta);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---------------------------------------------------------------- K K^T -> ACC0, Q K^T -> ACC1
+    if (i == 0) {
+      tc_fence_after();
+      mma128(tmem + ACC0, s_kp, false, s_kp, false, false);
+      mma128(tmem + ACC1, s_q, false, s_kp, false, false);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+    {  // this row of A (packed, float32) and of P (bf16 over kn's tile); q~ = e^G qn in place
+      float* arow = apk + a_row(i);
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t kk[32], qk[32];
+        tmem_ld32(lane_base + ACC0 + 32 * cc, kk);
+        tmem_ld32(lane_base + ACC1 + 32 * cc, qk);
+        tmem_ld_wait_regs(kk, qk);
+        float p[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) {
+          const int j = 32 * cc + e;
+          const float dec = (j <= i && live) ? fast_exp2((gi - g_s[j]) * 1.4426950408889634f) : 0.f;
+          if (j < i) arow[j] = beta * __uint_as_float(kk[e]) * dec;
+          p[e] = __uint_as_float(qk[e]) * dec;
+        }
+        put_cols(tile_kp, i, cc, p);
+      }
+      for (int j = i; j < ((i + 3) & ~3); ++j) arow[j] = 0.f;  // the row's padding
+#pragma unroll
+      for (int u = 0; u < 16; ++u) {
+        uint4* at = reinterpret_cast<uint4*>(tile_q + unit_at(i, u));
+        const uint4 v = *at;
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float2 f = unpack_bf16x2(w[e]);
+          o[e] = pack_bf16x2(f.x * e_g, f.y * e_g);
+        }
+        *at = make_uint4(o[0], o[1], o[2], o[3]);
+      }
+    }
+    __syncthreads();
+    {  // T_bd = blockdiag((I + A_11)^-1, (I + A_22)^-1) over the two 64-row halves, by forward substitution: this
+       // thread's column c = i of its half, by blocks of 16 rows (first every earlier block's contribution to the
+       // block's rows, 16 independent sums, then the block's own rows in order). The column's float32 values live in
+       // this thread's own lane of tensor memory (columns TCOL + row), read 16 at a time, so the loops stay rolled.
+      const uint32_t tcol = lane_base + TCOL;
+      const int base = i & ~63;  // the half this column belongs to
+#pragma unroll 1
+      for (int b = 0; b < 4; ++b) {
+        const int row0 = base + 16 * b;
+        float acc[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) acc[r] = (row0 + r == i) ? 1.f : 0.f;
+#pragma unroll 1
+        for (int m0 = base; m0 < row0; m0 += 16) {
+          uint32_t tv[16];
+          tmem_ld16(tcol + m0, tv);
+          tmem_ld_wait_regs(tv);
+#pragma unroll
+          for (int r = 0; r < 16; ++r) {
+            const float* arow = apk + a_row(row0 + r) + m0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const float4 av = *reinterpret_cast<const float4*>(arow + 4 * q);
+              acc[r] = fmaf(-av.x, __uint_as_float(tv[4 * q]), acc[r]);
+              acc[r] = fmaf(-av.y, __uint_as_float(tv[4 * q + 1]), acc[r]);
+              acc[r] = fmaf(-av.z, __uint_as_float(tv[4 * q + 2]), acc[r]);
+              acc[r] = fmaf(-av.w, __uint_as_float(tv[4 * q + 3]), acc[r]);
+            }
+          }
+        }
+        uint32_t tb[16];
+#pragma unroll
+        for (int r = 0; r < 16; ++r) {
+          const float* arow = apk + a_row(row0 + r) + row0;
+          float v = acc[r];
+#pragma unroll
+          for (int r2 = 0; r2 < r; ++r2) v = fmaf(-arow[r2], __uint_as_float(tb[r2]), v);
+          tb[r] = __float_as_uint(v);
+        }
+        tmem_st16(tcol + row0, tb);
+        tmem_st_wait();
+      }
+      // column c of T_bd (bf16) into the K-major A tile: its half's 64 rows, zeros in the other half's rows
+      __nv_bfloat16* col = reinterpret_cast<__nv_bfloat16*>(tile_t);
+#pragma unroll 1
+      for (int j0 = 0; j0 < C; j0 += 32) {
+        uint32_t tv[32];
+        const bool mine = (j0 & ~63) == base;
+        if (mine) {
+          tmem_ld32(tcol + j0, tv);
+          tmem_ld_wait_regs(tv);
+        }
+#pragma unroll
+        for (int e = 0; e < 32; ++e)
+          col[(unit_at(j0 + e, i >> 3) >> 1) + (i & 7)] = __float2bfloat16_rn(mine ? __uint_as_float(tv[e]) : 0.f);
+      }
+      // L = A's lower-left 64 x 64 block (rows 64.., columns ..63) as a bf16 K-major tile over A's space, zeros
+      // elsewhere: every thread reads its row first, then all write
+      float lrow[64];
+#pragma unroll
+      for (int m = 0; m < 64; ++m) lrow[m] = i >= 64 ? apk[a_row(i) + m] : 0.f;
+      __syncthreads();
+      put_cols(tile_d, i, 0, lrow);
+      put_cols(tile_d, i, 1, lrow + 32);
+      float zero[32];
+#pragma unroll
+      for (int m = 0; m < 32; ++m) zero[m] = 0.f;
+      put_cols(tile_d, i, 2, zero);
+      put_cols(tile_d, i, 3, zero);
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---------------------------------------------------------------- W = T X_w -> ACC0, U = T X_u -> ACC1
+    // with T = T_bd - T_bd L T_bd ((T_bd L)^2 = 0: L has only the lower-left block): Z = T_bd X, Y = L Z, T X = Z - T_bd Y
+    if (i == 0) {
+      tc_fence_after();
+      mma128(tmem + ACC0, s_t, false, s_xw, true, false);
+      mma128(tmem + ACC1, s_t, false, s_xu, true, false);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {  // Z_w, Z_u -> bf16 over X_w, X_u (MN-major B, row = token)
+      uint32_t zw[32], zu[32];
+      tmem_ld32(lane_base + ACC0 + 32 * cc, zw);
+      tmem_ld32(lane_base + ACC1 + 32 * cc, zu);
+      tmem_ld_wait_regs(zw, zu);
+      put_cols(tile_xw, i, cc, reinterpret_cast<const float*>(zw));
+      put_cols(tile_xu, i, cc, reinterpret_cast<const float*>(zu));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (i == 0) {  // Y_w = L Z_w -> TCOL
+      tc_fence_after();
+      mma128(tmem + TCOL, s_d, false, s_xw, true, false);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {  // Y_w -> bf16 over Z_w
+      uint32_t y[32];
+      tmem_ld32(lane_base + TCOL + 32 * cc, y);
+      tmem_ld_wait_regs(y);
+      put_cols(tile_xw, i, cc, reinterpret_cast<const float*>(y));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (i == 0) {  // W = Z_w - T_bd Y_w in ACC0; Y_u = L Z_u -> TCOL
+      tc_fence_after();
+      mma128(tmem + ACC0, s_t, false, s_xw, true, true, true);
+      mma128(tmem + TCOL, s_d, false, s_xu, true, false);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {  // Y_u -> bf16 over Z_u; W row -> bf16 (K-major A) over Y_w
+      uint32_t y[32], w[32];
+      tmem_ld32(lane_base + TCOL + 32 * cc, y);
+      tmem_ld32(lane_base + ACC0 + 32 * cc, w);
+      tmem_ld_wait_regs(y, w);
+      put_cols(tile_xu, i, cc, reinterpret_cast<const float*>(y));
+      put_cols(tile_xw, i, cc, reinterpret_cast<const float*>(w));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    if (i == 0) {  // U = Z_u - T_bd Y_u in ACC1
+      tc_fence_after();
+      mma128(tmem + ACC1, s_t, false, s_xu, true, true, true);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {  // S row (lane = key dim) -> bf16 (MN-major B) over Y_u
+      uint32_t sv[32];
+      tmem_ld32(lane_base + SST + 32 * cc, sv);
+      tmem_ld_wait_regs(sv);
+      put_cols(tile_xu, i, cc, reinterpret_cast<const float*>(sv));
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---------------------------------------------------------------- X = W S -> ACC0
+    if (i == 0) {
+      tc_fence_after();
+      mma128(tmem + ACC0, s_xw, false, s_xu, true, false);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+    {
+      const float gamma = expf(g_last);
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {  // D = U - W S -> bf16 (MN-major B, row = token)
+        uint32_t u[32], x[32];
+        tmem_ld32(lane_base + ACC1 + 32 * cc, u);
+        tmem_ld32(lane_base + ACC0 + 32 * cc, x);
+        tmem_ld_wait_regs(u, x);
+        float d[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) d[e] = __uint_as_float(u[e]) - __uint_as_float(x[e]);
+        put_cols(tile_d, i, cc, d);
+      }
+#pragma unroll 1
+      for (int cc = 0; cc < 4; ++cc) {  // S = gamma S, row by row in place
+        uint32_t sv[32];
+        tmem_ld32(lane_base + SST + 32 * cc, sv);
+        tmem_ld_wait_regs(sv);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[e] = __float_as_uint(__uint_as_float(sv[e]) * gamma);
+        tmem_st32(lane_base + SST + 32 * cc, sv);
+      }
+      tmem_st_wait();
+    }
+    fence_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // ---------------------------------------------------------------- O = q~ S + P D -> ACC0, S += k~^T D
+    if (i == 0) {
+      tc_fence_after();
+      mma128(tmem + ACC0, s_q, false, s_xu, true, false);
+      mma128(tmem + ACC0, s_kp, false, s_d, true, true);
+      mma128(tmem + SST, s_kt, true, s_d, true, true);
+      mma_commit(bar);
+    }
+    if (!(ok = wait_mma())) break;
+    if (i == 0 && c0 + C < t1) load_chunk(c0 + C);  // every tile the loads overwrite has been read
+#pragma unroll 1
+    for (int cc = 0; cc < 4; ++cc) {
+      uint32_t o[32];
+      tmem_ld32(lane_base + ACC0 + 32 * cc, o);
+      tmem_ld_wait_regs(o);
+      if (live) {
+        __nv_bfloat16* orow = a.out + (c0 + i) * a.ldo + (int64_t)head * HD + 32 * cc;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            pk[e] = pack_bf16x2(__uint_as_float(o[8 * q + 2 * e]), __uint_as_float(o[8 * q + 2 * e + 1]));
+          *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+int launch(const Args& a, int num_seqs, int64_t T, int* status, cudaStream_t stream) {
+  static bool configured[64] = {false};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return KD_ERR_ARGUMENT;
+  if (!configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(chunked_delta_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
+    if (e != cudaSuccess) return record_cuda_error(e, "gated_delta_rule: cudaFuncSetAttribute");
+    configured[dev] = true;
+  }
+  CUtensorMap map;
+  const int64_t width = 2LL * a.nk * HD + (int64_t)a.nv * HD;
+  int rc = make_tma_2d(&map, a.qkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (uint64_t)width, (uint64_t)T,
+                       (uint64_t)a.ldqkv, 64, C, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  chunked_delta_kernel<<<(unsigned)(num_seqs * a.nv), THREADS, SMEM, stream>>>(map, a, status);
+  return record_cuda_error(cudaGetLastError(), "gated_delta_rule: launch");
+}
+
+}  // namespace ck
+
 // ------------------------------------------------------------------------------------------------ gated norm
 
 // One warp per (token, head): out = bf16(bf16(w * bf16(x rsqrt(mean(x^2) + eps))) * silu(float(z))).
@@ -394,7 +911,7 @@ extern "C" int kd_conv_silu(const void* x, int64_t ldx, int64_t T, int C, const 
 extern "C" int kd_gated_delta_rule(const void* qkv, int64_t ldqkv, const void* ab, int64_t ldab, const void* a_log,
                                    const void* dt_bias, const int32_t* cu, int num_seqs, int64_t T, int num_k_heads,
                                    int num_v_heads, int head_k_dim, int head_v_dim, void* out, int64_t ldo,
-                                   cudaStream_t stream) {
+                                   int* status, cudaStream_t stream) {
   if (num_seqs < 0 || T < 0) return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: negative sizes");
   if (num_seqs == 0 || T == 0) return KD_OK;
   if (num_k_heads <= 0 || num_v_heads <= 0 || num_v_heads % num_k_heads)
@@ -416,8 +933,14 @@ extern "C" int kd_gated_delta_rule(const void* qkv, int64_t ldqkv, const void* a
   a.nv = num_v_heads;
   a.out = static_cast<__nv_bfloat16*>(out);
   a.ldo = ldo;
+  if (head_k_dim == 128 && head_v_dim == 128) {
+    if (!status) return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: status word required");
+    if ((reinterpret_cast<uintptr_t>(qkv) & 15) || (reinterpret_cast<uintptr_t>(out) & 15) || ldqkv % 8 || ldo % 8)
+      return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: qkv and out rows must be 16-byte aligned");
+    if (T > 0x7fffffffLL) return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: more than 2^31 rows");
+    return dn::ck::launch(a, num_seqs, T, status, stream);  // the chunked tensor-core form
+  }
   if (head_k_dim == 64 && head_v_dim == 64) return dn::launch_delta<64, 64>(a, num_seqs, stream);
-  if (head_k_dim == 128 && head_v_dim == 128) return dn::launch_delta<128, 128>(a, num_seqs, stream);
   if (head_k_dim == 128 && head_v_dim == 64) return dn::launch_delta<128, 64>(a, num_seqs, stream);
   if (head_k_dim == 64 && head_v_dim == 128) return dn::launch_delta<64, 128>(a, num_seqs, stream);
   return set_error(KD_ERR_ARGUMENT, "gated_delta_rule: head dims must be 64 or 128");

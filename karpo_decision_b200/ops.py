@@ -355,7 +355,8 @@ def conv_silu(x: torch.Tensor, weight: torch.Tensor, seqpos: torch.Tensor, chann
 def gated_delta_rule(qkv: torch.Tensor, ab: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor,
                      cu: torch.Tensor, k_heads: int, v_heads: int, k_dim: int, v_dim: int,
                      out: torch.Tensor | None = None) -> torch.Tensor:
-    """(T, Hv * dv) bf16: the gated delta rule over the packed sequences ``cu`` (int32 on the device)."""
+    """(T, Hv * dv) bf16: the gated delta rule over the packed sequences ``cu`` (int32 on the device); dk = dv = 128
+    runs the chunked tensor-core form, which reports a timed-out wait in the device's status word."""
     _require(qkv.dtype == torch.bfloat16 and qkv.stride(-1) == 1, "gated_delta_rule: bf16 qkv rows")
     _require(ab.dtype == torch.bfloat16 and ab.stride(-1) == 1, "gated_delta_rule: bf16 [b | a] rows")
     _require(cu.dtype == torch.int32 and cu.is_contiguous(), "cu: contiguous int32")
@@ -364,7 +365,7 @@ def gated_delta_rule(qkv: torch.Tensor, ab: torch.Tensor, a_log: torch.Tensor, d
         out = torch.empty(t, v_heads * v_dim, dtype=torch.bfloat16, device=qkv.device)
     call("kd_gated_delta_rule", qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr(),
          dt_bias.data_ptr(), cu.data_ptr(), cu.numel() - 1, t, k_heads, v_heads, k_dim, v_dim, out.data_ptr(),
-         out.stride(0), _stream(qkv))
+         out.stride(0), status_word(qkv.device).data_ptr(), _stream(qkv))
     return out
 
 

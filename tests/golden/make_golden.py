@@ -193,6 +193,11 @@ CASES = {
     "qwen_hybrid": dict(spec=small(CONFIGS["tiny"], layers=4, full_every=2, partial_rotary=0.5, lin_k_heads=2,
                                    lin_v_heads=4, lin_k_dim=64, lin_v_dim=64),
                         lengths=("uniform", 6, 8, 200), markers=(1, 3), fp8=False),
+    # Qwen3.5's real Gated DeltaNet head shape (128-dim keys and values, value heads twice the key heads), with
+    # sequences shorter than, at, one past and several times the 128-token chunk of the tensor-core delta rule.
+    "qwen_hybrid128": dict(spec=small(CONFIGS["tiny"], layers=4, full_every=2, partial_rotary=0.5, lin_k_heads=2,
+                                      lin_v_heads=4, lin_k_dim=128, lin_v_dim=128),
+                           lengths=("list", 100, 128, 129, 300, 517), markers=(1, 3), fp8=False),
     # Gemma 4 images (bidirectional checkpoints): soft-token runs in a single block, a shared block, a branch and at a
     # sequence's start; features stand in for the vision encoder's output (families/gemma/vision.py:136-144).
     "gemma_images": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0,

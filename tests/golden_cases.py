@@ -13,7 +13,7 @@ from karpo_decision_b200.synthetic import Spec, numpy_weights
 GOLDEN = Path(__file__).resolve().parent / "golden"
 IMAGE_TOKEN = 4095  # the image cases' soft-token id
 CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_tiny_fp8", "gemma_tiny_fp8", "qwen_bidir",
-         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid", "gemma_images"]
+         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid", "gemma_images", "qwen_hybrid128"]
 #: BASELINE configurations 2-5 at full width (depth cut), from the reference's bf16 path (float32 run beside it).
 WIDE = ["qwen_0p8b", "qwen_4b_fp8", "gemma_12b", "gemma_12b_fp8", "gemma_31b_fp8"]
 

@@ -35,7 +35,8 @@ def run_b200(name):
 
 
 @pytest.mark.parametrize("name", ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_bidir",
-                                  "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid"])
+                                  "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid",
+                                  "qwen_hybrid128"])
 def test_bf16_forward_matches_reference(name):
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
     assert hidden.shape == expected["hidden"].shape
@@ -52,7 +53,7 @@ def test_bf16_forward_matches_reference(name):
 
 
 @pytest.mark.parametrize("name", ["qwen_tiny", "gemma_tiny", "gemma_blocks", "qwen_bidir", "gemma_blocks_bidir",
-                                  "gemma_global512", "qwen_hybrid"])
+                                  "gemma_global512", "qwen_hybrid", "qwen_hybrid128"])
 def test_bf16_forward_tracks_bf16_oracle(name):
     """Against the oracle with the reference's bf16 rounding points: closer than to the float32 reference."""
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
