@@ -513,6 +513,16 @@ __global__ void __launch_bounds__(THREADS, 1)
     tmem_st_wait();
   }
   if (i == 0 && t0 < t1) load_chunk(t0);
+  // this row's b and a inputs (write strength, decay) of the next chunk, fetched a chunk ahead
+  float next_b = 0.f, next_a = 0.f;
+  auto fetch_ab = [&](int64_t c0) {
+    if (c0 + i < t1) {
+      const __nv_bfloat16* abr = a.ab + (c0 + i) * a.ldab;
+      next_b = __bfloat162float(abr[head]);
+      next_a = __bfloat162float(abr[a.nv + head]);
+    }
+  };
+  fetch_ab(t0);
 
   for (int64_t c0 = t0; c0 < t1 && ok; c0 += C) {
     const int n = t1 - c0 < C ? (int)(t1 - c0) : C;
@@ -520,9 +530,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     // ---------------------------------------------------------------- this row's decay, write strength, q, k, v
     float g = 0.f, beta = 0.f;
     if (live) {
-      const __nv_bfloat16* abr = a.ab + (c0 + i) * a.ldab;
-      beta = bf16_round(1.0f / (1.0f + expf(-__bfloat162float(abr[head]))));
-      g = decay_a * softplus(__bfloat162float(abr[a.nv + head]) + dt_bias);
+      beta = bf16_round(1.0f / (1.0f + expf(-next_b)));
+      g = decay_a * softplus(next_a + dt_bias);
     }
     float gi = g;  // inclusive running sum over the chunk's rows
 #pragma unroll
@@ -584,17 +593,20 @@ __global__ void __launch_bounds__(THREADS, 1)
         tmem_ld32(lane_base + ACC0 + 32 * cc, kk);
         tmem_ld32(lane_base + ACC1 + 32 * cc, qk);
         tmem_ld_wait_regs(kk, qk);
-        float p[32];
+        float p[32], av[32];
 #pragma unroll
         for (int e = 0; e < 32; ++e) {
           const int j = 32 * cc + e;
           const float dec = (j <= i && live) ? fast_exp2((gi - g_s[j]) * 1.4426950408889634f) : 0.f;
-          if (j < i) arow[j] = beta * __uint_as_float(kk[e]) * dec;
+          av[e] = j < i ? beta * __uint_as_float(kk[e]) * dec : 0.f;
           p[e] = __uint_as_float(qk[e]) * dec;
         }
         put_cols(tile_kp, i, cc, p);
+#pragma unroll
+        for (int e = 0; e < 32; e += 4)  // the row's entries j < i and its padding to a multiple of 4, 16 bytes at a time
+          if (32 * cc + e < i)
+            *reinterpret_cast<float4*>(arow + 32 * cc + e) = make_float4(av[e], av[e + 1], av[e + 2], av[e + 3]);
       }
-      for (int j = i; j < ((i + 3) & ~3); ++j) arow[j] = 0.f;  // the row's padding
 #pragma unroll
       for (int u = 0; u < 16; ++u) {
         uint4* at = reinterpret_cast<uint4*>(tile_q + unit_at(i, u));
@@ -799,6 +811,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (!(ok = wait_mma())) break;
     if (i == 0 && c0 + C < t1) load_chunk(c0 + C);  // every tile the loads overwrite has been read
+    fetch_ab(c0 + C);
 #pragma unroll 1
     for (int cc = 0; cc < 4; ++cc) {
       uint32_t o[32];
