@@ -6,6 +6,7 @@ Kernel profiles are captured on it, so that a capture holds one kernel at a smal
     python -m karpo_decision_b200.microbench qkv --lengths mix:8192 --k 1024 --hq 16 --hkv 8 --gate
     python -m karpo_decision_b200.microbench rmsnorm_e4m3 --rows 16384 --cols 5376
     python -m karpo_decision_b200.microbench delta_rule --lengths 8192,4096,2048,2048 --hk 16 --hv 32
+    python -m karpo_decision_b200.microbench attention --lengths mix:65536 --lib fa2    # a library kernel, same inputs
 
 ``--window=left,right`` takes its value after ``=`` (``-1`` is unbounded; ``-1,0``, the default, is causal).
 ``--lengths`` is a comma-separated list of sequence lengths, or ``mix:T`` for T tokens of lengths log-uniform in
@@ -69,6 +70,8 @@ def build(args: argparse.Namespace, dev: torch.device):
         def run():
             ops.attention_varlen(q, k, v, cu, cu, max(lengths), scale, window, gate=gate, out=out)
 
+        if args.lib:
+            run = library_attention(args.lib, q, k, v, cu, lengths, scale, window)
         flops = 4 * args.hd * args.hq * visible_pairs(lengths, window)
         return run, flops, "FLOP", {"sequences": len(lengths), "tokens": t, "hq": args.hq, "hkv": args.hkv,
                                     "hd": args.hd, "window": list(window), "gate": bool(args.gate)}
@@ -90,6 +93,18 @@ def build(args: argparse.Namespace, dev: torch.device):
             def run():
                 ops.gemm(a, w, out=out, epilogue=epi, residual=res)
 
+        if args.lib == "cublas":  # the library product alone, no epilogue: torch.matmul / rowwise torch._scaled_mm
+            full = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+            if args.fp8:
+                sa2, sw2 = sa.view(-1, 1).contiguous(), sw.view(1, -1).contiguous()
+
+                def run():
+                    torch._scaled_mm(qa, qw.t(), scale_a=sa2, scale_b=sw2, out_dtype=torch.bfloat16, out=full)
+            else:
+                def run():
+                    torch.matmul(a, w.t(), out=full)
+        elif args.lib:
+            raise SystemExit("gemm --lib takes cublas")
         return run, 2 * m * n * kk, "FLOP", {"m": m, "n": n, "k": kk, "fp8": bool(args.fp8),
                                              "epilogue": args.epilogue}
     if op == "qkv":
@@ -162,6 +177,11 @@ def build(args: argparse.Namespace, dev: torch.device):
             def run():
                 ops.gated_delta_rule(qkv, ab, a_log, dt_bias, cu, hk, hv, dk, dv, out=out)
 
+            if args.lib == "fla":
+                run = library_delta_rule(qkv, ab, a_log, dt_bias, cu, hk, hv, dk, dv)
+            elif args.lib:
+                raise SystemExit("delta_rule --lib takes fla")
+
             return run, 6 * t * hv * dk * dv, "FLOP", {"sequences": len(lengths), "tokens": t, "hk": hk, "hv": hv,
                                                         "dk": dk, "dv": dv}
         if op == "conv_silu":
@@ -184,6 +204,81 @@ def build(args: argparse.Namespace, dev: torch.device):
 
         return run, 3 * t * hv * dv * 2, "B", {"tokens": t, "heads": hv, "head_dim": dv}
     raise SystemExit(f"unknown op {op}")
+
+
+def library_attention(lib: str, q, k, v, cu, lengths, scale, window):
+    """The same attention by a library kernel on the same tensors (no output gate): ``fa2`` flash-attention 2's
+    flash_attn_varlen_func (GQA native), ``flashinfer[:backend]`` its ragged-KV prefill (``auto``: the backend it
+    picks for this GPU; ``cutlass``: its sm100 kernel), ``torch``
+    F.scaled_dot_product_attention per sequence with the key/value heads repeated to the query heads outside the timed
+    launch (whatever backend torch selects). Causal and sliding windows (left, 0) only."""
+    left, right = window
+    if right != 0 and not (left < 0 and right < 0):
+        raise SystemExit("library attention: causal, sliding or bidirectional windows")
+    causal = right == 0
+    t, hq, hd = q.shape
+    hkv = k.shape[1]
+    max_len = max(lengths)
+    if lib == "fa2":
+        from flash_attn import flash_attn_varlen_func
+
+        def run():
+            flash_attn_varlen_func(q, k, v, cu, cu, max_len, max_len, softmax_scale=scale, causal=causal,
+                                   window_size=(left if left >= 0 else -1, -1 if not causal else 0))
+        return run
+    if lib.split(":")[0] == "flashinfer":  # flashinfer[:backend], e.g. flashinfer:cutlass for its sm100 FMHA
+        import flashinfer
+
+        ws = torch.empty(256 << 20, dtype=torch.uint8, device=q.device)
+        backend = lib.split(":")[1] if ":" in lib else "auto"
+        wrapper = flashinfer.BatchPrefillWithRaggedKVCacheWrapper(ws, "NHD", backend=backend)
+        wrapper.plan(cu, cu, hq, hkv, hd, causal=causal, window_left=left if left >= 0 else -1, sm_scale=scale,
+                     q_data_type=torch.bfloat16)
+
+        def run():
+            wrapper.run(q, k, v)
+        return run
+    if lib == "torch":
+        import torch.nn.functional as F
+
+        group = hq // hkv
+        kx, vx = k.repeat_interleave(group, dim=1), v.repeat_interleave(group, dim=1)
+        bounds = cu.tolist()
+        mask = None
+        if left >= 0:
+            raise SystemExit("torch SDPA comparison: causal or bidirectional only")
+
+        def run():
+            for a, b in zip(bounds[:-1], bounds[1:]):
+                F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None], kx[a:b].transpose(0, 1)[None],
+                                               vx[a:b].transpose(0, 1)[None], attn_mask=mask, is_causal=causal,
+                                               scale=scale)
+        return run
+    raise SystemExit(f"unknown attention library {lib}")
+
+
+def library_delta_rule(qkv, ab, a_log, dt_bias, cu, hk, hv, dk, dv):
+    """The reference's own Gated DeltaNet kernel on the same inputs: flash-linear-attention's chunk_gated_delta_rule
+    with use_qk_l2norm_in_kernel and cu_seqlens, as families/qwen/packed.py:88-103 calls it; the query/key heads
+    repeated to the value heads, the decay and write strength computed (families/qwen/fused.py:42-44) outside the timed
+    launch."""
+    import torch.nn.functional as F
+    from fla.ops.gated_delta_rule import chunk_gated_delta_rule
+
+    t = qkv.shape[0]
+    kd = hk * dk
+    q = qkv[:, :kd].reshape(1, t, hk, dk).repeat_interleave(hv // hk, dim=2).contiguous()
+    k = qkv[:, kd:2 * kd].reshape(1, t, hk, dk).repeat_interleave(hv // hk, dim=2).contiguous()
+    v = qkv[:, 2 * kd:].reshape(1, t, hv, dv).contiguous()
+    b, a = ab[:, :hv].float(), ab[:, hv:].float()
+    g = (-a_log.float().exp() * F.softplus(a + dt_bias.float()))[None].contiguous()
+    beta = b.sigmoid().to(torch.bfloat16)[None].contiguous()
+    cu64 = cu.long()
+
+    def run():
+        chunk_gated_delta_rule(q, k, v, g=g, beta=beta, initial_state=None, output_final_state=False,
+                               use_qk_l2norm_in_kernel=True, cu_seqlens=cu64)
+    return run
 
 
 def main(argv: list[str] | None = None) -> dict:
@@ -209,6 +304,8 @@ def main(argv: list[str] | None = None) -> dict:
     p.add_argument("--dv", type=int, default=128)
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--lib", default="", help="time a library kernel on the same inputs instead: attention fa2, "
+                                             "flashinfer or torch; gemm cublas; delta_rule fla")
     args = p.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")
@@ -227,7 +324,8 @@ def main(argv: list[str] | None = None) -> dict:
     ops.check_status(dev)
     us = start.elapsed_time(end) * 1e3 / args.iters
     rate = work / (us * 1e-6)
-    line = {"op": args.op, "shape": shape, "iters": args.iters, "us_per_launch": round(us, 2),
+    line = {"op": args.op, "impl": args.lib or "libkd_b200", "shape": shape, "iters": args.iters,
+            "us_per_launch": round(us, 2),
             "work_per_launch": work, "unit": unit,
             "achieved": round(rate / 1e12, 2) if unit == "FLOP" else round(rate / 1e9, 1),
             "achieved_unit": "TFLOP/s" if unit == "FLOP" else "GB/s"}
