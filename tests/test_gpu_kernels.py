@@ -339,12 +339,15 @@ def test_attention_output_gate():
     assert np.abs(got - want).max() <= 2e-2
 
 
-def test_attention_sequences_do_not_see_each_other():
-    """A sequence's outputs are the same alone and packed with others (tests/gpu/test_packed_qwen.py:114-122)."""
+@pytest.mark.parametrize("hkv", [4, 2])
+def test_attention_sequences_do_not_see_each_other(hkv):
+    """A sequence's outputs are the same alone and packed with others (tests/gpu/test_packed_qwen.py:114-122), for
+    query heads taken one at a time (4/4) and in pairs sharing a key/value head (4/2)."""
     g = rng(11)
     lengths = [50, 90, 70]
     t = sum(lengths)
-    q, k, v = (bf16(g.standard_normal((t, 4, 128))) for _ in range(3))
+    q = bf16(g.standard_normal((t, 4, 128)))
+    k, v = (bf16(g.standard_normal((t, hkv, 128))) for _ in range(2))
     cu = torch.tensor([0, 50, 140, 210], dtype=torch.int32, device=DEV)
     together = ops.attention_varlen(q, k, v, cu, cu, 90, 0.1, (-1, 0))
     cu1 = torch.tensor([0, 90], dtype=torch.int32, device=DEV)
