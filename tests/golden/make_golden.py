@@ -233,6 +233,15 @@ WIDE = {
                           dtype="bf16"),
 }
 CASES.update(WIDE)
+#: BASELINE configuration 1's shape (2 layers, hidden 256, 4 / 2 heads of 64) through the reference's served
+#: ``--fp8`` path (the backbone cast to bf16, then quantized), so the FP8 forward meets the readout bar against the
+#: same path it replaces; the float32 ``--fp8`` run is stored beside it.
+CASES.update({
+    "qwen_tiny_fp8_served": dict(spec=CONFIGS["tiny"], lengths=("uniform", 16, 32, 160), markers=(1, 4), fp8=True,
+                                 dtype="bf16"),
+    "gemma_tiny_fp8_served": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
+                                  lengths=("uniform", 16, 8, 96), markers=(1, 1), fp8=True, dtype="bf16"),
+})
 
 
 #: FP8 cases also record, for layer 0, each quantized projection's input (e4m3 values and row scales) and output: the

@@ -111,3 +111,14 @@ def test_cpu_reference_matches_golden(name):
     torch.set_num_threads(4)
     logits = Model(weights, spec.as_dict()).forward(arrays).numpy()
     assert np.abs(logits - expected["logits"]).max() <= 2e-4 * max(1.0, np.abs(expected["logits"]).max())
+
+
+@pytest.mark.parametrize("name", ["qwen_tiny_fp8_served", "gemma_tiny_fp8_served"])
+def test_oracle_fp8_bf16_within_the_served_fp8_noise(name):
+    """The oracle's FP8 forward with the reference's bf16 rounding points lies as close to the reference's served
+    ``--fp8`` readout as the reference's own float32 ``--fp8`` run does (e4m3 rounding flips set that distance)."""
+    spec, weights, pack, expected = load(name)
+    logits = oracle.readout(forward(spec)(weights, spec.as_dict(), pack, mode="bf16", fp8=True), weights["readout"],
+                            spec.logit_cap)
+    floor = np.abs(expected["logits"] - expected["logits_fp32"]).max()
+    assert np.abs(logits - expected["logits"]).max() <= max(2e-2, floor)
