@@ -154,6 +154,16 @@ int kd_quantize_rows_e4m3(const void* x, int64_t rows, int cols, void* q, float*
 int kd_rope_table(const float* inv_freq, int rot, int64_t positions, float* cos_out, float* sin_out,
                   cudaStream_t stream);
 
+/* M-RoPE tables, one row per token (Qwen3.5 joint layouts with images): cos/sin[t, i] = bf16(cos/sin(pos[a, t] *
+ * inv_freq[i % (rot/2)])) stored as float, t < T, i < rot, where a = pair_axis[i % (rot/2)] picks the position axis
+ * (time, height, width: `axes` rows of `pos`, `ld_axis` apart) a frequency pair reads; an axis outside [0, axes) reads
+ * axis 0. The same arithmetic as kd_rope_table, so a token whose axes all hold p gets row p of that table. Rows feed
+ * kd_rope_gather / kd_qkv_norm_rope with positions 0..T-1. Replaces Transformers' Qwen3_5TextRotaryEmbedding with
+ * its interleaved M-RoPE sections (apply_interleaved_mrope), called with the pack's M-RoPE positions at
+ * families/qwen/packed.py:186 (Pack.rope, model/packed.py:64-70). */
+int kd_rope_table_axes(const float* inv_freq, int rot, const int64_t* pos, int64_t ld_axis, int64_t T,
+                       const int32_t* pair_axis, int axes, float* cos_out, float* sin_out, cudaStream_t stream);
+
 /* The attention inputs from the fused QKV projection output qkv[T, ldqkv]: per head RMSNorm over head_dim and RoPE
  * (rotate-half on the first `rot` dims, table rows at seqpos[t]); writes q[T, Hq, hd], k[T, Hkv, hd], v[T, Hkv, hd]
  * and, for Qwen's gated queries, gate[T, Hq * hd].

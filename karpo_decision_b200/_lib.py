@@ -39,6 +39,7 @@ SIGNATURES: dict[str, list] = {
     "kd_rmsnorm_e4m3": [P, c_int64, P, c_int, c_float, P, P, c_int64, c_int, P],
     "kd_quantize_rows_e4m3": [P, c_int64, c_int, P, P, P],
     "kd_rope_table": [P, c_int, c_int64, P, P, P],
+    "kd_rope_table_axes": [P, c_int, P, c_int64, c_int64, P, c_int, P, P, P],
     "kd_qkv_norm_rope": [P, c_int64, c_int64, P, c_int, c_int, c_int, c_int, P, P, c_int, c_int, c_float, P, P,
                          c_int, P, P, P, P, P],
     "kd_attention_varlen": [P, c_int64, P, c_int64, P, c_int64, P, c_int64, P, c_int64, P, P, c_int, c_int, c_int64,

@@ -494,6 +494,23 @@ __global__ void rope_table_kernel(const float* __restrict__ inv_freq, int rot, i
   sin_out[idx] = bf16_round(sinf(emb));
 }
 
+// Per-token tables for M-RoPE (several position axes): row t holds pair i's factors at the position of the axis that
+// pair reads, pos[axis(i) * ld_axis + t], with rope_table_kernel's arithmetic (float32 product, then bf16-rounded
+// cos / sin). An axis index outside [0, axes) reads axis 0.
+__global__ void rope_table_axes_kernel(const float* __restrict__ inv_freq, int rot, const int64_t* __restrict__ pos,
+                                       int64_t ld_axis, int64_t T, const int32_t* __restrict__ pair_axis, int axes,
+                                       float* __restrict__ cos_out, float* __restrict__ sin_out) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= T * rot) return;
+  const int64_t t = idx / rot;
+  const int pair = (int)(idx % rot) % (rot / 2);
+  int ax = pair_axis[pair];
+  if (ax < 0 || ax >= axes) ax = 0;
+  const float emb = (float)pos[ax * ld_axis + t] * inv_freq[pair];
+  cos_out[idx] = bf16_round(cosf(emb));
+  sin_out[idx] = bf16_round(sinf(emb));
+}
+
 // dst[i, :] = src[rows[i], :] for bf16 rows of `width` elements (width % 8 == 0): one warp per row, 16-byte copies.
 __global__ void gather_rows_kernel(const __nv_bfloat16* __restrict__ src, int64_t ld_src,
                                    const int64_t* __restrict__ rows, int64_t n, int width,
@@ -786,6 +803,20 @@ extern "C" int kd_rope_table(const float* inv_freq, int rot, int64_t positions, 
   if (n == 0) return KD_OK;
   ew::rope_table_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(inv_freq, rot, positions, cos_out, sin_out);
   return record_cuda_error(cudaGetLastError(), "rope_table: launch");
+}
+
+extern "C" int kd_rope_table_axes(const float* inv_freq, int rot, const int64_t* pos, int64_t ld_axis, int64_t T,
+                                  const int32_t* pair_axis, int axes, float* cos_out, float* sin_out,
+                                  cudaStream_t stream) {
+  if (rot <= 0 || rot % 2 || T < 0 || axes < 1 || (axes > 1 && ld_axis < T))
+    return set_error(KD_ERR_ARGUMENT, "rope_table_axes: bad sizes");
+  if (T == 0) return KD_OK;
+  if (!inv_freq || !pos || !pair_axis || !cos_out || !sin_out)
+    return set_error(KD_ERR_ARGUMENT, "rope_table_axes: null pointer");
+  const int64_t n = T * rot;
+  ew::rope_table_axes_kernel<<<(unsigned)((n + 255) / 256), 256, 0, stream>>>(inv_freq, rot, pos, ld_axis, T, pair_axis,
+                                                                              axes, cos_out, sin_out);
+  return record_cuda_error(cudaGetLastError(), "rope_table_axes: launch");
 }
 
 extern "C" int kd_qkv_norm_rope(const void* qkv, int64_t ldqkv, int64_t T, const int64_t* seqpos, int num_heads_q,

@@ -13,7 +13,7 @@ from ._lib import EPI_GEGLU, EPI_RESIDUAL, EPI_STORE, EPI_SWIGLU, NORM_NONE, NOR
 __all__ = ["EPI_GEGLU", "EPI_RESIDUAL", "EPI_STORE", "EPI_SWIGLU", "NORM_NONE", "NORM_ONE_PLUS", "NORM_WEIGHT",
            "add_rmsnorm", "attention_varlen", "check_status", "embed", "gather_rows", "gemm", "gemm_fp8", "marker_norm",
            "norm_add", "qkv_norm_rope", "qkv_projection", "quantize_rows_e4m3", "readout", "rmsnorm", "rmsnorm_e4m3",
-           "rope_gather", "rope_table",
+           "rope_gather", "rope_table", "rope_table_axes",
            "sched_pair", "status_word"]
 
 _STATUS: dict[int, torch.Tensor] = {}
@@ -188,6 +188,24 @@ def rope_table(inv_freq: torch.Tensor, positions: int) -> tuple[torch.Tensor, to
     cos = torch.empty(positions, rot, dtype=torch.float32, device=inv_freq.device)
     sin = torch.empty_like(cos)
     call("kd_rope_table", inv_freq.data_ptr(), rot, positions, cos.data_ptr(), sin.data_ptr(), _stream(inv_freq))
+    return cos, sin
+
+
+def rope_table_axes(inv_freq: torch.Tensor, positions: torch.Tensor, pair_axis: torch.Tensor
+                    ) -> tuple[torch.Tensor, torch.Tensor]:
+    """(cos, sin) float32 tables (T, rot), one row per token, for M-RoPE: ``positions`` int64 (axes, T) holds each
+    token's position on every axis, ``pair_axis`` int32 (rot / 2,) the axis each frequency pair reads."""
+    _require(inv_freq.dtype == torch.float32 and inv_freq.is_contiguous(), "inv_freq: contiguous float32")
+    _require(positions.dtype == torch.int64 and positions.dim() == 2 and positions.stride(1) == 1,
+             "positions: int64 (axes, T) with contiguous rows")
+    _require(pair_axis.dtype == torch.int32 and pair_axis.is_contiguous() and pair_axis.numel() == inv_freq.numel(),
+             "pair_axis: contiguous int32, one entry per frequency pair")
+    rot = 2 * inv_freq.numel()
+    axes, t = positions.shape
+    cos = torch.empty(t, rot, dtype=torch.float32, device=inv_freq.device)
+    sin = torch.empty_like(cos)
+    call("kd_rope_table_axes", inv_freq.data_ptr(), rot, positions.data_ptr(), positions.stride(0), t,
+         pair_axis.data_ptr(), axes, cos.data_ptr(), sin.data_ptr(), _stream(inv_freq))
     return cos, sin
 
 

@@ -27,11 +27,12 @@ class Pack:
     max_markers: int
     segment_ids: torch.Tensor | None = None  # block layouts: 0 a sequence's shared block, k its k-th branch
     segment_ids_cpu: torch.Tensor | None = None
-    rope: torch.Tensor | None = None
+    rope: torch.Tensor | None = None  # Qwen joint layouts with images: (3, 1, T) M-RoPE positions
     plan: Any = None
     markers_cpu: torch.Tensor | None = None  # the markers on the host (planning checks need no device read)
     pixel_values: torch.Tensor | None = None  # images: what the model's image_features reads (model/packed.py:43-48)
     image_position_ids: torch.Tensor | None = None
+    image_grid_thw: torch.Tensor | None = None  # Qwen joint layouts: each image's (t, h, w) grid of patches
 
     @property
     def tokens(self) -> int:
@@ -72,8 +73,8 @@ def pack(sequences: Sequence[Any], device: torch.device, blocks: bool = False) -
 
 def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: bool = False) -> Pack:
     """A pack from host arrays (``synthetic.synthetic_pack_arrays`` layout: input_ids, seqpos, cu, markers,
-    marker_cu, and segment_ids for block layouts); ``pinned`` stages them in page-locked memory so the copies are
-    asynchronous."""
+    marker_cu, and segment_ids for block layouts; with images, pixel_values and, for Qwen joint layouts, the (3, T)
+    M-RoPE positions ``rope``); ``pinned`` stages them in page-locked memory so the copies are asynchronous."""
 
     def host(a, dtype):
         t = torch.from_numpy(np.ascontiguousarray(a)).to(dtype)
@@ -98,4 +99,6 @@ def from_arrays(arrays: dict[str, np.ndarray], device: torch.device, pinned: boo
         markers_cpu=torch.from_numpy(np.asarray(arrays["markers"], dtype=np.int64)),
         pixel_values=(torch.from_numpy(np.ascontiguousarray(arrays["pixel_values"])).to(device)
                       if arrays.get("pixel_values") is not None else None),
+        rope=(host(arrays["rope"], torch.int64).reshape(len(arrays["rope"]), 1, -1).to(device, non_blocking=True)
+              if arrays.get("rope") is not None else None),
     )

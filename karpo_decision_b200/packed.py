@@ -107,6 +107,17 @@ class Layer:
     scalar: torch.Tensor | None = None
 
 
+@dataclass
+class JointImages:
+    """A Qwen joint-layout pack with images: the image-token rows its image features are written over, and the
+    rotary tables of its M-RoPE positions, one row per token (``index``: each token's row)."""
+
+    rows: torch.Tensor  # (soft tokens,) int64
+    index: torch.Tensor  # (T,) int64: 0 .. T - 1
+    cos: torch.Tensor  # (T, rot) float32
+    sin: torch.Tensor
+
+
 def mixer_width(spec: Spec) -> int:
     """Columns of a Gated DeltaNet layer's projection buffer (padded to a multiple of 32, the GEMM's N granule)."""
     width = spec.conv_dim + spec.lin_value_dim + 2 * spec.lin_v_heads
@@ -267,6 +278,7 @@ class Packed(torch.nn.Module):
                             if s.qkv_width_of(kind) % 256 == 0 and rotary_width(s, kind) % 32 == 0
                             and s.attn_dims(kind)[0] <= 256}
         self._tables: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+        self._pair_axis: torch.Tensor | None = None  # Qwen M-RoPE: the position axis of each rotary frequency pair
         self._workspace: Workspace | None = None
 
     def _linear_layer(self, weights: dict[str, Any], p: str, fp8: bool) -> Layer:
@@ -372,7 +384,8 @@ class Packed(torch.nn.Module):
                         lin_v_heads=getattr(config, "linear_num_value_heads", 32),
                         lin_k_dim=getattr(config, "linear_key_head_dim", 128),
                         lin_v_dim=getattr(config, "linear_value_head_dim", 128),
-                        conv_kernel=getattr(config, "linear_conv_kernel_dim", 4), attention=attention)
+                        conv_kernel=getattr(config, "linear_conv_kernel_dim", 4), attention=attention,
+                        mrope_section=tuple(rope["mrope_section"]) if rope.get("mrope_section") else None)
             if kinds != spec.layer_types():
                 raise NotImplementedError(f"layer pattern {kinds} is not a full-attention layer every n-th")
         else:
@@ -399,6 +412,14 @@ class Packed(torch.nn.Module):
                 device = torch.device("cuda")
         image_token = getattr(getattr(backbone, "config", None), "image_token_id", None)
         features = None
+        if family == "qwen" and getattr(backbone, "visual", None) is not None:
+            def features(p: Any) -> torch.Tensor:
+                """Every image's embeddings in pack order, from the backbone's own vision tower, as
+                families/qwen/packed.py:161-163 makes them."""
+                param = next(backbone.visual.parameters())
+                out = backbone.get_image_features(p.pixel_values.to(param.device, param.dtype),
+                                                  p.image_grid_thw.to(param.device), return_dict=True)
+                return torch.cat(list(out.pooler_output))
         if family == "gemma" and (getattr(backbone, "vision_tower", None) is not None or
                                   getattr(backbone, "embed_vision", None) is not None):
             def features(p: Any) -> torch.Tensor:
@@ -473,13 +494,16 @@ class Packed(torch.nn.Module):
         """(M, hidden) final-normalized hidden states at the markers, in pack order."""
         plan = self.plan(p)
         images = self.images(p)
-        return self.head(self.body(p, plan, images), p, plan)
+        return self.head(self.body(p, plan, images), p, plan, images)
 
-    def images(self, p: Any) -> ImagePlan | None:
-        """The pack's image plan (None without images): each image's soft-token rows and the keys they see in the
-        sliding layers (families/gemma/packed.py:310-315)."""
+    def images(self, p: Any) -> ImagePlan | JointImages | None:
+        """The pack's image plan (None without images). Gemma: each image's soft-token rows and the keys they see in
+        the sliding layers (families/gemma/packed.py:310-315). Qwen: the image-token rows and the rotary tables of the
+        pack's M-RoPE positions (families/qwen/packed.py:158-165, :186)."""
         if getattr(p, "pixel_values", None) is None:
             return None
+        if self.family == "qwen":
+            return self._joint_images(p)
         seg = None if p.segment_ids_cpu is None else p.segment_ids_cpu.numpy()
         return image_plan(p.input_ids.cpu().numpy(), [int(x) for x in p.cu_cpu.tolist()], seg,
                           p.seqpos.cpu().numpy(), self.image_token_id, self.window, self.device)
@@ -490,9 +514,11 @@ class Packed(torch.nn.Module):
         Qwen reads joint layouts only (families/qwen/packed.py:180-181); a Gemma block's readout marker is its last
         token, one per block or branch (families/gemma/packed.py:136-143)."""
         if getattr(p, "pixel_values", None) is not None:
-            if self.family != "gemma":
-                raise NotImplementedError("Qwen packs with images (M-RoPE positions) are not run by the B200 path")
-            if not self.prune_last:  # families/gemma/packed.py:311-313
+            if self.image_token_id is None or self.image_features is None:
+                raise ValueError("a pack with images needs the model's image_token_id and image_features")
+            if self.family == "qwen" and getattr(p, "rope", None) is None:
+                raise ValueError("a Qwen pack with images needs its M-RoPE positions (Pack.rope)")
+            if self.family == "gemma" and not self.prune_last:  # families/gemma/packed.py:311-313
                 raise ValueError("images are supported on bidirectional checkpoints only, the ones the image path was "
                                  "validated on")
             if self.image_token_id is None or self.image_features is None:
@@ -512,7 +538,22 @@ class Packed(torch.nn.Module):
         marker_bounds([int(x) for x in p.cu_cpu.tolist()], np.asarray(markers))
         return None
 
-    def head(self, h: torch.Tensor, p: Any, plan: BlockPlan | None = None) -> torch.Tensor:
+    def _joint_images(self, p: Any) -> JointImages:
+        """A Qwen joint layout's image-token rows and its rotary tables, one row per token: each frequency pair at
+        the position of the M-RoPE axis it reads (Pack.rope, (3, 1, T) or (3, T); model/packed.py:64-70)."""
+        rope = p.rope.reshape(p.rope.shape[0], -1).to(self.device, torch.int64).contiguous()
+        t = int(p.input_ids.numel())
+        if rope.shape[1] != t:
+            raise ValueError(f"M-RoPE positions for {rope.shape[1]} tokens in a pack of {t}")
+        if self._pair_axis is None:
+            self._pair_axis = torch.tensor(self.spec.pair_axes(), dtype=torch.int32, device=self.device)
+        cos, sin = ops.rope_table_axes(self._inv_freq["full_attention"], rope, self._pair_axis)
+        rows = torch.nonzero(p.input_ids.to(self.device) == self.image_token_id).reshape(-1)
+        index = torch.arange(t, dtype=torch.int64, device=self.device)
+        return JointImages(rows=rows, index=index, cos=cos, sin=sin)
+
+    def head(self, h: torch.Tensor, p: Any, plan: BlockPlan | None = None,
+             images: ImagePlan | JointImages | None = None) -> torch.Tensor:
         """(M, hidden): the final norm of the body's output at the markers (families/qwen/packed.py:173-176,
         families/gemma/packed.py:297-303); a bidirectional model first runs its last layer for the marker rows."""
         mode = ops.NORM_ONE_PLUS if self.spec.family == "qwen" else ops.NORM_WEIGHT
@@ -520,10 +561,11 @@ class Packed(torch.nn.Module):
             return ops.marker_norm(h, p.markers, self.norm, mode, self.spec.eps)
         if plan is None and p.segment_ids_cpu is not None and bool((p.segment_ids_cpu != 0).any()):
             plan = self.plan(p)
-        hm = self._last_layer_at_markers(h, p, plan)
+        hm = self._last_layer_at_markers(h, p, plan, images if isinstance(images, JointImages) else None)
         return ops.rmsnorm(hm, self.norm, mode, self.spec.eps)
 
-    def body(self, p: Any, plan: BlockPlan | None = None, images: ImagePlan | None = None) -> torch.Tensor:
+    def body(self, p: Any, plan: BlockPlan | None = None, images: ImagePlan | JointImages | None = None
+             ) -> torch.Tensor:
         """(T, hidden) hidden states after every layer the whole pack runs (all but the last in a bidirectional
         model; the workspace's residual buffer): embedding and layers, no host synchronization, so it can be captured
         in a CUDA graph when ``p``'s tensors are static. Branched block layouts need their ``plan``; packs with
@@ -536,7 +578,9 @@ class Packed(torch.nn.Module):
         ws = self.workspace(t)
         qwen = s.family == "qwen"
         h = ops.embed(p.input_ids, self.embed_tokens, 0.0 if qwen else math.sqrt(s.hidden), out=ws.h[:t])
-        if images is not None:  # the features over the scaled token embeddings, unscaled (families/gemma/packed.py:316)
+        joint = images if isinstance(images, JointImages) else None
+        if images is not None:  # the features over the (Gemma: scaled) token embeddings at the image-token rows
+            # (families/qwen/packed.py:161-165, families/gemma/packed.py:316)
             features = self.image_features(p)
             if features.shape[0] != images.rows.numel():
                 raise ValueError(f"{images.rows.numel()} soft tokens for {features.shape[0]} image features")
@@ -546,7 +590,7 @@ class Packed(torch.nn.Module):
             if layer.kind == "linear_attention":
                 self._after_attention(layer, h, self._linear_mixer(layer, h, p, ws), ws)
                 continue
-            q, k, v, gate = self._attention_inputs(layer, h, p, ws, rope_cs)
+            q, k, v, gate = self._attention_inputs(layer, h, p, ws, rope_cs, joint)
             window = (self.window - 1, 0) if layer.kind == "sliding_attention" else self.full_window
             o_buf = ws.o(s, layer.kind, t)
             if plan is None:
@@ -558,7 +602,7 @@ class Packed(torch.nn.Module):
                 kg, vg = ops.gather_rows(k, rows), ops.gather_rows(v, rows)
                 o = ops.attention_varlen(q, kg, vg, plan.q_cu, k_cu, plan.max_q, self._scale, window, gate=gate,
                                          out=o_buf, sched=ws.sched)
-            if images is not None and layer.kind == "sliding_attention":
+            if isinstance(images, ImagePlan) and layer.kind == "sliding_attention":
                 # each image's rows again, over the window before the image and the whole image
                 # (families/gemma/vision.py:199-210)
                 oi = ops.attention_varlen(ops.gather_rows(q, images.rows), ops.gather_rows(k, images.keys),
@@ -596,9 +640,10 @@ class Packed(torch.nn.Module):
                               out=ws.gn[:t])
 
     def _attention_inputs(self, layer: Layer, h: torch.Tensor, p: Any, ws: Workspace,
-                          rope_cs: dict[str, torch.Tensor]) -> tuple:
+                          rope_cs: dict[str, torch.Tensor], joint: JointImages | None = None) -> tuple:
         """q, k, v (normed, rotated) and Qwen's gate for every row of ``h`` (the layer's input norm and QKV
-        projection; families/qwen/packed.py:108-121, families/gemma/packed.py:183-193)."""
+        projection; families/qwen/packed.py:108-121, families/gemma/packed.py:183-193). ``joint``: a Qwen pack with
+        images, rotated by its M-RoPE tables (a row per token, read at the token's own index)."""
         s = self.spec
         t = h.shape[0]
         qwen = s.family == "qwen"
@@ -607,7 +652,10 @@ class Packed(torch.nn.Module):
         fp8_qkv = any(proj.fp8 for proj, _, _ in layer.qkv)
         bf16_qkv = any(not proj.fp8 for proj, _, _ in layer.qkv)
         x, x8 = self._normed(ws, h, layer.input_norm, mode, bf16_qkv, fp8_qkv)
-        cos, sin = self.tables(layer.kind, int(p.max_length))  # a position is below its sequence's length
+        if joint is not None:
+            seqpos, cos, sin = joint.index, joint.cos, joint.sin
+        else:
+            cos, sin = self.tables(layer.kind, int(p.max_length))  # a position is below its sequence's length
         heads_out = ws.heads(s, layer.kind, t)
         hd, hkv = s.attn_dims(layer.kind)
         v_mode = -1 if qwen else ops.NORM_NONE
@@ -649,14 +697,15 @@ class Packed(torch.nn.Module):
             d = self._project(layer.down, m, m8, ws.a[:t])
             ops.norm_add(h, d, layer.post_feedforward_norm, mode, s.eps, scalar=layer.scalar, out=h)
 
-    def _last_layer_at_markers(self, h: torch.Tensor, p: Any, plan: BlockPlan | None) -> torch.Tensor:
+    def _last_layer_at_markers(self, h: torch.Tensor, p: Any, plan: BlockPlan | None,
+                               joint: JointImages | None = None) -> torch.Tensor:
         """(M, hidden) before the final norm: the last layer for the marker rows only (families/qwen/packed.py:127-140,
         families/gemma/packed.py:267-281). Every row's keys and values come from one QKV projection of ``h`` (the
         queries and gates are then read at the markers); each marker attends to every key of its sequence (Gemma: of
         its virtual sequence) without a mask; output projection and MLP run on the marker rows."""
         layer = self.layers[-1]
         ws = self.workspace(h.shape[0])
-        q, k, v, gate = self._attention_inputs(layer, h, p, ws, {})
+        q, k, v, gate = self._attention_inputs(layer, h, p, ws, {}, joint)
         markers = p.markers
         n = int(markers.numel())
         qm = ops.gather_rows(q, markers)

@@ -56,9 +56,25 @@ class Spec:
     lin_k_dim: int = 128
     lin_v_dim: int = 128
     conv_kernel: int = 4
+    # Qwen3.5 joint layouts with images: the interleaved M-RoPE sections (time, height, width frequency pairs; their
+    # sum is the rotary pairs) of Transformers' rope_parameters["mrope_section"]. None: positions on one axis only.
+    mrope_section: tuple | None = None
 
     def as_dict(self) -> dict:
         return asdict(self)
+
+    def pair_axes(self) -> list[int]:
+        """The position axis (0 time, 1 height, 2 width) each rotary frequency pair of a Qwen full-attention layer
+        reads under interleaved M-RoPE (Transformers' apply_interleaved_mrope): pair i reads height when i % 3 == 1 and
+        i < 3 * sections[1], width when i % 3 == 2 and i < 3 * sections[2], time otherwise."""
+        half = int(self.head_dim * self.partial_rotary) // 2
+        if self.mrope_section is None:
+            return [0] * half
+        sections = [int(x) for x in self.mrope_section]
+        if len(sections) != 3 or sum(sections) != half:
+            raise ValueError(f"mrope_section {sections} must split the {half} rotary pairs into 3")
+        return [1 if i % 3 == 1 and i < 3 * sections[1] else 2 if i % 3 == 2 and i < 3 * sections[2] else 0
+                for i in range(half)]
 
     def attn_dims(self, kind: str) -> tuple[int, int]:
         """(head size, key/value heads) of a layer of ``kind``."""

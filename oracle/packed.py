@@ -124,6 +124,26 @@ def rope_tables(positions: np.ndarray, head_dim: int, theta: float, partial: flo
     return _round(np.cos(emb), mode), _round(np.sin(emb), mode)
 
 
+def mrope_tables(rope: np.ndarray, head_dim: int, theta: float, partial: float, sections, mode: str
+                 ) -> tuple[np.ndarray, np.ndarray]:
+    """cos/sin (T, rot) of Qwen3.5's interleaved M-RoPE at the (3, T) positions ``rope`` (time, height, width):
+    freqs per axis as rope_tables forms them, then pair i takes the height axis where i % 3 == 1 and i < 3 *
+    sections[1], the width axis where i % 3 == 2 and i < 3 * sections[2], the time axis otherwise (Transformers'
+    Qwen3_5TextRotaryEmbedding.apply_interleaved_mrope), emb = cat(f, f)."""
+    rot = int(head_dim * partial)
+    half = rot // 2
+    inv_freq = (1.0 / (np.float32(theta) ** (np.arange(0, rot, 2, dtype=np.float32) / np.float32(rot)))
+                ).astype(np.float32)
+    freqs = rope.astype(np.float32)[:, :, None] * inv_freq[None, None, :]  # (3, T, half)
+    f = freqs[0].copy()
+    for axis in (1, 2):
+        idx = np.arange(axis, 3 * int(sections[axis]), 3)
+        idx = idx[idx < half]
+        f[:, idx] = freqs[axis][:, idx]
+    emb = np.concatenate([f, f], axis=-1)
+    return _round(np.cos(emb), mode), _round(np.sin(emb), mode)
+
+
 def apply_rope(x: np.ndarray, cos: np.ndarray, sin: np.ndarray) -> np.ndarray:
     """Rotate-half RoPE on the first ``rot`` dims of (T, H, hd) (Transformers apply_rotary_pos_emb, partial rotary
     as in Qwen3.5; families/gemma/fused.py:41-45)."""
@@ -353,14 +373,22 @@ def qwen_forward(weights: dict, spec: dict, pack: dict, mode: str = "fp32", fp8:
     activation quantized from its bf16 value at each call). ``spec["attention"] == "bidirectional"`` widens the window
     to (-1, -1) (:31-32); the reference then runs the last layer for the marker rows only (:127-140), whose result is
     the marker rows of the whole layer, which is what this restatement computes (pinned by the ``qwen_bidir``
-    fixture)."""
+    fixture). Joint layouts with images (``pack["image_features"]``, ``pack["image_token"]``, ``pack["rope"]``): the
+    features replace the image tokens' embeddings in order (:161-165) and RoPE takes the M-RoPE positions (:186)."""
     eps, hq, hkv, hd = spec["eps"], spec["heads"], spec["kv_heads"], spec["head_dim"]
     if fp8:
         weights = quantize_weights(weights, QWEN_FP8_MIN_FEATURES)
     ids, seqpos, cu = pack["input_ids"], pack["seqpos"], pack["cu"]
     t = len(ids)
     h = _round(weights["embed_tokens"][ids], mode)  # :158-159
-    cos, sin = rope_tables(seqpos, hd, spec["rope_theta"], spec.get("partial_rotary", 1.0), mode)  # :186
+    if pack.get("image_features") is not None:  # :161-165 masked_scatter, features cast to the activations' dtype
+        h = h.copy()
+        h[ids == pack["image_token"]] = _round(pack["image_features"].astype(np.float32), mode)
+    if pack.get("rope") is not None:  # :186 with Pack.rope
+        cos, sin = mrope_tables(np.asarray(pack["rope"]).reshape(3, -1), hd, spec["rope_theta"],
+                                spec.get("partial_rotary", 1.0), spec["mrope_section"], mode)
+    else:
+        cos, sin = rope_tables(seqpos, hd, spec["rope_theta"], spec.get("partial_rotary", 1.0), mode)  # :186
     window = (-1, 0) if spec.get("attention", "causal") == "causal" else (-1, -1)
     every = spec.get("full_every", 0)
     for i in range(spec["layers"]):

@@ -22,7 +22,7 @@ def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
 
     rot = int(spec.head_dim * spec.partial_rotary)
     half = rot // 2
-    section = [half - 2 * (half // 3), half // 3, half // 3]
+    section = list(spec.mrope_section) if spec.mrope_section else [half - 2 * (half // 3), half // 3, half // 3]
     text = dict(vocab_size=spec.vocab, hidden_size=spec.hidden, intermediate_size=spec.intermediate,
                 num_hidden_layers=spec.layers, num_attention_heads=spec.heads, num_key_value_heads=spec.kv_heads,
                 head_dim=spec.head_dim, rms_norm_eps=spec.eps, layer_types=spec.layer_types(),
@@ -32,7 +32,8 @@ def qwen_backbone(spec: Spec, weights: dict[str, np.ndarray]):
                 linear_num_value_heads=spec.lin_v_heads, linear_key_head_dim=spec.lin_k_dim,
                 linear_value_head_dim=spec.lin_v_dim, linear_conv_kernel_dim=spec.conv_kernel)
     config = Qwen3_5Config(text_config=text, vision_config={"depth": 1, "hidden_size": 32, "intermediate_size": 64,
-                                                           "num_heads": 2, "out_hidden_size": spec.hidden})
+                                                           "num_heads": 2, "out_hidden_size": spec.hidden},
+                           image_token_id=spec.vocab - 1)  # the fixtures' image token (the last id)
     config._attn_implementation = "sdpa"
     model = Qwen3_5Model(config).float().eval()
     lm = model.language_model

@@ -144,6 +144,12 @@ def encoded(arrays: dict[str, np.ndarray], blocks: bool):
                       segment_ids=torch.from_numpy(arrays["segment_ids"][a:b].astype(np.int16)))
         elif blocks:
             kw = dict(positions=torch.arange(n), segment_ids=torch.zeros(n, dtype=torch.int16))
+        if "image_grids" in arrays:  # Qwen joint layouts: this sequence's images, in row order
+            grids = [g for row, g in zip(arrays["image_rows"], arrays["image_grids"]) if a <= row < b]
+            if grids:
+                ids = torch.from_numpy(arrays["input_ids"][a:b].copy())
+                kw = dict(mm_token_type_ids=(ids == IMAGE_TOKEN).to(torch.int32), pixel_values=torch.zeros(1, 1),
+                          image_grid_thw=torch.tensor(np.asarray(grids, dtype=np.int64)))
         out.append(Encoded(keys=tuple(f"q{i}" for i in range(len(local))), counts=(3,) * len(local),
                            input_ids=torch.from_numpy(arrays["input_ids"][a:b].copy()), markers=local, **kw))
     return out
@@ -241,6 +247,12 @@ CASES.update({
                                  dtype="bf16"),
     "gemma_tiny_fp8_served": dict(spec=Spec("gemma", 6, 256, 4, 2, 64, 512, 4096, window=16, logit_cap=30.0),
                                   lengths=("uniform", 16, 8, 96), markers=(1, 1), fp8=True, dtype="bf16"),
+    # Qwen3.5 joint layouts with images (families/qwen/packed.py:158-165, :186): image-token runs whose embeddings
+    # the given features replace, and the reference's own M-RoPE positions (model/packed.py:64-70, the backbone's
+    # get_rope_index over each image's (1, h, w) grid, merged 2 x 2); two sequences with images, one without
+    "qwen_images": dict(spec=dataclasses.replace(CONFIGS["tiny"], mrope_section=(12, 10, 10)),
+                        lengths=("list", 90, 70, 120), markers=(2, 4), fp8=False,
+                        joint_images=[(20, 4, 6), (50, 2, 4), (100, 6, 4), (130, 4, 4)]),
 })
 
 
@@ -306,6 +318,10 @@ def reference_forward(case: dict, spec: Spec, weights: dict, arrays: dict, seqs:
             model = to_dtype(qwen_backbone(spec, weights), cast)
             stack.enter_context(_patched(qp, "_kernels", lambda: (delta_rule_contract, varlen_contract,
                                                                    conv_contract)))
+            if features is not None:  # the vision tower's output, given
+                given = torch.from_numpy(arrays["image_features"]).to(cast)
+                stack.enter_context(_patched(model, "get_image_features",
+                                             lambda *_, **__: types.SimpleNamespace(pooler_output=[given])))
             packed = qp.Packed(model, spec.attention)
             if case["fp8"]:
                 from karpo_decision.serve import qwen_fp8
@@ -314,6 +330,8 @@ def reference_forward(case: dict, spec: Spec, weights: dict, arrays: dict, seqs:
                     _name_pins(packed, qwen_fp8)
                     _record_fp8(stack, qwen_fp8, captured)
             p = pack(seqs, model, torch.device("cpu"))
+            if p.rope is not None and features is not None:
+                captured["rope"] = p.rope
         else:
             from karpo_decision.families.gemma import packed as gp
             from karpo_decision.families.gemma import sliding_attention
@@ -367,8 +385,22 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
         n_soft = sum(length for _, length in case["images"])
         features = np.random.default_rng(seed + 2).standard_normal((n_soft, spec.hidden)).astype(np.float32) * 0.3
         arrays["image_features"] = oracle_bf16(features)
+    if "joint_images" in case:  # Qwen: an image of grid (1, gh, gw) is gh * gw / 4 image tokens from `row` on
+        arrays = dict(arrays, input_ids=arrays["input_ids"].copy())
+        arrays["input_ids"][arrays["input_ids"] == IMAGE_TOKEN] = 0
+        rows, grids, n_soft = [], [], 0
+        for row, gh, gw in case["joint_images"]:
+            tokens = gh * gw // 4
+            arrays["input_ids"][row:row + tokens] = IMAGE_TOKEN
+            rows.append(row)
+            grids.append((1, gh, gw))
+            n_soft += tokens
+        arrays["image_rows"], arrays["image_grids"] = np.asarray(rows), np.asarray(grids)
+        features = np.random.default_rng(seed + 2).standard_normal((n_soft, spec.hidden)).astype(np.float32) * 0.3
+        arrays["image_features"] = oracle_bf16(features)
+        features = arrays["image_features"]
     seqs = encoded(arrays, blocks=spec.family == "gemma")
-    if features is not None:  # the sequences with soft tokens carry (placeholder) pixels, so the pack has images
+    if features is not None and spec.family == "gemma":  # sequences with soft tokens carry (placeholder) pixels
         seqs = [dataclasses.replace(q, pixel_values=torch.zeros(1, 1), image_position_ids=torch.zeros(1, 1, 2))
                 if bool((q.input_ids == IMAGE_TOKEN).any()) else q for q in seqs]
     hidden, logits, captured = reference_forward(case, spec, weights, arrays, seqs, features, case.get("dtype", "fp32"))
@@ -376,6 +408,7 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
     if case.get("dtype", "fp32") == "bf16":  # the float32 run of the same case, the noise reference
         h32, l32, _ = reference_forward(case, spec, weights, arrays, seqs, features, "fp32", record=False)
         noise = {"hidden_fp32": h32.float().numpy(), "logits_fp32": l32.float().numpy()}
+    rope = captured.pop("rope", None)
     pins = {}
     for proj, (values, scale, out) in captured.items():
         if values.dtype == np.uint8:  # full width, served bf16 path
@@ -383,6 +416,8 @@ def run_case(name: str, case: dict, seed: int = 0) -> dict[str, np.ndarray]:
         else:
             pins[f"pin_{proj}_in"], pins[f"pin_{proj}_scale"], pins[f"pin_{proj}_out"] = values, scale, out
     extra = {k: arrays[k] for k in ("segment_ids", "image_features") if k in arrays}
+    if rope is not None:
+        extra["rope"] = rope.reshape(rope.shape[0], -1).numpy()
     return {
         **pins, **extra, **noise,
         "input_ids": arrays["input_ids"], "seqpos": arrays["seqpos"], "cu": arrays["cu"],

@@ -13,7 +13,8 @@ from karpo_decision_b200.synthetic import Spec, numpy_weights
 GOLDEN = Path(__file__).resolve().parent / "golden"
 IMAGE_TOKEN = 4095  # the image cases' soft-token id
 CASES = ["qwen_tiny", "qwen_partial", "gemma_tiny", "gemma_blocks", "qwen_tiny_fp8", "gemma_tiny_fp8", "qwen_bidir",
-         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid", "gemma_images", "qwen_hybrid128"]
+         "gemma_bidir", "gemma_blocks_bidir", "gemma_global512", "qwen_hybrid", "gemma_images", "qwen_hybrid128",
+         "qwen_images"]
 #: BASELINE configurations 2-5 at full width (depth cut), from the reference's bf16 path (float32 run beside it).
 WIDE = ["qwen_0p8b", "qwen_4b_fp8", "gemma_12b", "gemma_12b_fp8", "gemma_31b_fp8"]
 
@@ -30,8 +31,8 @@ def load(name: str) -> tuple[Spec, dict, dict, dict]:
         h.update(np.ascontiguousarray(weights[key], dtype=np.float32).tobytes())
     if h.hexdigest() != str(z["weights_sha256"]):
         raise AssertionError(f"{name}: regenerated weights differ from the ones the fixture was made with")
-    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu", "segment_ids", "image_features")
-            if k in z.files}
+    pack = {k: z[k] for k in ("input_ids", "seqpos", "cu", "markers", "marker_cu", "segment_ids", "image_features",
+                              "rope") if k in z.files}
     if "image_features" in pack:  # the image cases' soft-token id (tests/golden/make_golden.py IMAGE_TOKEN)
         pack["image_token"] = IMAGE_TOKEN
     expected = {k: z[k] for k in ("hidden", "logits", "hidden_fp32", "logits_fp32") if k in z.files}

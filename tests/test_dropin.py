@@ -79,3 +79,14 @@ def test_readout_from_reference_reads_rows_and_cap():
     rows = torch.randn(5, 64)
     head = Readout.from_reference(ReferenceReadout(rows, 30.0), device=CPU)
     assert torch.equal(head.weight.cpu(), rows) and head.cap == 30.0
+
+
+def test_from_backbone_reads_the_mrope_sections_and_image_token():
+    """A Qwen3.5 backbone's interleaved M-RoPE sections and image token reach the spec and the model, and its vision
+    tower is wired as the image-feature source (families/qwen/packed.py:70, :161-163)."""
+    spec, weights, _, _ = load("qwen_images")
+    model = Packed.from_backbone(qwen_backbone(spec, weights), device=CPU)
+    assert model.spec.mrope_section == (12, 10, 10)
+    assert model.image_token_id == spec.vocab - 1 and model.image_features is not None
+    axes = model.spec.pair_axes()
+    assert axes[:7] == [0, 1, 2, 0, 1, 2, 0] and axes[30:] == [0, 0] and len(axes) == 32

@@ -208,6 +208,38 @@ def test_rope_table_matches_transformers_formula():
         assert (diff > 0).float().mean().item() < 1e-4 and diff.max().item() <= 2 ** -8
 
 
+def test_mrope_tables_match_transformers_rotary_module():
+    """M-RoPE tables (one row per token) against Transformers' own Qwen3_5TextRotaryEmbedding (interleaved sections)
+    run by torch on the same GPU over the same (3, 1, T) positions, and equal to kd_rope_table's rows where a token's
+    three axes hold the same position."""
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextRotaryEmbedding
+
+    from karpo_decision_b200.synthetic import Spec
+
+    spec = Spec("qwen", 1, 256, 2, 1, 256, 512, 1024, partial_rotary=0.25, mrope_section=(11, 11, 10))
+    config = Qwen3_5TextConfig(hidden_size=256, num_attention_heads=2, num_key_value_heads=1, head_dim=256,
+                               rope_parameters={"rope_type": "default", "rope_theta": 1e7,
+                                                "partial_rotary_factor": 0.25, "mrope_section": [11, 11, 10]})
+    module = Qwen3_5TextRotaryEmbedding(config, device=DEV)
+    g = rng(31)
+    t = 3000
+    text = np.arange(t)
+    pos = np.stack([text, text, text])
+    pos[1, 100:400] = 100 + g.integers(0, 40, 300)  # an image's height and width positions
+    pos[2, 100:400] = 100 + g.integers(0, 40, 300)
+    positions = torch.from_numpy(pos).to(DEV)
+    axis = torch.tensor(spec.pair_axes(), dtype=torch.int32, device=DEV)
+    cos, sin = ops.rope_table_axes(module.inv_freq.float().contiguous(), positions, axis)
+    want_cos, want_sin = module(torch.zeros(1, dtype=torch.bfloat16, device=DEV), positions[:, None, :])
+    for got, want in ((cos, want_cos[0].float()), (sin, want_sin[0].float())):
+        diff = (got - want).abs()
+        assert (diff > 0).float().mean().item() < 1e-4 and diff.max().item() <= 2 ** -8
+    plain_cos, plain_sin = ops.rope_table(module.inv_freq.float().contiguous(), t)
+    text_rows = torch.from_numpy(np.r_[0:100, 400:t]).to(DEV)
+    assert torch.equal(cos[text_rows], plain_cos[text_rows]) and torch.equal(sin[text_rows], plain_sin[text_rows])
+
+
 @pytest.mark.parametrize("family,hd,partial", [("qwen", 128, 1.0), ("qwen", 64, 0.5), ("gemma", 256, 1.0),
                                                ("gemma", 128, 1.0), ("gemma", 512, 1.0)])
 def test_qkv_norm_rope_matches_oracle(family, hd, partial):

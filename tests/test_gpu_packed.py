@@ -67,13 +67,17 @@ def test_bf16_forward_tracks_bf16_oracle(name):
 @pytest.mark.parametrize("name", ["qwen_tiny_fp8_served", "gemma_tiny_fp8_served"])
 def test_fp8_forward_meets_the_served_fp8_bar(name):
     """BASELINE configuration 1's shape against the reference's served ``--fp8`` path (its bf16 backbone quantized as
-    ``--fp8`` does at load): the readout bar at 2e-2, or at the reference's own distance between that path and its
-    float32 ``--fp8`` run where that is larger (0.050 and 0.115 on these cases: single e4m3 rounding flips)."""
+    ``--fp8`` does at load). The reference's own two FP8 realizations (served and float32 ``--fp8``) lie 0.050 and
+    0.115 apart on these cases (single e4m3 rounding flips move a random model's readout), so another FP8 realization
+    that is no noisier lies within twice that of the served one (the triangle bound); the bar is 2e-2 or that bound,
+    whichever is larger, with the same top answers on clear margins."""
     spec, weights, arrays, expected, hidden, logits = run_b200(name)
     floor = float(np.abs(expected["logits"] - expected["logits_fp32"]).max())
-    err, agree, ties = readout_bar(logits, expected["logits"], max(2e-2, floor))
-    print(f"{name}: readout max-abs vs the reference's served --fp8 path {err:.4f} (its own served vs float32 --fp8: "
-          f"{floor:.4f}), top answers agree on {agree:.0%} of {len(logits)} ({ties} near ties)")
+    err, agree, ties = readout_bar(logits, expected["logits"], max(2e-2, 2 * floor))
+    err32 = float(np.abs(logits - expected["logits_fp32"]).max())
+    print(f"{name}: readout max-abs vs the reference's served --fp8 path {err:.4f} and its float32 --fp8 run "
+          f"{err32:.4f} (its own served vs float32 --fp8: {floor:.4f}), top answers agree on {agree:.0%} of "
+          f"{len(logits)} ({ties} near ties)")
 
 
 @pytest.mark.parametrize("name", ["qwen_tiny_fp8", "gemma_tiny_fp8"])
@@ -129,6 +133,31 @@ def test_bidirectional_marker_layer_equals_the_whole_last_layer(name):
     p = from_arrays(arrays, DEV)
     a, b = pruned(p).float(), whole(from_arrays(arrays, DEV)).float()
     assert torch.allclose(a, b, atol=2e-2, rtol=2e-2), (a - b).abs().max().item()
+
+
+def test_qwen_images_match_reference():
+    """Qwen3.5 joint layouts with images (families/qwen/packed.py:158-165, :186): the image features written over
+    the image tokens' embeddings and RoPE at the reference's own M-RoPE positions (Pack.rope from its pack(), the
+    backbone's get_rope_index); the vision tower's output is given (the fixture's features), as the reference's was."""
+    from golden_cases import IMAGE_TOKEN
+
+    spec, weights, arrays, expected = load("qwen_images")
+    features = torch.from_numpy(arrays["image_features"]).to(DEV)
+    model = Packed(spec, weights, DEV, image_token_id=IMAGE_TOKEN, image_features=lambda p: features)
+    head = Readout(weights["readout"], spec.logit_cap, DEV)
+    p = from_arrays(dict(arrays, pixel_values=np.zeros((1, 1), np.float32)), DEV)
+    hidden = model(p)
+    logits = head(hidden).cpu().numpy()
+    err, agree, ties = readout_bar(logits, expected["logits"])
+    print(f"qwen_images: readout max-abs vs reference {err:.3g}, top answers agree on {agree:.0%} ({ties} near ties)")
+    h = hidden.float().cpu().numpy()
+    cosine = (h * expected["hidden"]).sum(-1) / (np.linalg.norm(h, axis=-1) * np.linalg.norm(expected["hidden"],
+                                                                                               axis=-1))
+    assert cosine.min() > 0.995, cosine
+    # the M-RoPE positions matter: the same features at the tokens' plain positions give another answer
+    plain_pos = dict(arrays, rope=np.stack([arrays["seqpos"]] * 3), pixel_values=np.zeros((1, 1), np.float32))
+    moved = model(from_arrays(plain_pos, DEV)).float().cpu().numpy()
+    assert np.abs(moved - expected["hidden"]).max() > 10 * np.abs(h - expected["hidden"]).max()
 
 
 def test_gemma_images_match_reference():
