@@ -271,3 +271,39 @@ def test_block_and_image_plans_match_oracle_on_random_layouts():
         assert plan.keys.tolist() == np.concatenate([seen for _, _, seen in spans]).tolist()
         checked_images += 1
     assert checked_images == 200
+
+
+def test_mrope_pair_axes_and_oracle_tables_follow_transformers():
+    """Spec.pair_axes (the axis each rotary pair reads, which kd_rope_table_axes takes) and the oracle's M-RoPE tables
+    against Transformers' own Qwen3_5TextRotaryEmbedding on the host, over positions whose three axes differ."""
+    import torch
+    from transformers.models.qwen3_5.configuration_qwen3_5 import Qwen3_5TextConfig
+    from transformers.models.qwen3_5.modeling_qwen3_5 import Qwen3_5TextRotaryEmbedding
+
+    import oracle
+
+    for head_dim, partial, sections in ((256, 0.25, (11, 11, 10)), (64, 1.0, (12, 10, 10))):
+        spec = Spec("qwen", 1, 256, 2, 1, head_dim, 512, 1024, partial_rotary=partial, mrope_section=sections)
+        config = Qwen3_5TextConfig(hidden_size=256, num_attention_heads=2, num_key_value_heads=1, head_dim=head_dim,
+                                   rope_parameters={"rope_type": "default", "rope_theta": 1e7,
+                                                    "partial_rotary_factor": partial,
+                                                    "mrope_section": list(sections)})
+        module = Qwen3_5TextRotaryEmbedding(config)
+        rng = np.random.default_rng(3)
+        pos = rng.integers(0, 500, size=(3, 200))
+        # which axis each pair reads: positions that differ on one axis only move exactly that axis's pairs
+        axes = spec.pair_axes()
+        for axis in range(3):
+            shifted = pos.copy()
+            shifted[axis] += 1
+            def freqs(p):  # the module's own layout: (3, batch, tokens, pairs), then its interleaving
+                f = (module.inv_freq[None, None, :, None].expand(3, 1, -1, 1).float()
+                     @ torch.from_numpy(p)[:, None, None, :].float()).transpose(2, 3)
+                return module.apply_interleaved_mrope(f, list(sections))
+
+            moved = (freqs(pos) != freqs(shifted)).any(dim=1).reshape(-1).numpy()  # per frequency pair
+            assert moved.tolist() == [x == axis for x in axes], (head_dim, axis)
+        cos, sin = module(torch.zeros(1), torch.from_numpy(pos)[:, None, :])
+        want_cos, want_sin = oracle.packed.mrope_tables(pos, head_dim, 1e7, partial, sections, "fp32")
+        # float32 angles up to position 500: the two inv_freq computations may differ in the last bit
+        assert np.abs(cos[0].numpy() - want_cos).max() < 1e-4 and np.abs(sin[0].numpy() - want_sin).max() < 1e-4
