@@ -242,13 +242,6 @@ KD_DEVICE bool staged_epilogue(const Args& a, const Item& w, int n, int64_t col0
   return true;
 }
 
-// Brings a tile of a tensor into L2 ahead of its use.
-KD_DEVICE void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y) {
-  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y)
-               : "memory");
-}
-
 template <int HD, int DV>
 __global__ void __launch_bounds__(THREADS, Cfg<HD, DV>::CTAS_PER_SM)
     attention_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_k,

@@ -122,6 +122,13 @@ KD_DEVICE void tma_load_3d(const CUtensorMap* map, uint64_t* bar, void* dst, int
       : "memory");
 }
 
+// Brings the box at (x, y) of a tensor into L2 ahead of its use (no completion to wait for).
+KD_DEVICE void tma_prefetch_l2(const CUtensorMap* map, int32_t x, int32_t y) {
+  asm volatile("cp.async.bulk.prefetch.tensor.2d.L2.global.tile [%0, {%1, %2}];" ::"l"(reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y)
+               : "memory");
+}
+
 // 2-D tiled store of a shared-memory box to (x, y) of the tensor; rows and columns past the tensor are clipped.
 KD_DEVICE void tma_store_2d(const CUtensorMap* map, const void* src, int32_t x, int32_t y) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(

@@ -550,6 +550,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool loaded = mbar_wait(load_bar, load_phase, status);
       load_phase ^= 1u;
       if (!(ok = __syncthreads_and(loaded) != 0)) break;
+      if (i == 0 && c0 + C < t1) {  // the next chunk's rows into L2 now: its loads are issued only at this chunk's end
+        for (int h = 0; h < 2; ++h) {
+          tma_prefetch_l2(&map_qkv, (int)(kd + (int64_t)khead * HD) + 64 * h, (int)(c0 + C));
+          tma_prefetch_l2(&map_qkv, khead * HD + 64 * h, (int)(c0 + C));
+          tma_prefetch_l2(&map_qkv, (int)(2 * kd + (int64_t)head * HD) + 64 * h, (int)(c0 + C));
+        }
+      }
       uint4 rk[16];
       auto take = [&](uint8_t* tile) -> float {  // this row of a tile (zeros past n), and its sum of squares
         float ss = 0.f;
