@@ -357,16 +357,16 @@ KD_DEVICE float fast_exp2(float x) {
   return y;
 }
 
-constexpr int C = 128;                // tokens per chunk = MMA rows = TMEM lanes = threads
+constexpr int C = 128;                // tokens per chunk = MMA rows = TMEM lanes
 constexpr int HD = 128;               // key and value head dim
-constexpr int THREADS = 128;
+constexpr int THREADS = 256;          // two threads per token row, each taking half of its columns
 constexpr int TILE = C * HD * 2;      // a 128 x 128 bf16 tile: two 64-column halves
 constexpr int HALF = C * 128;         // one half: 128 rows of 128 bytes (128-byte swizzle)
 constexpr int A_FLOATS = 8320;        // the strictly lower A, each row padded to a multiple of 4 floats
 constexpr int A_OFF = 6 * TILE;
 constexpr int G_OFF = A_OFF + A_FLOATS * 4;
 constexpr int MISC_OFF = G_OFF + C * 4;
-constexpr int SMEM = MISC_OFF + 64 + 1024;  // + alignment of the tiles to 1024 bytes
+constexpr int SMEM = MISC_OFF + 96 + 1024;  // + alignment of the tiles to 1024 bytes
 static_assert(SMEM <= 227 * 1024, "shared memory budget");
 // tiles: kn then P (K-major A) | qn then q~ (K-major A) | X_w = beta e^G kn (MN-major B) then W (K-major A) |
 // X_u = beta v (MN-major B) then S (MN-major B) | k~ = e^(G_last - G) kn (MN-major A) | T (K-major A)
@@ -400,10 +400,10 @@ KD_DEVICE void mma128(uint32_t d, uint32_t a, bool a_mn, uint32_t b, bool b_mn, 
   }
 }
 
-// Row r of a tile from 128 floats times `s`, rounded to bf16 (units in order, 16 bytes at a time).
-KD_DEVICE void put_row(uint8_t* tile, int r, const uint4 (&raw)[16], float s) {
+// Half hf of row r of a tile (units 8 hf .. 8 hf + 7, 64 values) from its raw bf16 units times `s`, rounded to bf16.
+KD_DEVICE void put_half(uint8_t* tile, int r, int hf, const uint4 (&raw)[8], float s) {
 #pragma unroll
-  for (int u = 0; u < 16; ++u) {
+  for (int u = 0; u < 8; ++u) {
     const uint32_t w[4] = {raw[u].x, raw[u].y, raw[u].z, raw[u].w};
     uint32_t o[4];
 #pragma unroll
@@ -411,7 +411,7 @@ KD_DEVICE void put_row(uint8_t* tile, int r, const uint4 (&raw)[16], float s) {
       const float2 f = unpack_bf16x2(w[e]);
       o[e] = pack_bf16x2(f.x * s, f.y * s);
     }
-    *reinterpret_cast<uint4*>(tile + unit_at(r, u)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(tile + unit_at(r, 8 * hf + u)) = make_uint4(o[0], o[1], o[2], o[3]);
   }
 }
 
@@ -442,13 +442,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* bar = reinterpret_cast<uint64_t*>(sm + MISC_OFF);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + MISC_OFF + 8);
   int* seq_s = reinterpret_cast<int*>(sm + MISC_OFF + 12);
-  float* wtot = reinterpret_cast<float*>(sm + MISC_OFF + 16);  // [4]
-  uint64_t* load_bar = reinterpret_cast<uint64_t*>(sm + MISC_OFF + 32);
+  float* wtot = reinterpret_cast<float*>(sm + MISC_OFF + 16);  // [8]: per warp, the scan's partial sums
+  uint64_t* load_bar = reinterpret_cast<uint64_t*>(sm + MISC_OFF + 48);
+  float* red = apk;  // [2][256] before A is built: each thread's half-row sums of squares (k, q)
 
-  const int i = threadIdx.x, warp = i >> 5, lane = i & 31;
+  // thread (row i, half hf): token row i of the chunk (its TMEM lane, in the warp's lane quarter) and the columns
+  // [64 hf, 64 hf + 64) of every row-wise phase; the two halves' warps share the row's TMEM lane quarter
+  const int tid = threadIdx.x, i = tid & (C - 1), hf = tid >> 7, warp = tid >> 5, lane = tid & 31;
   // the chain: value head `head` of the `rank`-th longest sequence (ties in pack order), so long chains start first
   const int rank = blockIdx.x / a.nv, head = blockIdx.x % a.nv;
-  if (i == 0) {
+  if (tid == 0) {
     *seq_s = rank;
     mbar_init(bar, 1);
     mbar_init(load_bar, 1);
@@ -456,7 +459,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&map_qkv);
   }
   __syncthreads();
-  for (int s0 = i; s0 < a.num_seqs; s0 += THREADS) {
+  for (int s0 = tid; s0 < a.num_seqs; s0 += THREADS) {
     const int len = a.cu[s0 + 1] - a.cu[s0];
     int before = 0;
     for (int s1 = 0; s1 < a.num_seqs; ++s1) {
@@ -473,7 +476,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t lane_base = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t lane_base = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   const int seq = *seq_s;
   const int64_t t0 = a.cu[seq], t1 = a.cu[seq + 1];
   const int khead = head / (a.nv / a.nk);
@@ -509,10 +512,10 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
     for (int e = 0; e < 32; ++e) z[e] = 0u;
 #pragma unroll
-    for (int cc = 0; cc < 4; ++cc) tmem_st32(lane_base + SST + 32 * cc, z);
+    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) tmem_st32(lane_base + SST + 32 * cc, z);
     tmem_st_wait();
   }
-  if (i == 0 && t0 < t1) load_chunk(t0);
+  if (tid == 0 && t0 < t1) load_chunk(t0);
   // this row's b and a inputs (write strength, decay) of the next chunk, fetched a chunk ahead
   float next_b = 0.f, next_a = 0.f;
   auto fetch_ab = [&](int64_t c0) {
@@ -541,8 +544,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (lane == 31) wtot[warp] = gi;
     __syncthreads();
-    for (int w2 = 0; w2 < warp; ++w2) gi += wtot[w2];
-    g_s[i] = gi;
+    for (int w2 = 4 * hf; w2 < warp; ++w2) gi += wtot[w2];
+    if (hf == 0) g_s[i] = gi;
     __syncthreads();
     const float g_last = g_s[n - 1];
     const float e_g = live ? expf(gi) : 0.f, e_tail = live ? expf(g_last - gi) : 0.f;
@@ -550,20 +553,20 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool loaded = mbar_wait(load_bar, load_phase, status);
       load_phase ^= 1u;
       if (!(ok = __syncthreads_and(loaded) != 0)) break;
-      if (i == 0 && c0 + C < t1) {  // the next chunk's rows into L2 now: its loads are issued only at this chunk's end
+      if (tid == 0 && c0 + C < t1) {  // the next chunk's rows into L2 now: its loads are issued only at this chunk's end
         for (int h = 0; h < 2; ++h) {
           tma_prefetch_l2(&map_qkv, (int)(kd + (int64_t)khead * HD) + 64 * h, (int)(c0 + C));
           tma_prefetch_l2(&map_qkv, khead * HD + 64 * h, (int)(c0 + C));
           tma_prefetch_l2(&map_qkv, (int)(2 * kd + (int64_t)head * HD) + 64 * h, (int)(c0 + C));
         }
       }
-      uint4 rk[16];
-      auto take = [&](uint8_t* tile) -> float {  // this row of a tile (zeros past n), and its sum of squares
+      uint4 rk[8], rq[8];
+      auto take = [&](uint8_t* tile, uint4 (&r)[8]) -> float {  // this thread's half of the row (zeros past n)
         float ss = 0.f;
 #pragma unroll
-        for (int u = 0; u < 16; ++u) {
-          rk[u] = live ? *reinterpret_cast<const uint4*>(tile + unit_at(i, u)) : make_uint4(0, 0, 0, 0);
-          const uint32_t w[4] = {rk[u].x, rk[u].y, rk[u].z, rk[u].w};
+        for (int u = 0; u < 8; ++u) {
+          r[u] = live ? *reinterpret_cast<const uint4*>(tile + unit_at(i, 8 * hf + u)) : make_uint4(0, 0, 0, 0);
+          const uint32_t w[4] = {r[u].x, r[u].y, r[u].z, r[u].w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const float2 f = unpack_bf16x2(w[e]);
@@ -572,20 +575,24 @@ __global__ void __launch_bounds__(THREADS, 1)
         }
         return ss;
       };
-      const float ik = rsqrtf(take(tile_kp) + 1e-6f);
-      put_row(tile_kp, i, rk, ik);
-      put_row(tile_xw, i, rk, ik * beta * e_g);
-      put_row(tile_kt, i, rk, ik * e_tail);
-      const float iq = rsqrtf(take(tile_q) + 1e-6f) * qscale;
-      put_row(tile_q, i, rk, iq);
-      take(tile_xu);
-      put_row(tile_xu, i, rk, beta);
+      red[tid] = take(tile_kp, rk);
+      red[THREADS + tid] = take(tile_q, rq);
+      __syncthreads();
+      // the row's sums: the first half's then the second's, in the same order for both threads of the row
+      const float ik = rsqrtf((red[i] + red[C + i]) + 1e-6f);
+      const float iq = rsqrtf((red[THREADS + i] + red[THREADS + C + i]) + 1e-6f) * qscale;
+      put_half(tile_kp, i, hf, rk, ik);
+      put_half(tile_xw, i, hf, rk, ik * beta * e_g);
+      put_half(tile_kt, i, hf, rk, ik * e_tail);
+      put_half(tile_q, i, hf, rq, iq);
+      take(tile_xu, rk);
+      put_half(tile_xu, i, hf, rk, beta);
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     // ---------------------------------------------------------------- K K^T -> ACC0, Q K^T -> ACC1
-    if (i == 0) {
+    if (tid == 0) {
       tc_fence_after();
       mma128(tmem + ACC0, s_kp, false, s_kp, false, false);
       mma128(tmem + ACC1, s_q, false, s_kp, false, false);
@@ -595,7 +602,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     {  // this row of A (packed, float32) and of P (bf16 over kn's tile); q~ = e^G qn in place
       float* arow = apk + a_row(i);
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {
         uint32_t kk[32], qk[32];
         tmem_ld32(lane_base + ACC0 + 32 * cc, kk);
         tmem_ld32(lane_base + ACC1 + 32 * cc, qk);
@@ -615,7 +622,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             *reinterpret_cast<float4*>(arow + 32 * cc + e) = make_float4(av[e], av[e + 1], av[e + 2], av[e + 3]);
       }
 #pragma unroll
-      for (int u = 0; u < 16; ++u) {
+      for (int u = 8 * hf; u < 8 * hf + 8; ++u) {
         uint4* at = reinterpret_cast<uint4*>(tile_q + unit_at(i, u));
         const uint4 v = *at;
         const uint32_t w[4] = {v.x, v.y, v.z, v.w};
@@ -635,6 +642,7 @@ __global__ void __launch_bounds__(THREADS, 1)
        // this thread's own lane of tensor memory (columns TCOL + row), read 16 at a time, so the loops stay rolled.
       const uint32_t tcol = lane_base + TCOL;
       const int base = i & ~63;  // the half this column belongs to
+      if (hf == 0) {  // the column solves run on the first half's threads, a column each
 #pragma unroll 1
       for (int b = 0; b < 4; ++b) {
         const int row0 = base + 16 * b;
@@ -685,26 +693,25 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int e = 0; e < 32; ++e)
           col[(unit_at(j0 + e, i >> 3) >> 1) + (i & 7)] = __float2bfloat16_rn(mine ? __uint_as_float(tv[e]) : 0.f);
       }
+      }
       // L = A's lower-left 64 x 64 block (rows 64.., columns ..63) as a bf16 K-major tile over A's space, zeros
-      // elsewhere: every thread reads its row first, then all write
-      float lrow[64];
+      // elsewhere: every thread reads its 32 columns of its row first (half hf: columns 32 hf ..), then all write
+      float lrow[32];
 #pragma unroll
-      for (int m = 0; m < 64; ++m) lrow[m] = i >= 64 ? apk[a_row(i) + m] : 0.f;
+      for (int m = 0; m < 32; ++m) lrow[m] = i >= 64 ? apk[a_row(i) + 32 * hf + m] : 0.f;
       __syncthreads();
-      put_cols(tile_d, i, 0, lrow);
-      put_cols(tile_d, i, 1, lrow + 32);
+      put_cols(tile_d, i, hf, lrow);
       float zero[32];
 #pragma unroll
       for (int m = 0; m < 32; ++m) zero[m] = 0.f;
-      put_cols(tile_d, i, 2, zero);
-      put_cols(tile_d, i, 3, zero);
+      put_cols(tile_d, i, 2 + hf, zero);
     }
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
     // ---------------------------------------------------------------- W = T X_w -> ACC0, U = T X_u -> ACC1
     // with T = T_bd - T_bd L T_bd ((T_bd L)^2 = 0: L has only the lower-left block): Z = T_bd X, Y = L Z, T X = Z - T_bd Y
-    if (i == 0) {
+    if (tid == 0) {
       tc_fence_after();
       mma128(tmem + ACC0, s_t, false, s_xw, true, false);
       mma128(tmem + ACC1, s_t, false, s_xu, true, false);
@@ -712,7 +719,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (!(ok = wait_mma())) break;
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {  // Z_w, Z_u -> bf16 over X_w, X_u (MN-major B, row = token)
+    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // Z_w, Z_u -> bf16 over X_w, X_u (MN-major B, row = token)
       uint32_t zw[32], zu[32];
       tmem_ld32(lane_base + ACC0 + 32 * cc, zw);
       tmem_ld32(lane_base + ACC1 + 32 * cc, zu);
@@ -723,14 +730,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (i == 0) {  // Y_w = L Z_w -> TCOL
+    if (tid == 0) {  // Y_w = L Z_w -> TCOL
       tc_fence_after();
       mma128(tmem + TCOL, s_d, false, s_xw, true, false);
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {  // Y_w -> bf16 over Z_w
+    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // Y_w -> bf16 over Z_w
       uint32_t y[32];
       tmem_ld32(lane_base + TCOL + 32 * cc, y);
       tmem_ld_wait_regs(y);
@@ -739,7 +746,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (i == 0) {  // W = Z_w - T_bd Y_w in ACC0; Y_u = L Z_u -> TCOL
+    if (tid == 0) {  // W = Z_w - T_bd Y_w in ACC0; Y_u = L Z_u -> TCOL
       tc_fence_after();
       mma128(tmem + ACC0, s_t, false, s_xw, true, true, true);
       mma128(tmem + TCOL, s_d, false, s_xu, true, false);
@@ -747,7 +754,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (!(ok = wait_mma())) break;
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {  // Y_u -> bf16 over Z_u; W row -> bf16 (K-major A) over Y_w
+    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // Y_u -> bf16 over Z_u; W row -> bf16 (K-major A) over Y_w
       uint32_t y[32], w[32];
       tmem_ld32(lane_base + TCOL + 32 * cc, y);
       tmem_ld32(lane_base + ACC0 + 32 * cc, w);
@@ -758,14 +765,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_async_smem();
     tc_fence_before();
     __syncthreads();
-    if (i == 0) {  // U = Z_u - T_bd Y_u in ACC1
+    if (tid == 0) {  // U = Z_u - T_bd Y_u in ACC1
       tc_fence_after();
       mma128(tmem + ACC1, s_t, false, s_xu, true, true, true);
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {  // S row (lane = key dim) -> bf16 (MN-major B) over Y_u
+    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // S row (lane = key dim) -> bf16 (MN-major B) over Y_u
       uint32_t sv[32];
       tmem_ld32(lane_base + SST + 32 * cc, sv);
       tmem_ld_wait_regs(sv);
@@ -775,7 +782,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
     // ---------------------------------------------------------------- X = W S -> ACC0
-    if (i == 0) {
+    if (tid == 0) {
       tc_fence_after();
       mma128(tmem + ACC0, s_xw, false, s_xu, true, false);
       mma_commit(bar);
@@ -784,7 +791,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     {
       const float gamma = expf(g_last);
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {  // D = U - W S -> bf16 (MN-major B, row = token)
+      for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // D = U - W S -> bf16 (MN-major B, row = token)
         uint32_t u[32], x[32];
         tmem_ld32(lane_base + ACC1 + 32 * cc, u);
         tmem_ld32(lane_base + ACC0 + 32 * cc, x);
@@ -795,7 +802,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         put_cols(tile_d, i, cc, d);
       }
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {  // S = gamma S, row by row in place
+      for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // S = gamma S, row by row in place
         uint32_t sv[32];
         tmem_ld32(lane_base + SST + 32 * cc, sv);
         tmem_ld_wait_regs(sv);
@@ -809,7 +816,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_before();
     __syncthreads();
     // ---------------------------------------------------------------- O = q~ S + P D -> ACC0, S += k~^T D
-    if (i == 0) {
+    if (tid == 0) {
       tc_fence_after();
       mma128(tmem + ACC0, s_q, false, s_xu, true, false);
       mma128(tmem + ACC0, s_kp, false, s_d, true, true);
@@ -817,10 +824,10 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-    if (i == 0 && c0 + C < t1) load_chunk(c0 + C);  // every tile the loads overwrite has been read
+    if (tid == 0 && c0 + C < t1) load_chunk(c0 + C);  // every tile the loads overwrite has been read
     fetch_ab(c0 + C);
 #pragma unroll 1
-    for (int cc = 0; cc < 4; ++cc) {
+    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {
       uint32_t o[32];
       tmem_ld32(lane_base + ACC0 + 32 * cc, o);
       tmem_ld_wait_regs(o);
