@@ -736,12 +736,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-#pragma unroll 1
-    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // Y_w -> bf16 over Z_w
-      uint32_t y[32];
-      tmem_ld32(lane_base + TCOL + 32 * cc, y);
-      tmem_ld_wait_regs(y);
-      put_cols(tile_xw, i, cc, reinterpret_cast<const float*>(y));
+    {  // Y_w -> bf16 over Z_w (this thread's two 32-column pieces, both loads in flight)
+      uint32_t y0[32], y1[32];
+      tmem_ld32(lane_base + TCOL + 64 * hf, y0);
+      tmem_ld32(lane_base + TCOL + 64 * hf + 32, y1);
+      tmem_ld_wait_regs(y0, y1);
+      put_cols(tile_xw, i, 2 * hf, reinterpret_cast<const float*>(y0));
+      put_cols(tile_xw, i, 2 * hf + 1, reinterpret_cast<const float*>(y1));
     }
     fence_async_smem();
     tc_fence_before();
@@ -771,12 +772,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-#pragma unroll 1
-    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // S row (lane = key dim) -> bf16 (MN-major B) over Y_u
-      uint32_t sv[32];
-      tmem_ld32(lane_base + SST + 32 * cc, sv);
-      tmem_ld_wait_regs(sv);
-      put_cols(tile_xu, i, cc, reinterpret_cast<const float*>(sv));
+    {  // S row (lane = key dim) -> bf16 (MN-major B) over Y_u
+      uint32_t s0[32], s1[32];
+      tmem_ld32(lane_base + SST + 64 * hf, s0);
+      tmem_ld32(lane_base + SST + 64 * hf + 32, s1);
+      tmem_ld_wait_regs(s0, s1);
+      put_cols(tile_xu, i, 2 * hf, reinterpret_cast<const float*>(s0));
+      put_cols(tile_xu, i, 2 * hf + 1, reinterpret_cast<const float*>(s1));
     }
     fence_async_smem();
     tc_fence_before();
@@ -801,14 +803,18 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int e = 0; e < 32; ++e) d[e] = __uint_as_float(u[e]) - __uint_as_float(x[e]);
         put_cols(tile_d, i, cc, d);
       }
-#pragma unroll 1
-      for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // S = gamma S, row by row in place
-        uint32_t sv[32];
-        tmem_ld32(lane_base + SST + 32 * cc, sv);
-        tmem_ld_wait_regs(sv);
+      {  // S = gamma S, row by row in place
+        uint32_t s0[32], s1[32];
+        tmem_ld32(lane_base + SST + 64 * hf, s0);
+        tmem_ld32(lane_base + SST + 64 * hf + 32, s1);
+        tmem_ld_wait_regs(s0, s1);
 #pragma unroll
-        for (int e = 0; e < 32; ++e) sv[e] = __float_as_uint(__uint_as_float(sv[e]) * gamma);
-        tmem_st32(lane_base + SST + 32 * cc, sv);
+        for (int e = 0; e < 32; ++e) {
+          s0[e] = __float_as_uint(__uint_as_float(s0[e]) * gamma);
+          s1[e] = __float_as_uint(__uint_as_float(s1[e]) * gamma);
+        }
+        tmem_st32(lane_base + SST + 64 * hf, s0);
+        tmem_st32(lane_base + SST + 64 * hf + 32, s1);
       }
       tmem_st_wait();
     }
@@ -826,19 +832,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!(ok = wait_mma())) break;
     if (tid == 0 && c0 + C < t1) load_chunk(c0 + C);  // every tile the loads overwrite has been read
     fetch_ab(c0 + C);
-#pragma unroll 1
-    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {
-      uint32_t o[32];
-      tmem_ld32(lane_base + ACC0 + 32 * cc, o);
-      tmem_ld_wait_regs(o);
+    {  // this row's outputs: its two 32-column pieces (both loads in flight), bf16 rows of the head's slice
+      uint32_t o0[32], o1[32];
+      tmem_ld32(lane_base + ACC0 + 64 * hf, o0);
+      tmem_ld32(lane_base + ACC0 + 64 * hf + 32, o1);
+      tmem_ld_wait_regs(o0, o1);
       if (live) {
-        __nv_bfloat16* orow = a.out + (c0 + i) * a.ldo + (int64_t)head * HD + 32 * cc;
+        __nv_bfloat16* orow = a.out + (c0 + i) * a.ldo + (int64_t)head * HD + 64 * hf;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
+        for (int q = 0; q < 8; ++q) {
+          const uint32_t* o = q < 4 ? o0 + 8 * q : o1 + 8 * (q - 4);
           uint32_t pk[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e)
-            pk[e] = pack_bf16x2(__uint_as_float(o[8 * q + 2 * e]), __uint_as_float(o[8 * q + 2 * e + 1]));
+          for (int e = 0; e < 4; ++e) pk[e] = pack_bf16x2(__uint_as_float(o[2 * e]), __uint_as_float(o[2 * e + 1]));
           *reinterpret_cast<uint4*>(orow + 8 * q) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
