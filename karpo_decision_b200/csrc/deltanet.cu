@@ -718,14 +718,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-#pragma unroll 1
-    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // Z_w, Z_u -> bf16 over X_w, X_u (MN-major B, row = token)
-      uint32_t zw[32], zu[32];
-      tmem_ld32(lane_base + ACC0 + 32 * cc, zw);
-      tmem_ld32(lane_base + ACC1 + 32 * cc, zu);
-      tmem_ld_wait_regs(zw, zu);
-      put_cols(tile_xw, i, cc, reinterpret_cast<const float*>(zw));
-      put_cols(tile_xu, i, cc, reinterpret_cast<const float*>(zu));
+    {  // Z_w, Z_u -> bf16 over X_w, X_u (MN-major B, row = token): four loads in flight, one wait
+      uint32_t w0[32], w1[32], u0[32], u1[32];
+      tmem_ld32(lane_base + ACC0 + 64 * hf, w0);
+      tmem_ld32(lane_base + ACC0 + 64 * hf + 32, w1);
+      tmem_ld32(lane_base + ACC1 + 64 * hf, u0);
+      tmem_ld32(lane_base + ACC1 + 64 * hf + 32, u1);
+      tmem_ld_wait_regs(w0, w1);
+      tmem_ld_wait_regs(u0, u1);  // no load left to wait for: ties u0, u1 to the wait above
+      put_cols(tile_xw, i, 2 * hf, reinterpret_cast<const float*>(w0));
+      put_cols(tile_xw, i, 2 * hf + 1, reinterpret_cast<const float*>(w1));
+      put_cols(tile_xu, i, 2 * hf, reinterpret_cast<const float*>(u0));
+      put_cols(tile_xu, i, 2 * hf + 1, reinterpret_cast<const float*>(u1));
     }
     fence_async_smem();
     tc_fence_before();
@@ -754,14 +758,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       mma_commit(bar);
     }
     if (!(ok = wait_mma())) break;
-#pragma unroll 1
-    for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // Y_u -> bf16 over Z_u; W row -> bf16 (K-major A) over Y_w
-      uint32_t y[32], w[32];
-      tmem_ld32(lane_base + TCOL + 32 * cc, y);
-      tmem_ld32(lane_base + ACC0 + 32 * cc, w);
-      tmem_ld_wait_regs(y, w);
-      put_cols(tile_xu, i, cc, reinterpret_cast<const float*>(y));
-      put_cols(tile_xw, i, cc, reinterpret_cast<const float*>(w));
+    {  // Y_u -> bf16 over Z_u; W row -> bf16 (K-major A) over Y_w: four loads in flight, one wait
+      uint32_t y0[32], y1[32], w0[32], w1[32];
+      tmem_ld32(lane_base + TCOL + 64 * hf, y0);
+      tmem_ld32(lane_base + TCOL + 64 * hf + 32, y1);
+      tmem_ld32(lane_base + ACC0 + 64 * hf, w0);
+      tmem_ld32(lane_base + ACC0 + 64 * hf + 32, w1);
+      tmem_ld_wait_regs(y0, y1);
+      tmem_ld_wait_regs(w0, w1);  // no load left to wait for: ties w0, w1 to the wait above
+      put_cols(tile_xu, i, 2 * hf, reinterpret_cast<const float*>(y0));
+      put_cols(tile_xu, i, 2 * hf + 1, reinterpret_cast<const float*>(y1));
+      put_cols(tile_xw, i, 2 * hf, reinterpret_cast<const float*>(w0));
+      put_cols(tile_xw, i, 2 * hf + 1, reinterpret_cast<const float*>(w1));
     }
     fence_async_smem();
     tc_fence_before();
@@ -792,16 +800,21 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (!(ok = wait_mma())) break;
     {
       const float gamma = expf(g_last);
-#pragma unroll 1
-      for (int cc = 2 * hf; cc < 2 * hf + 2; ++cc) {  // D = U - W S -> bf16 (MN-major B, row = token)
-        uint32_t u[32], x[32];
-        tmem_ld32(lane_base + ACC1 + 32 * cc, u);
-        tmem_ld32(lane_base + ACC0 + 32 * cc, x);
-        tmem_ld_wait_regs(u, x);
+      {  // D = U - W S -> bf16 (MN-major B, row = token): four loads in flight, one wait
+        uint32_t u0[32], u1[32], x0[32], x1[32];
+        tmem_ld32(lane_base + ACC1 + 64 * hf, u0);
+        tmem_ld32(lane_base + ACC1 + 64 * hf + 32, u1);
+        tmem_ld32(lane_base + ACC0 + 64 * hf, x0);
+        tmem_ld32(lane_base + ACC0 + 64 * hf + 32, x1);
+        tmem_ld_wait_regs(u0, u1);
+        tmem_ld_wait_regs(x0, x1);  // no load left to wait for: ties x0, x1 to the wait above
         float d[32];
 #pragma unroll
-        for (int e = 0; e < 32; ++e) d[e] = __uint_as_float(u[e]) - __uint_as_float(x[e]);
-        put_cols(tile_d, i, cc, d);
+        for (int e = 0; e < 32; ++e) d[e] = __uint_as_float(u0[e]) - __uint_as_float(x0[e]);
+        put_cols(tile_d, i, 2 * hf, d);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) d[e] = __uint_as_float(u1[e]) - __uint_as_float(x1[e]);
+        put_cols(tile_d, i, 2 * hf + 1, d);
       }
       {  // S = gamma S, row by row in place
         uint32_t s0[32], s1[32];
