@@ -14,7 +14,8 @@
 // one sequence for one query head (and value slice). Each CTA's first item is its index; the rest come from a
 // device counter that the last CTA to finish returns to zero. Items are ordered sequence by sequence, each
 // sequence's tiles from the last (the most expensive when causal) to the first, query heads innermost, so the heads
-// of one key/value group run at about the same time and share the key/value reads in L2. Head dim 512 (Gemma 4's
+// of one key/value group run at about the same time and share the key/value reads in L2; a sequence whose keys and
+// values outgrow L2 runs key/value head by key/value head (next_item). Head dim 512 (Gemma 4's
 // global layers) exceeds tensor memory for a whole output row block next to the scores, so its output is computed in
 // two 256-wide value slices (separate items), each forming the full scores (K and V single-buffered to fit the
 // 128 KB query tile). 6 warps:
@@ -105,27 +106,49 @@ KD_DEVICE float fast_exp2(float x) {
 }
 
 
+// Keys and values of a sequence (all its key/value heads) beyond which its items run key/value head by key/value head:
+// half of the 126 MB L2.
+constexpr int64_t KV_MAJOR_BYTES = 64ll << 20;
+
 // The next work item: item `idx` in the order sequences (pack order) > query tiles of the sequence, from its last
-// (the most expensive when causal) to its first > query heads > value slices. (cs, cbase) is the caller's cursor: a
-// sequence and the number of query tiles before it. A CTA's item indices only grow, so the cursor only moves forward.
+// (the most expensive when causal) to its first > query heads > value slices, so that the heads of one key/value
+// group run at about the same time and share the key/value reads in L2, and the launch ends on short items. A
+// sequence whose keys and values exceed KV_MAJOR_BYTES with no left window bound runs key/value head by key/value
+// head instead (tiles from the last, the group's query heads innermost): the CTAs running at one time then stream one
+// or two heads' keys and values, which stay in L2 however long the sequence (all heads of a 131,072-token sequence at
+// once re-read them from DRAM: 520 GB per launch at a 51% L2 hit rate, 950 TFLOP/s; head by head 1,110). (cs, cbase) is
+// the caller's cursor: a sequence and the number of query tiles before it. A CTA's item indices only grow, so the
+// cursor only moves forward.
 template <int HD, int DV>
 KD_DEVICE void next_item(const Args& a, int idx, int& cs, int& cbase, Item& w) {
   using C = Cfg<HD, DV>;
   constexpr int BM = C::BM, BN = C::BN;
   const int rest = idx / C::SLICES;
   w.slice = idx - rest * C::SLICES;
-  w.head = rest % a.hq;
-  const int tile = rest / a.hq;
+  const int coarse = rest / a.hq;  // a sequence of n query tiles holds n * hq consecutive values of `rest`
   w.n_tiles = -1;
   while (cs < a.num_seqs) {
     const int qa = a.cu_q[cs], qb = a.cu_q[cs + 1];
     const int n = (qb - qa + BM - 1) / BM;
-    if (tile < cbase + n) {
+    if (coarse < cbase + n) {
+      const int local = rest - cbase * a.hq;  // the item within its sequence
+      const int lk = a.cu_k[cs + 1] - a.cu_k[cs];
+      int tile;                                // 0: the sequence's last query tile
+      if (a.left < 0 && (int64_t)lk * a.hkv * HD * 4 > KV_MAJOR_BYTES) {
+        const int group = a.hq / a.hkv;
+        const int kvh = local / (n * group);
+        const int within = local - kvh * (n * group);
+        tile = within / group;
+        w.head = kvh * group + (within - tile * group);
+      } else {
+        tile = local / a.hq;
+        w.head = local - tile * a.hq;
+      }
       w.q0 = qa;
       w.lq = qb - qa;
       w.k0 = a.cu_k[cs];
       w.lk = a.cu_k[cs + 1] - w.k0;
-      w.qs = (n - 1 - (tile - cbase)) * BM;
+      w.qs = (n - 1 - tile) * BM;
       const int off = w.lk - w.lq;  // end alignment of queries to keys
       const int qe = min(w.qs + BM, w.lq);
       int kmin = 0, kmax = w.lk - 1;

@@ -209,9 +209,10 @@ def build(args: argparse.Namespace, dev: torch.device):
 def library_attention(lib: str, q, k, v, cu, lengths, scale, window):
     """The same attention by a library kernel on the same tensors (no output gate): ``fa2`` flash-attention 2's
     flash_attn_varlen_func (GQA native), ``flashinfer[:backend]`` its ragged-KV prefill (``auto``: the backend it
-    picks for this GPU; ``cutlass``: its sm100 kernel), ``torch``
+    picks for this GPU; ``cutlass``: its sm100 kernel), ``torch[:backend]``
     F.scaled_dot_product_attention per sequence with the key/value heads repeated to the query heads outside the timed
-    launch (whatever backend torch selects). Causal and sliding windows (left, 0) only."""
+    launch (whatever backend torch selects, or the one named: ``cudnn``, ``flash``, ``efficient``; ``cudnn`` is the
+    library the reference's head-512 global layers call). Causal and sliding windows (left, 0) only."""
     left, right = window
     if right != 0 and not (left < 0 and right < 0):
         raise SystemExit("library attention: causal, sliding or bidirectional windows")
@@ -238,9 +239,17 @@ def library_attention(lib: str, q, k, v, cu, lengths, scale, window):
         def run():
             wrapper.run(q, k, v)
         return run
-    if lib == "torch":
-        import torch.nn.functional as F
+    if lib.split(":")[0] == "torch":
+        import contextlib
 
+        import torch.nn.functional as F
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        backends = {"cudnn": SDPBackend.CUDNN_ATTENTION, "flash": SDPBackend.FLASH_ATTENTION,
+                    "efficient": SDPBackend.EFFICIENT_ATTENTION}
+        name = lib.split(":")[1] if ":" in lib else None
+        if name is not None and name not in backends:
+            raise SystemExit(f"torch SDPA backend {name}: one of {sorted(backends)}")
         group = hq // hkv
         kx, vx = k.repeat_interleave(group, dim=1), v.repeat_interleave(group, dim=1)
         bounds = cu.tolist()
@@ -249,10 +258,11 @@ def library_attention(lib: str, q, k, v, cu, lengths, scale, window):
             raise SystemExit("torch SDPA comparison: causal or bidirectional only")
 
         def run():
-            for a, b in zip(bounds[:-1], bounds[1:]):
-                F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None], kx[a:b].transpose(0, 1)[None],
-                                               vx[a:b].transpose(0, 1)[None], attn_mask=mask, is_causal=causal,
-                                               scale=scale)
+            with sdpa_kernel(backends[name]) if name else contextlib.nullcontext():
+                for a, b in zip(bounds[:-1], bounds[1:]):
+                    F.scaled_dot_product_attention(q[a:b].transpose(0, 1)[None], kx[a:b].transpose(0, 1)[None],
+                                                   vx[a:b].transpose(0, 1)[None], attn_mask=mask, is_causal=causal,
+                                                   scale=scale)
         return run
     raise SystemExit(f"unknown attention library {lib}")
 
@@ -305,7 +315,8 @@ def main(argv: list[str] | None = None) -> dict:
     p.add_argument("--iters", type=int, default=3)
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--lib", default="", help="time a library kernel on the same inputs instead: attention fa2, "
-                                             "flashinfer or torch; gemm cublas; delta_rule fla")
+                                             "flashinfer[:backend] or torch[:cudnn|flash|efficient]; gemm cublas; "
+                                             "delta_rule fla")
     args = p.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("microbench needs a CUDA device")

@@ -147,3 +147,32 @@ def test_attention_one_131072_token_sequence(window):
         want = _reference_rows(q, kf, vf, chunk, 0, window, scale)
         worst = max(worst, (got[chunk].float() - want).abs().max().item())
     assert worst <= 2e-2, worst
+
+
+def test_attention_long_sequence_runs_head_by_head_among_short_ones():
+    """A pack whose middle sequence's keys and values outgrow L2 (33,000 tokens x 4 key/value heads of 128: 68 MB),
+    so the kernel runs that sequence key/value head by key/value head while the short ones keep the query-heads-
+    innermost order: 16 query heads (groups of 4), causal; every row of the short sequences and 256 sampled rows of
+    the long one, all heads, against float32."""
+    g = torch.Generator(device=DEV).manual_seed(43)
+    lengths = [300, 33000, 700]
+    t, hq, hkv, hd = sum(lengths), 16, 4, 128
+    scale = hd ** -0.5
+    q = torch.randn(t, hq, hd, generator=g, device=DEV).bfloat16()
+    k = torch.randn(t, hkv, hd, generator=g, device=DEV).bfloat16()
+    v = torch.randn(t, hkv, hd, generator=g, device=DEV).bfloat16()
+    cu = torch.tensor(np.concatenate([[0], np.cumsum(lengths)]), dtype=torch.int32, device=DEV)
+    got = ops.attention_varlen(q, k, v, cu, cu, max(lengths), scale, (-1, 0)).view(t, hq, hd)
+    torch.cuda.synchronize()
+    ops.check_status(DEV)
+    pick = torch.Generator().manual_seed(44)
+    kf, vf = k.float(), v.float()
+    worst = 0.0
+    for start, n in zip(cu[:-1].tolist(), lengths, strict=True):
+        rows = torch.arange(start, start + n)
+        if n > 1000:
+            rows = torch.cat([rows[:4], rows[127:130], rows[-4:], rows[torch.randint(0, n, (245,), generator=pick)]])
+        for chunk in rows.to(DEV).split(64):
+            want = _reference_rows(q, kf, vf, chunk, start, -1, scale)
+            worst = max(worst, (got[chunk].float() - want).abs().max().item())
+    assert worst <= 2e-2, worst
