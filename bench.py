@@ -494,12 +494,17 @@ def request_latency(model, head, config: str, dev, n: int) -> dict:
 
     spec = model.spec
     _, (low, high), log = WORKLOADS[config]
+    every = fine_buckets(65536)
+    if low > every[-1]:  # one sequence per pack (config 5(a)): the request is the step
+        return {"requests": 0, "note": f"single requests of {low} tokens are this configuration's step (ms_per_step); "
+                                       f"the graph buckets end at {every[-1]} tokens"}
     rng = np.random.default_rng(7)
     lengths = [int(round(math.exp(rng.uniform(math.log(low), math.log(high))))) if log else
                int(rng.integers(low, high + 1)) for _ in range(n)]
     requests = request_arrays(spec, lengths, [1] * n, seed=7)
-    every = fine_buckets(65536)
-    needed = sorted({min(b for b in every if b >= len(r["input_ids"])) for r in requests})
+    # requests longer than the largest bucket run the plain path inside the graph wrapper, as in the reference
+    needed = sorted({min(b for b in every if b >= len(r["input_ids"])) for r in requests
+                     if len(r["input_ids"]) <= every[-1]})
     graphs = Graphs(model, buckets=tuple(needed), max_sequences=1)
     out = {"requests": n, "lengths": f"one sequence each, {'log-uniform' if log else 'uniform'} [{low},{high}], "
                                       f"one question", "graph_buckets": len(needed)}
