@@ -307,3 +307,20 @@ def test_mrope_pair_axes_and_oracle_tables_follow_transformers():
         want_cos, want_sin = oracle.packed.mrope_tables(pos, head_dim, 1e7, partial, sections, "fp32")
         # float32 angles up to position 500: the two inv_freq computations may differ in the last bit
         assert np.abs(cos[0].numpy() - want_cos).max() < 1e-4 and np.abs(sin[0].numpy() - want_sin).max() < 1e-4
+
+
+def test_bench_latency_of_one_sequence_configurations_is_the_step():
+    """Configuration 5(a)'s requests (one 131,072-token sequence) are longer than the largest graph bucket: the bench
+    reports the step as their latency instead of building graphs for them; the other configurations' request lengths
+    all fit a bucket."""
+    import types
+
+    import bench
+    from karpo_decision_b200.graphs import fine_buckets
+
+    model = types.SimpleNamespace(spec=CONFIGS["gemma-31b"])
+    out = bench.request_latency(model, None, "gemma-31b@131k", torch.device("cpu"), 4)
+    assert out["requests"] == 0 and "step" in out["note"]
+    for config, (_, (low, high), _) in bench.WORKLOADS.items():
+        if "@" not in config:
+            assert high <= fine_buckets(65536)[-1], config
